@@ -1,0 +1,273 @@
+"""Fused tiered decode attention (host side of ``fade_decode_attn``).
+
+One call computes, for every (batch row, query head), softmax attention of the
+decode query over the union of the cache tiers -- FP16/BF16 sink and recent
+tokens plus an INT4 / INT4K-INT2V / rotated 2-or-4-bit middle -- reading the
+compressed tiers straight from HBM.  It replaces the reference's per-step
+``_materialize`` (fade/cache.py:693-808) + SDPA (transformers
+sdpa_attention.py:40-62) and its standalone ``fused_int4_sdpa``
+(fade/kernels/fused_int4_attn.py:277-342).
+
+Tier tensors use the cache's own layouts ([B, Hkv, S, row] with contiguous
+rows); views into larger capacity buffers are fine.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from fade_b200 import _lib
+
+
+@dataclass
+class FPTier:
+    """Unquantised tier (sink or recent window): k, v [B, Hkv, L, D] in the model dtype."""
+
+    k: Tensor
+    v: Tensor
+    lens: Tensor | None = None      # optional device int32 [B] (ragged lengths)
+
+
+@dataclass
+class Int4Tier:
+    """INT4 middle: K per-channel (k_scale [B,Hkv,1,D]), V per-token (v_scale [B,Hkv,S,1])."""
+
+    k_packed: Tensor
+    k_scale: Tensor
+    v_packed: Tensor
+    v_scale: Tensor
+    lens: Tensor | None = None
+    max_len: int | None = None
+
+
+@dataclass
+class Int4K2VTier:
+    """INT4 K (per-channel) + grouped 2-bit V (v_packed [B,Hkv,S_pad,D/4], v_scale [B,Hkv,S_pad/G,D])."""
+
+    k_packed: Tensor
+    k_scale: Tensor
+    v_packed: Tensor
+    v_scale: Tensor
+    group: int
+    length: int | None = None       # valid tokens (<= S_pad)
+    lens: Tensor | None = None
+    max_len: int | None = None
+
+
+@dataclass
+class RotTier:
+    """Rotated middle (fade/rotated_quant.py): codes at `bits`, K per-channel, V per-token."""
+
+    k_packed: Tensor
+    k_scale: Tensor
+    v_packed: Tensor
+    v_scale: Tensor
+    bits: int
+    rotation: Tensor                # [D, D] float32 on the device
+    lens: Tensor | None = None
+    max_len: int | None = None
+
+
+def _row_strides(t: Tensor, row: int, what: str) -> tuple[int, int]:
+    if t.dim() != 4 or t.stride(3) != 1 or t.stride(2) != row:
+        raise ValueError(f"{what}: rows of {row} elements must be contiguous, got strides {t.stride()}")
+    sb, sh = t.stride(0), t.stride(1)
+    if sb % row or sh % row:
+        raise ValueError(f"{what}: batch/head strides must be whole rows, got {t.stride()}")
+    return sb // row, sh // row
+
+
+def _rows_available(t: Tensor, row_elems: int) -> int:
+    """Rows addressable from t.data_ptr() to the end of its storage."""
+    nbytes = t.untyped_storage().nbytes() - t.storage_offset() * t.element_size()
+    return nbytes // (row_elems * t.element_size())
+
+
+def _fill_fp(seg: _lib.KVSegment, tier: FPTier, D: int) -> list:
+    seg.kind = _lib.SEG_FP
+    sb, sh = _row_strides(tier.k, D, "fp tier k")
+    if _row_strides(tier.v, D, "fp tier v") != (sb, sh):
+        raise ValueError("fp tier k and v must share a layout")
+    seg.k, seg.v = tier.k.data_ptr(), tier.v.data_ptr()
+    seg.row_sb, seg.row_sh = sb, sh
+    L = tier.k.shape[2]
+    seg.len = L
+    seg.max_len = L
+    if tier.lens is not None:
+        seg.lens = tier.lens.data_ptr()
+    return [tier.k, tier.v, tier.lens]
+
+
+def _fill_mid(seg: _lib.KVSegment, tier, D: int, dtype: torch.dtype) -> list:
+    if isinstance(tier, Int4Tier):
+        seg.kind, kb, vb = _lib.SEG_INT4, 4, 4
+    elif isinstance(tier, Int4K2VTier):
+        seg.kind, kb, vb = _lib.SEG_INT4K_INT2V, 4, 2
+        seg.group = int(tier.group)
+    elif isinstance(tier, RotTier):
+        seg.kind, kb, vb = _lib.SEG_ROT, tier.bits, tier.bits
+        seg.bits = int(tier.bits)
+    else:
+        raise TypeError(f"unknown tier {type(tier)}")
+    rbk, rbv = D * kb // 8, D * vb // 8
+    sb, sh = _row_strides(tier.k_packed, rbk, "middle k codes")
+    if _row_strides(tier.v_packed, rbv, "middle v codes") != (sb, sh):
+        raise ValueError("middle K and V codes must share a row layout")
+    seg.k, seg.v = tier.k_packed.data_ptr(), tier.v_packed.data_ptr()
+    seg.row_sb, seg.row_sh = sb, sh
+    ks = tier.k_scale
+    if ks.dtype != dtype or ks.stride(-1) != 1:
+        raise ValueError("k_scale must be contiguous in D and in the model dtype")
+    seg.k_scale = ks.data_ptr()
+    seg.ks_sb, seg.ks_sh = ks.stride(0), ks.stride(1)
+    vs = tier.v_scale
+    if vs.dtype != dtype:
+        raise ValueError("v_scale must be in the model dtype")
+    if isinstance(tier, Int4K2VTier):
+        G = int(tier.group)
+        if vs.stride(3) != 1 or vs.stride(2) != D or sb % G or sh % G or vs.stride(0) != sb // G * D or vs.stride(1) != sh // G * D:
+            raise ValueError("grouped v_scale must be laid out [rows/G][D] alongside the codes")
+    else:
+        if vs.stride(2) != 1 or vs.stride(0) != sb or vs.stride(1) != sh:
+            raise ValueError("per-token v_scale must be indexed like the code rows")
+    seg.v_scale = vs.data_ptr()
+    S = tier.k_packed.shape[2]
+    length = getattr(tier, "length", None)
+    seg.len = int(length) if length is not None else S
+    seg.max_len = int(tier.max_len) if getattr(tier, "max_len", None) is not None else seg.len
+    if tier.lens is not None:
+        seg.lens = tier.lens.data_ptr()
+    seg.n_rows = min(_rows_available(tier.k_packed, rbk), _rows_available(tier.v_packed, rbv))
+    keep = [tier.k_packed, tier.v_packed, ks, vs, tier.lens]
+    if isinstance(tier, RotTier):
+        keep.append(tier.rotation)
+    return keep
+
+
+class DecodePlan:
+    """A filled ``fade_decode_desc`` plus its workspace, reusable across calls
+    whose tensors keep the same addresses (e.g. inside a CUDA graph)."""
+
+    def __init__(self, q: Tensor, tiers: list, out: Tensor | None = None, sm_scale: float | None = None,
+                 n_ctas: int = 0, cu_units: Tensor | None = None, workspace: Tensor | None = None):
+        if q.dim() != 4:
+            raise ValueError(f"query must be [B, Hq, n_q, D]; got shape {tuple(q.shape)}")
+        dev = _lib.require_cuda(q)
+        B, Hq, n_q, D = q.shape
+        if q.stride(-1) != 1:
+            raise ValueError("query must be contiguous in head_dim")
+        dtype = q.dtype
+        if dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError(f"unsupported dtype {dtype}")
+        d = _lib.DecodeDesc()
+        d.dtype = _lib.dtype_code(dtype)
+        d.B, d.Hq, d.D, d.n_q = B, Hq, D, n_q
+        d.sm_scale = float(sm_scale) if sm_scale is not None else 1.0 / math.sqrt(D)
+        d.q = q.data_ptr()
+        d.q_sb, d.q_sh, d.q_ss = q.stride(0), q.stride(1), q.stride(2)
+        if out is None:
+            out = torch.empty_like(q, memory_format=torch.contiguous_format)
+        if out.shape != q.shape or out.dtype != dtype or out.stride(-1) != 1:
+            raise ValueError("out must match the query's shape and dtype")
+        d.out = out.data_ptr()
+        d.o_sb, d.o_sh, d.o_ss = out.stride(0), out.stride(1), out.stride(2)
+        keep = [q, out]
+        Hkv = None
+        n = 0
+        for t in tiers:
+            if t is None:
+                continue
+            if n >= _lib.MAX_SEGMENTS:
+                raise ValueError("too many tiers")
+            if isinstance(t, FPTier):
+                h = t.k.shape[1]
+                keep += _fill_fp(d.seg[n], t, D)
+            else:
+                h = t.k_packed.shape[1]
+                keep += _fill_mid(d.seg[n], t, D, dtype)
+                if isinstance(t, RotTier):
+                    R = t.rotation
+                    if R.dtype != torch.float32 or not R.is_contiguous() or tuple(R.shape) != (D, D):
+                        raise ValueError("rotation must be a contiguous float32 [D, D] tensor")
+                    d.rotation = R.data_ptr()
+            if Hkv is None:
+                Hkv = h
+            elif h != Hkv:
+                raise ValueError("all tiers must have the same number of kv heads")
+            n += 1
+        if Hkv is None:
+            raise ValueError("no tiers given")
+        if Hq % Hkv:
+            raise ValueError(f"Hq={Hq} not divisible by Hkv={Hkv}")
+        d.Hkv = Hkv
+        d.n_segments = n
+        d.n_ctas = int(n_ctas)
+        if cu_units is not None:
+            d.cu_units = cu_units.data_ptr()
+            keep.append(cu_units)
+        self.desc = d
+        self.out = out
+        self._keep = keep
+        lib = _lib.load()
+        _lib.bind(dev)
+        need = lib.fade_decode_attn_workspace_size(ctypes.byref(d))
+        if need == 0:
+            raise ValueError(
+                f"unsupported decode configuration (D={D}, Hq/Hkv*n_q={Hq // Hkv * n_q}, dtype={dtype})"
+            )
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+        self.workspace = workspace
+        self.ws_bytes = workspace.numel()
+        self.device = dev
+
+    def run(self) -> Tensor:
+        lib = _lib.load()
+        st = _lib.bind(self.device)
+        _lib.check(lib.fade_decode_attn(ctypes.byref(self.desc), self.workspace.data_ptr(), self.ws_bytes, st),
+                   "fade_decode_attn")
+        return self.out
+
+    def check_device_errors(self) -> None:
+        st = _lib.bind(self.device)
+        _lib.check(_lib.load().fade_workspace_check(self.workspace.data_ptr(), self.ws_bytes, st),
+                   "fade_decode_attn")
+
+
+_WS: dict = {}
+
+
+def _workspace(dev: torch.device) -> Tensor | None:
+    key = (dev, torch.cuda.current_stream(dev).cuda_stream)
+    return _WS.get(key)
+
+
+def tiered_decode_attention(q: Tensor, tiers: list, sm_scale: float | None = None, out: Tensor | None = None,
+                            n_ctas: int = 0, cu_units: Tensor | None = None) -> Tensor:
+    """out[B,Hq,n_q,D] = softmax(q K^T * sm_scale) V over the union of `tiers`.
+
+    GQA: query head ``hq`` reads kv head ``hq // (Hq // Hkv)`` (transformers'
+    ``repeat_kv`` convention).  Non-causal over the cached tokens, as a decode
+    step is.  Workspace is cached per (device, stream); calls that share a
+    stream run in order, so sharing it is safe.
+    """
+    dev = _lib.require_cuda(q)
+    plan = DecodePlan(q, tiers, out=out, sm_scale=sm_scale, n_ctas=n_ctas, cu_units=cu_units,
+                      workspace=_workspace(dev))
+    _WS[(dev, torch.cuda.current_stream(dev).cuda_stream)] = plan.workspace
+    return plan.run()
+
+
+__all__ = [
+    "DecodePlan",
+    "FPTier",
+    "Int4K2VTier",
+    "Int4Tier",
+    "RotTier",
+    "tiered_decode_attention",
+]

@@ -1,0 +1,1389 @@
+// K2: fused tiered decode attention for sm_100a.
+//
+// Replaces, for one decode step of one layer, the reference's
+//   TieredKVCache._materialize (fade/cache.py:693-808: cat(sink, dequant(middle),
+//   recent)) followed by HF SDPA (transformers sdpa_attention.py:40-62), and the
+//   standalone fused_int4_sdpa (fade/kernels/fused_int4_attn.py:277-342).
+// Attention is a sum over keys, so the tiers are processed independently and
+// merged: the token order of the reference's cat() does not matter.
+//
+// Launch sequence (one stream, chained with programmatic dependent launch):
+//   k0  rotate_queries      (only with a rotated tier): q_rot = q @ R^T, fp32.
+//   k1  middle_kernel       persistent stream-K over the quantised middle tier.
+//   k2  tier0_merge_kernel  one CTA per (b, kv-head): attention over the FP
+//                           sink/recent tiers, then (after griddepcontrol.wait)
+//                           merges k1's split-K partials and writes `out`.
+//
+// k1 data path per CTA (5 warps):
+//   warp 4 (producer): 2-D TMA (cp.async.bulk.tensor, no multicast) of 128
+//     token rows of packed K and V codes into a 4-stage ring, swizzled so the
+//     ldmatrix reads below are bank-conflict free; it also stages the V scales
+//     (normalised per 32-token slice) with plain loads.  mbarrier full/empty.
+//   warps 0-3 (consumers): each owns 32 tokens of a stage.
+//     S^T[16 tok x 8 rows] = K_codes[16 x D] . (q*k_scale/qn)^T   (mma.sync
+//       m16n8k16 f16 -> f32; the GQA query rows of one kv head are the N dim)
+//     codes are turned into exact fp16 integers in registers with the
+//     magic-exponent trick (LUT-free int4 -> fp16 conversion, as used in
+//     FasterTransformer's mixed-precision GEMMs): (x & mask) ^ (0x6400|sign)
+//     makes 1024 + u (or 1024 + 16u), one HADD2 removes the bias.
+//     online softmax in log2 space; P (fp16, V scale folded in) is transposed
+//     with movmatrix and O^T[D x 8] += V_codes^T . P^T (mma.sync again).
+//   The channel order inside a thread is permuted to match the packed layout;
+//   q fragments are built with the same permutation, so nothing is shuffled.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace fade {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kMidThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
+constexpr int kStages = 4;
+constexpr int kTier0Threads = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polling
+
+// ---------------------------------------------------------------------------
+// PTX wrappers (mbarrier, TMA, ldmatrix, movmatrix, mma)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after kWaitLimit polls (each poll may suspend the
+// thread for a hardware-defined interval) and never spins forever.  A CTA-wide
+// abort flag makes every later wait of the CTA fail at once, so a CTA whose
+// pipeline stalled walks the rest of its (uniform) control flow quickly and
+// exits; the device error word tells the host.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err) {
+    if (*abort_flag) return false;
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023u) == 1023u && *abort_flag) return false;
+    }
+    *abort_flag = 1;
+    atomicExch(err, 1);
+    return false;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t (&r)[2]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t (&r)[2]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(addr));
+}
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Code -> fp16 conversion.  u = code XOR sign bit is the offset-binary value;
+// (x & mask) ^ (0x6400 | sign-bits & mask) = fp16(1024 + u * 2^shift).
+// Subtracting (1024 + bias * 2^shift) leaves code * 2^shift exactly.
+// ---------------------------------------------------------------------------
+struct Int4Conv {
+    // returns 4 half2: [0]=(n1,n5) x1, [1]=(n0,n4) x16, [2]=(n3,n7) x1, [3]=(n2,n6) x16
+    // where n_i are the nibbles in element order of the 4 bytes of x
+    // (byte j = (hi: element 2j, lo: element 2j+1)).
+    __device__ __forceinline__ static void conv(uint32_t x, uint32_t (&h)[4]) {
+        const uint32_t x8 = x >> 8;
+        h[0] = hadd2_u32(lop3_and_xor(x, 0x000F000Fu, 0x64086408u), 0xE408E408u);   // -1032
+        h[1] = hadd2_u32(lop3_and_xor(x, 0x00F000F0u, 0x64806480u), 0xE480E480u);   // -1152
+        h[2] = hadd2_u32(lop3_and_xor(x8, 0x000F000Fu, 0x64086408u), 0xE408E408u);
+        h[3] = hadd2_u32(lop3_and_xor(x8, 0x00F000F0u, 0x64806480u), 0xE480E480u);
+    }
+};
+struct Int2Conv {
+    // 8 half2 from 4 bytes; field f (0..3) of a byte sits at bit 6-2f.
+    // [0]=f3 x1, [1]=f2 x4, [2]=f1 x16, [3]=f0 x64 for bytes (0,2);
+    // [4..7] the same for bytes (1,3).
+    __device__ __forceinline__ static void conv(uint32_t x, uint32_t (&h)[8]) {
+        const uint32_t x8 = x >> 8;
+        h[0] = hadd2_u32(lop3_and_xor(x, 0x00030003u, 0x64026402u), 0xE402E402u);   // -1026
+        h[1] = hadd2_u32(lop3_and_xor(x, 0x000C000Cu, 0x64086408u), 0xE408E408u);   // -1032
+        h[2] = hadd2_u32(lop3_and_xor(x, 0x00300030u, 0x64206420u), 0xE420E420u);   // -1056
+        h[3] = hadd2_u32(lop3_and_xor(x, 0x00C000C0u, 0x64806480u), 0xE480E480u);   // -1152
+        h[4] = hadd2_u32(lop3_and_xor(x8, 0x00030003u, 0x64026402u), 0xE402E402u);
+        h[5] = hadd2_u32(lop3_and_xor(x8, 0x000C000Cu, 0x64086408u), 0xE408E408u);
+        h[6] = hadd2_u32(lop3_and_xor(x8, 0x00300030u, 0x64206420u), 0xE420E420u);
+        h[7] = hadd2_u32(lop3_and_xor(x8, 0x00C000C0u, 0x64806480u), 0xE480E480u);
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Channel maps.  For a K operand (QK^T, B = q fragment) of thread lane
+// t = lane % 4, k-step ks, slot s in {0,1,2,3} = (b0, b1, b2, b3), kdim()
+// gives the channel and kfac() the power of two the converted code carries.
+// For the V operand (O^T rows), m-tile mi and row half hr (0: row gid,
+// 1: row gid+8) of thread gid = lane / 4, vdim()/vfac() likewise.
+// ---------------------------------------------------------------------------
+template <int BITS> struct ChanMap;
+template <> struct ChanMap<4> {
+    __device__ __forceinline__ static int kdim(int ks, int s, int t) {
+        const int cb = ks >> 1, u = ks & 1;
+        // u=0: (n1,n5 | n0,n4), u=1: (n3,n7 | n2,n6)
+        const int off[2][4] = {{1, 5, 0, 4}, {3, 7, 2, 6}};
+        return 32 * cb + 8 * t + off[u][s];
+    }
+    __device__ __forceinline__ static float kfac(int ks, int s) { return s >= 2 ? 16.f : 1.f; }
+    __device__ __forceinline__ static int vdim(int mi, int hr, int gid) {
+        const int cb = mi >> 1, j = mi & 1;
+        return 32 * cb + 4 * gid + 2 * j + hr;
+    }
+    __device__ __forceinline__ static float vfac(int mi, int hr) { return hr == 0 ? 16.f : 1.f; }
+};
+template <> struct ChanMap<2> {
+    __device__ __forceinline__ static int kdim(int ks, int s, int t) {
+        const int cb = ks >> 2, u = ks & 3;
+        // pairs M_{2u}, M_{2u+1}; M_i for bytes (0,2) (i<4) or (1,3) (i>=4)
+        const int off[4][4] = {{3, 11, 2, 10}, {1, 9, 0, 8}, {7, 15, 6, 14}, {5, 13, 4, 12}};
+        return 64 * cb + 16 * t + off[u][s];
+    }
+    __device__ __forceinline__ static float kfac(int ks, int s) {
+        const int u = ks & 3;
+        const float f[4][2] = {{1.f, 4.f}, {16.f, 64.f}, {1.f, 4.f}, {16.f, 64.f}};
+        return f[u][s >> 1];
+    }
+    __device__ __forceinline__ static int vdim(int mi, int hr, int gid) {
+        const int cb = mi >> 2, j = mi & 3;
+        return 64 * cb + 8 * gid + 2 * j + hr;
+    }
+    __device__ __forceinline__ static float vfac(int mi, int hr) {
+        const int j = mi & 3;
+        const float f[4][2] = {{64.f, 16.f}, {4.f, 1.f}, {64.f, 16.f}, {4.f, 1.f}};
+        return f[j][hr];
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Kernel parameters
+// ---------------------------------------------------------------------------
+struct MidParams {
+    int dtype;
+    int B, Hq, Hkv, D, n_q, g, rows;
+    float qk_scale;                 // sm_scale * log2(e)
+    const void* q;                  // dtype [B,Hq,n_q,D] (strided) or fp32 q_rot
+    int64_t q_sb, q_sh, q_ss;
+    int q_is_f32;                   // 1: q points at the fp32 rotated queries
+    const void* k_scale;            // per-channel, dtype
+    int64_t ks_sb, ks_sh;
+    const void* v_scale;            // per-token (row-indexed) or grouped
+    int group;                      // grouped V: tokens per group, else 0
+    int64_t row_sb, row_sh;
+    const int64_t* row_base;
+    const int32_t* lens;
+    int64_t len;
+    const int32_t* cu_units;        // ragged: [Z+1]; null = uniform
+    int units_per_z;                // uniform case
+    int n_ctas;
+    float* ws_ml;                   // [U][rows][2]
+    float* ws_o;                    // [U][rows][D]
+    int* ws_err;
+};
+
+__device__ __forceinline__ int64_t seg_len(const MidParams& p, int b) {
+    return p.lens ? (int64_t)p.lens[b] : p.len;
+}
+__device__ __forceinline__ int64_t seg_row0(const MidParams& p, int z) {
+    const int b = z / p.Hkv, h = z % p.Hkv;
+    return p.row_base ? p.row_base[z] : (int64_t)b * p.row_sb + (int64_t)h * p.row_sh;
+}
+__device__ __forceinline__ int total_units(const MidParams& p, int Z) {
+    return p.cu_units ? p.cu_units[Z] : Z * p.units_per_z;
+}
+__device__ __forceinline__ int units_begin(const MidParams& p, int z) {
+    return p.cu_units ? p.cu_units[z] : z * p.units_per_z;
+}
+// z such that units_begin(z) <= u < units_begin(z+1)
+__device__ __forceinline__ int z_of_unit(const MidParams& p, int Z, int u) {
+    if (!p.cu_units) return u / p.units_per_z;
+    int lo = 0, hi = Z - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.cu_units[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+__device__ __forceinline__ int cta_of_unit(int u, int C, int U) {
+    return (int)(((int64_t)(u + 1) * C - 1) / U);
+}
+
+template <int D, int KB, int VB, bool VGROUP, int NT>
+struct MidLayout {
+    static constexpr int RBK = D * KB / 8;
+    static constexpr int RBV = D * VB / 8;
+    static constexpr int NCHK = RBK / 16;
+    static constexpr int NCHV = RBV / 16;
+    static constexpr int K_BYTES = kStageTokens * RBK;
+    static constexpr int V_BYTES = kStageTokens * RBV;
+    // scale region: per-token (normalised) scales + per-slice max, or grouped
+    // scales for up to kStageTokens/16 groups.
+    static constexpr int SC_BYTES = VGROUP ? (kStageTokens / 16) * D * 4 : kStageTokens * 4 + 64;
+    // [K0 V0 K1 V1 ...] (each region a multiple of 1024 B, so every TMA
+    // destination keeps the 1024-B alignment the swizzle modes need), then
+    // the per-stage scale regions.
+    static constexpr int K_OFF = 0;
+    static constexpr int V_OFF = K_BYTES;
+    static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+    static_assert(K_BYTES % 1024 == 0 && V_BYTES % 1024 == 0, "stage regions must stay 1 KB aligned");
+    static constexpr int SC_BASE = kStages * STAGE_BYTES;
+    static constexpr int RING_BYTES = SC_BASE + kStages * SC_BYTES;
+    static constexpr int OBUF_BYTES = NT * 8 * D * 4;
+    static constexpr int ML_BYTES = kConsumerWarps * 16 * 2 * 4;
+    static constexpr int BAR_OFF = RING_BYTES + OBUF_BYTES + ML_BYTES;
+    static constexpr int FLAG_OFF = BAR_OFF + 2 * kStages * 8;
+    static constexpr int SMEM_BYTES = FLAG_OFF + 16 + 1024;  // +1024 for alignment
+};
+
+__device__ __forceinline__ uint32_t swz(uint32_t off, uint32_t smask) {
+    return off ^ (((off >> 7) & smask) << 4);
+}
+
+template <int DT>
+__device__ __forceinline__ float load_f(const void* p, int64_t i) {
+    return Elem<DT>::to_f(reinterpret_cast<const typename Elem<DT>::T*>(p)[i]);
+}
+
+// ---------------------------------------------------------------------------
+// k1: middle tier, persistent stream-K
+// ---------------------------------------------------------------------------
+template <int DT, int D, int KB, int VB, bool VGROUP, int NT>
+__global__ void __launch_bounds__(kMidThreads)
+middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+              MidParams p) {
+    using L = MidLayout<D, KB, VB, VGROUP, NT>;
+    using KMap = ChanMap<KB>;
+    using VMap = ChanMap<VB>;
+    constexpr int KSTEPS = D / 16;   // k-steps of the QK product
+    constexpr int MT = D / 16;       // m-tiles of the PV product (rows = channels)
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* obuf = reinterpret_cast<float*>(smem + L::RING_BYTES);
+    float* mlbuf = reinterpret_cast<float*>(smem + L::RING_BYTES + L::OBUF_BYTES);
+    const uint32_t bar_base = smem_u32(smem + L::BAR_OFF);
+    auto full_bar = [&](int s) { return bar_base + 8u * s; };
+    auto empty_bar = [&](int s) { return bar_base + 8u * (kStages + s); };
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int Z = p.B * p.Hkv;
+    const int U = total_units(p, Z);
+    const int C = p.n_ctas;
+    const int c = blockIdx.x;
+    const int ub = (int)((int64_t)c * U / C), ue = (int)((int64_t)(c + 1) * U / C);
+
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::FLAG_OFF);
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full_bar(s), 32);
+            mbar_init(empty_bar(s), kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncthreads();
+    // Inputs may be produced by the previous kernel in the stream (age-out,
+    // query rotation): wait for it before touching global memory, then let the
+    // next kernel (tier0/merge) start its independent prologue.
+    griddep_wait();
+    griddep_launch_dependents();
+    if (ub >= ue) return;
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------ producer ------------------------------
+        const uint64_t policy = evict_first_policy();
+        if (lane == 0) {
+            prefetch_tmap(&tmap_k);
+            prefetch_tmap(&tmap_v);
+        }
+        int z = z_of_unit(p, Z, ub);
+        int zb = units_begin(p, z), ze = units_begin(p, z + 1);
+        for (int u = ub, i = 0; u < ue; ++u, ++i) {
+            while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
+            const int s = i % kStages;
+            const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+            if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.ws_err)) continue;
+            const int64_t tok0 = (int64_t)(u - zb) * kStageTokens;
+            const int64_t row0 = seg_row0(p, z) + tok0;
+            const int64_t len = seg_len(p, z / p.Hkv);
+            uint8_t* st = smem + s * L::STAGE_BYTES;
+            // Units past this row's length (uniform grid over a capacity bound)
+            // carry no tokens: complete the stage without a copy.
+            if (lane == 0 && tok0 < len) {
+                mbar_expect_tx(full_bar(s), (uint32_t)(L::K_BYTES + L::V_BYTES));
+                tma_load_2d(smem_u32(st + L::K_OFF), &tmap_k, 0, (int)row0, full_bar(s), policy);
+                tma_load_2d(smem_u32(st + L::V_OFF), &tmap_v, 0, (int)row0, full_bar(s), policy);
+            }
+            float* sc = reinterpret_cast<float*>(smem + L::SC_BASE + s * L::SC_BYTES);
+            if constexpr (!VGROUP) {
+                // per-token scales, normalised by the max of each warp's 32-token slice
+                float v[4];
+                float mx = 0.f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int tt = lane * 4 + j;
+                    v[j] = (tok0 + tt < len) ? fabsf(load_f<DT>(p.v_scale, row0 + tt)) : 0.f;
+                    mx = fmaxf(mx, v[j]);
+                }
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                const float inv = mx > 0.f ? 1.f / mx : 0.f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) sc[lane * 4 + j] = v[j] * inv;
+                if ((lane & 7) == 0) sc[kStageTokens + lane / 8] = mx;
+            } else {
+                // grouped scales: row r uses group r / G.  Stage rows start on a
+                // group boundary (G divides 128 and row bases are group aligned).
+                const int G = p.group;
+                const int ngr = kStageTokens / G;
+                const int64_t g0 = row0 / G;
+                for (int e = lane; e < ngr * D; e += 32) {
+                    const int gi = e / D, d = e % D;
+                    const bool ok = tok0 + (int64_t)gi * G < len;
+                    sc[e] = ok ? load_f<DT>(p.v_scale, (g0 + gi) * D + d) : 0.f;
+                }
+            }
+            mbar_arrive(full_bar(s));
+        }
+        // Drain: wait until the consumers released every stage still in flight,
+        // so no TMA write targets this CTA's shared memory after it exits.
+        const int n = ue - ub;
+        for (int i = (n > kStages ? n : kStages); i < n + kStages; ++i) {
+            const int s = i % kStages;
+            const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+            mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.ws_err);
+        }
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
+    const int gid = lane >> 2, t = lane & 3;
+    const int ctid = threadIdx.x;  // 0..127
+    uint32_t qf[NT][KSTEPS][2];
+    float qn[NT][2];
+    float m_run[NT][2], l_run[NT][2];
+    float o[NT][MT][4];
+    int cur_z = -1;
+    int64_t cur_len = 0;
+
+    auto setup_z = [&](int z) {
+        const int b = z / p.Hkv, h = z % p.Hkv;
+        const void* ksb = p.k_scale;
+        const int64_t ks_off = (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int r = nt * 8 + gid;
+            float prod[KSTEPS][4];
+            float amax = 0.f;
+            const bool rv = r < p.rows;
+            const int j = rv ? r / p.n_q : 0, sq = rv ? r % p.n_q : 0;
+            const int64_t qoff = (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss;
+#pragma unroll
+            for (int ks = 0; ks < KSTEPS; ++ks) {
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const int d = KMap::kdim(ks, s, t);
+                    float qv = 0.f;
+                    if (rv) {
+                        qv = p.q_is_f32 ? reinterpret_cast<const float*>(p.q)[qoff + d]
+                                        : load_f<DT>(p.q, qoff + d);
+                    }
+                    const float v = qv * load_f<DT>(ksb, ks_off + d) * p.qk_scale;
+                    prod[ks][s] = v;
+                    amax = fmaxf(amax, fabsf(v));
+                }
+            }
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            const float inv = amax > 0.f ? 1.f / amax : 0.f;
+#pragma unroll
+            for (int ks = 0; ks < KSTEPS; ++ks) {
+                qf[nt][ks][0] = pack_h2(prod[ks][0] * inv / KMap::kfac(ks, 0),
+                                        prod[ks][1] * inv / KMap::kfac(ks, 1));
+                qf[nt][ks][1] = pack_h2(prod[ks][2] * inv / KMap::kfac(ks, 2),
+                                        prod[ks][3] * inv / KMap::kfac(ks, 3));
+            }
+            // qn for the two score columns this thread owns (rows 2t, 2t+1 of
+            // the n-tile) is held by lanes gid = 2t, 2t+1.
+            qn[nt][0] = __shfl_sync(0xffffffffu, amax, (2 * t) * 4);
+            qn[nt][1] = __shfl_sync(0xffffffffu, amax, (2 * t + 1) * 4);
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            m_run[nt][0] = m_run[nt][1] = -INFINITY;
+            l_run[nt][0] = l_run[nt][1] = 0.f;
+#pragma unroll
+            for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[nt][mi][e] = 0.f;
+        }
+        cur_len = seg_len(p, b);
+    };
+
+    auto flush = [&](int z) {
+        // 1) complete the per-thread row sums over the 8 token lanes
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float l = l_run[nt][e];
+                l += __shfl_xor_sync(0xffffffffu, l, 4);
+                l += __shfl_xor_sync(0xffffffffu, l, 8);
+                l += __shfl_xor_sync(0xffffffffu, l, 16);
+                l_run[nt][e] = l;
+            }
+        if (gid == 0) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int r = nt * 8 + 2 * t + e;
+                    mlbuf[(warp * 16 + r) * 2 + 0] = m_run[nt][e];
+                    mlbuf[(warp * 16 + r) * 2 + 1] = l_run[nt][e];
+                }
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+        // 2) rescale this warp's O to the CTA max and accumulate into obuf
+        float f[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int r = nt * 8 + 2 * t + e;
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mlbuf[(w * 16 + r) * 2]);
+                f[nt][e] = (m_run[nt][e] == -INFINITY) ? 0.f : ex2(m_run[nt][e] - M);
+            }
+        for (int pass = 0; pass < kConsumerWarps; ++pass) {
+            if (warp == pass) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int hr = e >> 1;
+                            const int col = e & 1;
+                            const int r = nt * 8 + 2 * t + col;
+                            const int d = VMap::vdim(mi, hr, gid);
+                            const float v = o[nt][mi][e] * f[nt][col] / VMap::vfac(mi, hr);
+                            if (pass == 0) obuf[r * D + d] = v; else obuf[r * D + d] += v;
+                        }
+            }
+            named_bar_sync(1, kConsumerWarps * 32);
+        }
+        // 3) write the CTA partial for z to its slot
+        const int zb = units_begin(p, z);
+        const int slot = zb + (c - cta_of_unit(zb, C, U));
+        float* go = p.ws_o + (int64_t)slot * p.rows * D;
+        for (int i = ctid; i < p.rows * D; i += kConsumerWarps * 32) go[i] = obuf[i];
+        if (ctid < p.rows) {
+            const int r = ctid;
+            float M = -INFINITY, Ls = 0.f;
+            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mlbuf[(w * 16 + r) * 2]);
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                const float mw = mlbuf[(w * 16 + r) * 2];
+                if (mw != -INFINITY) Ls += ex2(mw - M) * mlbuf[(w * 16 + r) * 2 + 1];
+            }
+            p.ws_ml[((int64_t)slot * p.rows + r) * 2 + 0] = M;
+            p.ws_ml[((int64_t)slot * p.rows + r) * 2 + 1] = Ls;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+    };
+
+    int z = z_of_unit(p, Z, ub);
+    int zb = units_begin(p, z), ze = units_begin(p, z + 1);
+    const uint32_t smask_k = (uint32_t)(L::NCHK - 1);
+    const uint32_t smask_v = (uint32_t)(L::NCHV - 1);
+    for (int u = ub, i = 0; u < ue; ++u, ++i) {
+        while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
+        if (z != cur_z) {
+            if (cur_z >= 0) flush(cur_z);
+            setup_z(z);
+            cur_z = z;
+        }
+        const int s = i % kStages;
+        const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+        const bool ready = mbar_wait(full_bar(s), ph, abort_flag, p.ws_err);
+        const int64_t tok_w = (int64_t)(u - zb) * kStageTokens + warp * 32;  // first token of this warp
+        const uint8_t* st = smem + s * L::STAGE_BYTES;
+        const uint32_t kbase = smem_u32(st + L::K_OFF);
+        const uint32_t vbase = smem_u32(st + L::V_OFF);
+        const float* sc = reinterpret_cast<const float*>(smem + L::SC_BASE + s * L::SC_BYTES);
+
+        if (ready && tok_w < cur_len) {
+            // ---- S^T = K . q^T for the warp's 2 m-tiles ----
+            float sacc[2][NT][4];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = 0.f;
+                const int trow0 = warp * 32 + mt * 16;  // tile row within the stage
+                // matrices (tb, cb) -> regs kr[tb][cb]
+                uint32_t kr[2][L::NCHK];
+                constexpr int NMAT = 2 * L::NCHK;
+                if constexpr (NMAT >= 4) {
+#pragma unroll
+                    for (int x = 0; x < NMAT / 4; ++x) {
+                        const int mi = x * 4 + lane / 8;
+                        const int tb = mi / L::NCHK, cb = mi % L::NCHK;
+                        const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * L::RBK + cb * 16);
+                        uint32_t r4[4];
+                        ldsm_x4(kbase + swz(off, smask_k), r4);
+#pragma unroll
+                        for (int y = 0; y < 4; ++y) {
+                            const int mj = x * 4 + y;
+                            kr[mj / L::NCHK][mj % L::NCHK] = r4[y];
+                        }
+                    }
+                } else {
+                    const int mi = (lane / 8) & 1;
+                    const int tb = mi / L::NCHK, cb = mi % L::NCHK;
+                    const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * L::RBK + cb * 16);
+                    uint32_t r2[2];
+                    ldsm_x2(kbase + swz(off, smask_k), r2);
+                    kr[0][0] = r2[0];
+                    kr[1][0] = r2[1];
+                }
+#pragma unroll
+                for (int cb = 0; cb < L::NCHK; ++cb) {
+                    if constexpr (KB == 4) {
+                        uint32_t h0[4], h1[4];
+                        Int4Conv::conv(kr[0][cb], h0);
+                        Int4Conv::conv(kr[1][cb], h1);
+#pragma unroll
+                        for (int u2 = 0; u2 < 2; ++u2) {
+                            const int ks = cb * 2 + u2;
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt)
+                                mma16816(sacc[mt][nt], h0[2 * u2], h1[2 * u2], h0[2 * u2 + 1],
+                                         h1[2 * u2 + 1], qf[nt][ks][0], qf[nt][ks][1]);
+                        }
+                    } else {
+                        uint32_t h0[8], h1[8];
+                        Int2Conv::conv(kr[0][cb], h0);
+                        Int2Conv::conv(kr[1][cb], h1);
+#pragma unroll
+                        for (int u4 = 0; u4 < 4; ++u4) {
+                            const int ks = cb * 4 + u4;
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt)
+                                mma16816(sacc[mt][nt], h0[2 * u4], h1[2 * u4], h0[2 * u4 + 1],
+                                         h1[2 * u4 + 1], qf[nt][ks][0], qf[nt][ks][1]);
+                        }
+                    }
+                }
+            }
+            // ---- online softmax over the 32 tokens (log2 domain) ----
+            uint32_t pb[2][NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int tok = (int)tok_w + mt * 16 + gid + ((e >> 1) << 3);
+                        float v = sacc[mt][nt][e] * qn[nt][e & 1];
+                        if (tok >= cur_len) v = -INFINITY;
+                        sacc[mt][nt][e] = v;
+                        mx[e & 1] = fmaxf(mx[e & 1], v);
+                    }
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 4));
+                    mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 8));
+                    mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
+                    const float mnew = fmaxf(m_run[nt][e], mx[e]);
+                    const float corr = (m_run[nt][e] == -INFINITY) ? 0.f : ex2(m_run[nt][e] - mnew);
+                    m_run[nt][e] = mnew;
+                    l_run[nt][e] *= corr;
+#pragma unroll
+                    for (int mi = 0; mi < MT; ++mi) {
+                        o[nt][mi][e] *= corr;
+                        o[nt][mi][e + 2] *= corr;
+                    }
+                }
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    float pv[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float mref = m_run[nt][e & 1];
+                        const float pe = (sacc[mt][nt][e] == -INFINITY) ? 0.f : ex2(sacc[mt][nt][e] - mref);
+                        l_run[nt][e & 1] += pe;
+                        pv[e] = pe;
+                    }
+                    if constexpr (!VGROUP) {
+                        const int tr = warp * 32 + mt * 16 + gid;
+                        const float s0 = sc[tr], s1 = sc[tr + 8];
+                        pv[0] *= s0; pv[1] *= s0; pv[2] *= s1; pv[3] *= s1;
+                    }
+                    pb[mt][nt][0] = movmatrix_t(pack_h2(pv[0], pv[1]));
+                    pb[mt][nt][1] = movmatrix_t(pack_h2(pv[2], pv[3]));
+                }
+            }
+            // ---- O^T += V^T . P^T ----
+            float vmul = 1.f;
+            if constexpr (!VGROUP) vmul = sc[kStageTokens + warp];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const int trow0 = warp * 32 + mt * 16;
+                uint32_t vr[2][L::NCHV];
+                constexpr int NMAT = 2 * L::NCHV;
+                if constexpr (NMAT >= 4) {
+#pragma unroll
+                    for (int x = 0; x < NMAT / 4; ++x) {
+                        const int mi = x * 4 + lane / 8;
+                        const int tb = mi / L::NCHV, cb = mi % L::NCHV;
+                        const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * L::RBV + cb * 16);
+                        uint32_t r4[4];
+                        ldsm_x4_t(vbase + swz(off, smask_v), r4);
+#pragma unroll
+                        for (int y = 0; y < 4; ++y) {
+                            const int mj = x * 4 + y;
+                            vr[mj / L::NCHV][mj % L::NCHV] = r4[y];
+                        }
+                    }
+                } else {
+                    const int mi = (lane / 8) & 1;
+                    const int tb = mi / L::NCHV, cb = mi % L::NCHV;
+                    const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * L::RBV + cb * 16);
+                    uint32_t r2[2];
+                    ldsm_x2_t(vbase + swz(off, smask_v), r2);
+                    vr[0][0] = r2[0];
+                    vr[1][0] = r2[1];
+                }
+                float tacc[NT][MT][4];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) tacc[nt][mi][e] = 0.f;
+#pragma unroll
+                for (int cb = 0; cb < L::NCHV; ++cb) {
+                    if constexpr (VB == 4) {
+                        uint32_t h0[4], h1[4];
+                        Int4Conv::conv(vr[0][cb], h0);   // tokens 2t,2t+1
+                        Int4Conv::conv(vr[1][cb], h1);   // tokens 8+2t, 9+2t
+                        // m-tile j=0: rows (gid: n0 x16 -> h[1]), (gid+8: n1 -> h[0])
+                        // m-tile j=1: rows (gid: n2 x16 -> h[3]), (gid+8: n3 -> h[2])
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            const int mi = cb * 2 + j;
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt)
+                                mma16816(tacc[nt][mi], h0[2 * j + 1], h0[2 * j], h1[2 * j + 1], h1[2 * j],
+                                         pb[mt][nt][0], pb[mt][nt][1]);
+                        }
+                    } else {
+                        uint32_t h0[8], h1[8];
+                        Int2Conv::conv(vr[0][cb], h0);
+                        Int2Conv::conv(vr[1][cb], h1);
+                        // 8 channels: +0 (h[3],x64) +1 (h[2],x16) +2 (h[1],x4) +3 (h[0],x1)
+                        //             +4 (h[7],x64) +5 (h[6],x16) +6 (h[5],x4) +7 (h[4],x1)
+                        const int lo[4] = {3, 1, 7, 5};
+                        const int hi[4] = {2, 0, 6, 4};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int mi = cb * 4 + j;
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt)
+                                mma16816(tacc[nt][mi], h0[lo[j]], h0[hi[j]], h1[lo[j]], h1[hi[j]],
+                                         pb[mt][nt][0], pb[mt][nt][1]);
+                        }
+                    }
+                }
+                if constexpr (VGROUP) {
+                    // grouped scales: channel d of this m-tile's group
+                    const int gi = (trow0) / p.group;
+                    const float* gs = sc + gi * D;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                o[nt][mi][e] += tacc[nt][mi][e] * gs[VMap::vdim(mi, e >> 1, gid)];
+                } else {
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) o[nt][mi][e] += tacc[nt][mi][e] * vmul;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(s));
+    }
+    if (cur_z >= 0) flush(cur_z);
+}
+
+// ---------------------------------------------------------------------------
+// k0: q_rot = q @ R^T (fp32), one CTA per query row
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void rotate_queries_kernel(const void* q, int Hq, int n_q, int D, int64_t q_sb,
+                                      int64_t q_sh, int64_t q_ss, const float* __restrict__ R,
+                                      float* __restrict__ q_rot) {
+    griddep_wait();
+    griddep_launch_dependents();
+    extern __shared__ float qs[];
+    const int row = blockIdx.x;  // (b*Hq + hq)*n_q + s
+    const int s = row % n_q, bh = row / n_q;
+    const int hq = bh % Hq, b = bh / Hq;
+    const int64_t off = (int64_t)b * q_sb + (int64_t)hq * q_sh + (int64_t)s * q_ss;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) qs[d] = load_f<DT>(q, off + d);
+    __syncthreads();
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float acc = 0.f;
+        for (int e = 0; e < D; ++e) acc = __fadd_rn(acc, __fmul_rn(qs[e], R[(int64_t)d * D + e]));
+        q_rot[(int64_t)row * D + d] = acc;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k2: FP tiers (SIMT) + split-K merge + output, one CTA per (b, kv-head)
+// ---------------------------------------------------------------------------
+struct FpSeg {
+    const void* k;
+    const void* v;
+    int64_t row_sb, row_sh;
+    const int64_t* row_base;
+    const int32_t* lens;
+    int64_t len;
+};
+struct Tier0Params {
+    int B, Hq, Hkv, D, n_q, g, rows;
+    float qk_scale;
+    const void* q;
+    int64_t q_sb, q_sh, q_ss;
+    void* out;
+    int64_t o_sb, o_sh, o_ss;
+    int n_fp;
+    FpSeg fp[FADE_MAX_SEGMENTS];
+    int has_mid;
+    const float* rotation;          // non-null: middle partials are in rotated space
+    const int32_t* cu_units;
+    int units_per_z;
+    int n_ctas;
+    const float* ws_ml;
+    const float* ws_o;
+};
+
+template <int DT, int D, int NT>
+__global__ void __launch_bounds__(kTier0Threads)
+tier0_merge_kernel(Tier0Params p) {
+    constexpr int ROWS = NT * 8;
+    constexpr int DPL = D / 32;  // channels per lane in the PV accumulation
+    constexpr int DQ = D / 4;    // channels per lane in the QK dot product
+    // With a middle tier the preceding grid is k1, which only let this grid
+    // start after its own griddepcontrol.wait, so q and the FP tiers are final
+    // and the FP pass can overlap k1.  Without one, wait for the predecessor.
+    if (!p.has_mid) griddep_wait();
+    griddep_launch_dependents();
+    __shared__ float qsm[ROWS * D];
+    __shared__ float osm[ROWS * D];
+    __shared__ float msm[kTier0Threads / 32][ROWS], lsm[kTier0Threads / 32][ROWS];
+    __shared__ float fin_m[ROWS], fin_l[ROWS];
+
+    const int z = blockIdx.x;
+    const int b = z / p.Hkv, h = z % p.Hkv;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int nw = kTier0Threads / 32;
+    const int rows = p.rows;
+
+    for (int i = threadIdx.x; i < ROWS * D; i += kTier0Threads) {
+        const int r = i / D, d = i % D;
+        float v = 0.f;
+        if (r < rows) {
+            const int j = r / p.n_q, sq = r % p.n_q;
+            v = load_f<DT>(p.q, (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss + d) *
+                p.qk_scale;
+        }
+        qsm[i] = v;
+        osm[i] = 0.f;
+    }
+    __syncthreads();
+
+    float m[ROWS], l[ROWS], o[ROWS][DPL];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+        m[r] = -INFINITY;
+        l[r] = 0.f;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) o[r][e] = 0.f;
+    }
+    const int tk = lane >> 2, qd = lane & 3;  // QK layout: token tk (0..7), quarter qd
+    for (int si = 0; si < p.n_fp; ++si) {
+        const FpSeg& sg = p.fp[si];
+        const int64_t len = sg.lens ? (int64_t)sg.lens[b] : sg.len;
+        const int64_t row0 = sg.row_base ? sg.row_base[z] : (int64_t)b * sg.row_sb + (int64_t)h * sg.row_sh;
+        const auto* K = reinterpret_cast<const typename Elem<DT>::T*>(sg.k);
+        const auto* V = reinterpret_cast<const typename Elem<DT>::T*>(sg.v);
+        for (int64_t t0 = (int64_t)warp * 8; t0 < len; t0 += (int64_t)nw * 8) {
+            const int64_t tok = t0 + tk;
+            const bool tv = tok < len;
+            float kd[DQ];
+            const auto* kr = K + (row0 + (tv ? tok : 0)) * D + qd * DQ;
+#pragma unroll
+            for (int e = 0; e < DQ; ++e) kd[e] = tv ? Elem<DT>::to_f(kr[e]) : 0.f;
+            float sc[ROWS];
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) {
+                float acc = 0.f;
+#pragma unroll
+                for (int e = 0; e < DQ; ++e) acc = fmaf(qsm[r * D + qd * DQ + e], kd[e], acc);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+                sc[r] = tv ? acc : -INFINITY;
+            }
+            float pr[ROWS];
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) {
+                float mx = sc[r];
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float mnew = fmaxf(m[r], mx);
+                const float corr = (m[r] == -INFINITY) ? 0.f : ex2(m[r] - mnew);
+                m[r] = mnew;
+                pr[r] = (sc[r] == -INFINITY) ? 0.f : ex2(sc[r] - mnew);
+                float ps = (qd == 0) ? pr[r] : 0.f;
+                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+                l[r] = l[r] * corr + ps;
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) o[r][e] *= corr;
+            }
+            // PV: lane owns channels lane*DPL .. +DPL
+#pragma unroll
+            for (int tt = 0; tt < 8; ++tt) {
+                const int64_t tk2 = t0 + tt;
+                if (tk2 >= len) break;
+                const auto* vr = V + (row0 + tk2) * D + lane * DPL;
+                float vv[DPL];
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) vv[e] = Elem<DT>::to_f(vr[e]);
+#pragma unroll
+                for (int r = 0; r < ROWS; ++r) {
+                    const float pt = __shfl_sync(0xffffffffu, pr[r], tt * 4);
+#pragma unroll
+                    for (int e = 0; e < DPL; ++e) o[r][e] = fmaf(pt, vv[e], o[r][e]);
+                }
+            }
+        }
+    }
+    // combine warps -> (fin_m, fin_l, osm) for the FP tiers
+    if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) { msm[warp][r] = m[r]; lsm[warp][r] = l[r]; }
+    }
+    __syncthreads();
+    if (threadIdx.x < ROWS) {
+        const int r = threadIdx.x;
+        float M = -INFINITY, Ls = 0.f;
+        for (int w = 0; w < nw; ++w) M = fmaxf(M, msm[w][r]);
+        for (int w = 0; w < nw; ++w)
+            if (msm[w][r] != -INFINITY) Ls += ex2(msm[w][r] - M) * lsm[w][r];
+        fin_m[r] = M;
+        fin_l[r] = Ls;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+        const float f = (m[r] == -INFINITY) ? 0.f : ex2(m[r] - fin_m[r]);
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) atomicAdd(&osm[r * D + lane * DPL + e], o[r][e] * f);
+    }
+    __syncthreads();
+
+    // ---- merge with the middle tier's split-K partials ----
+    if (p.has_mid) {
+        griddep_wait();
+        const int Z = p.B * p.Hkv;
+        const int U = p.cu_units ? p.cu_units[Z] : Z * p.units_per_z;
+        const int zb = p.cu_units ? p.cu_units[z] : z * p.units_per_z;
+        const int ze = p.cu_units ? p.cu_units[z + 1] : (z + 1) * p.units_per_z;
+        int nslots = 0;
+        if (ze > zb) {
+            const int c0 = cta_of_unit(zb, p.n_ctas, U);
+            const int c1 = cta_of_unit(ze - 1, p.n_ctas, U);
+            nslots = c1 - c0 + 1;
+        }
+        // A CTA inside [c0, c1] owns units of z unless its whole unit range is
+        // empty (possible when the grid is larger than the unit count); empty
+        // CTAs wrote no partial, so their slots are skipped.
+        const int c0 = (ze > zb) ? cta_of_unit(zb, p.n_ctas, U) : 0;
+        auto slot_live = [&](int s2) {
+            const int c = c0 + s2;
+            return (int64_t)c * U / p.n_ctas < (int64_t)(c + 1) * U / p.n_ctas;
+        };
+        // Per row: global max / sum over the FP part and every slot.
+        __shared__ float mid_w[64][ROWS];  // weight per slot (nslots <= 64 handled in chunks)
+        __shared__ float fp_w[ROWS], inv_L[ROWS];
+        if (threadIdx.x < ROWS) {
+            const int r = threadIdx.x;
+            float M = fin_m[r];
+            for (int s2 = 0; s2 < nslots; ++s2)
+                if (slot_live(s2)) M = fmaxf(M, p.ws_ml[((int64_t)(zb + s2) * rows + r) * 2]);
+            float Ls = (fin_m[r] == -INFINITY) ? 0.f : ex2(fin_m[r] - M) * fin_l[r];
+            fp_w[r] = (fin_m[r] == -INFINITY) ? 0.f : ex2(fin_m[r] - M);
+            for (int s2 = 0; s2 < nslots; ++s2) {
+                if (!slot_live(s2)) continue;
+                const float ms = p.ws_ml[((int64_t)(zb + s2) * rows + r) * 2];
+                if (ms != -INFINITY) Ls += ex2(ms - M) * p.ws_ml[((int64_t)(zb + s2) * rows + r) * 2 + 1];
+            }
+            inv_L[r] = (Ls > 0.f) ? 1.f / Ls : 0.f;
+            fin_m[r] = M;
+        }
+        __syncthreads();
+        // qsm is reused as the merged middle accumulator
+        for (int i = threadIdx.x; i < ROWS * D; i += kTier0Threads) qsm[i] = 0.f;
+        for (int base = 0; base < nslots; base += 64) {
+            const int nb = min(64, nslots - base);
+            __syncthreads();
+            for (int i = threadIdx.x; i < nb * ROWS; i += kTier0Threads) {
+                const int s2 = i / ROWS, r = i % ROWS;
+                float w = 0.f;
+                if (r < rows && slot_live(base + s2)) {
+                    const float ms = p.ws_ml[((int64_t)(zb + base + s2) * rows + r) * 2];
+                    w = (ms == -INFINITY) ? 0.f : ex2(ms - fin_m[r]);
+                }
+                mid_w[s2][r] = w;
+            }
+            __syncthreads();
+            for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
+                const int r = i / D;
+                float acc = qsm[i];
+                for (int s2 = 0; s2 < nb; ++s2) {
+                    const float w = mid_w[s2][r];
+                    if (w != 0.f) acc = fmaf(w, p.ws_o[(int64_t)(zb + base + s2) * rows * D + i], acc);
+                }
+                qsm[i] = acc;
+            }
+        }
+        __syncthreads();
+        if (p.rotation) {
+            // out = fp + mid @ R
+            for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
+                const int r = i / D, d = i % D;
+                float acc = 0.f;
+                for (int e = 0; e < D; ++e) acc = fmaf(qsm[r * D + e], p.rotation[(int64_t)e * D + d], acc);
+                osm[i] = osm[i] * fp_w[r] + acc;
+            }
+        } else {
+            for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
+                const int r = i / D;
+                osm[i] = osm[i] * fp_w[r] + qsm[i];
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) osm[i] *= inv_L[i / D];
+    } else {
+        for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
+            const int r = i / D;
+            osm[i] = fin_l[r] > 0.f ? osm[i] / fin_l[r] : 0.f;
+        }
+    }
+    __syncthreads();
+    auto* out = reinterpret_cast<typename Elem<DT>::T*>(p.out);
+    for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
+        const int r = i / D, d = i % D;
+        const int j = r / p.n_q, sq = r % p.n_q;
+        out[(int64_t)b * p.o_sb + (int64_t)(h * p.g + j) * p.o_sh + (int64_t)sq * p.o_ss + d] =
+            Elem<DT>::from_f(osm[i]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+static int make_row_map(CUtensorMap* m, const void* base, int64_t n_rows, int row_bytes) {
+    auto enc = encode_fn();
+    if (!enc) return FADE_ERR_CUDA;
+    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+    if (row_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
+    else if (row_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
+    else if (row_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    else if (row_bytes != 16) return FADE_ERR_UNSUPPORTED;
+    cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)n_rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)row_bytes, (cuuint32_t)kStageTokens};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FADE_OK : FADE_ERR_ALIGN;
+}
+
+static int sm_count() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+struct MidKernelInfo {
+    void* fn;
+    int smem;
+    int occ;
+};
+
+// Function attributes are per device: configure each (kernel, device) once.
+constexpr int kMaxDevices = 64;
+
+template <int DT, int D, int KB, int VB, bool VG, int NT>
+static MidKernelInfo mid_info() {
+    static MidKernelInfo info[kMaxDevices] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) dev = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    MidKernelInfo& i = info[dev];
+    if (!i.fn) {
+        i.smem = MidLayout<D, KB, VB, VG, NT>::SMEM_BYTES;
+        cudaFuncSetAttribute(&middle_kernel<DT, D, KB, VB, VG, NT>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, i.smem);
+        int occ = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, &middle_kernel<DT, D, KB, VB, VG, NT>,
+                                                      kMidThreads, i.smem);
+        i.occ = occ > 0 ? occ : 1;
+        i.fn = reinterpret_cast<void*>(&middle_kernel<DT, D, KB, VB, VG, NT>);
+    }
+    return i;
+}
+
+template <int DT, int D, int NT>
+static MidKernelInfo select_mid(int kb, int vb, bool vg) {
+    if (kb == 4 && vb == 4 && !vg) return mid_info<DT, D, 4, 4, false, NT>();
+    if (kb == 4 && vb == 2 && vg) return mid_info<DT, D, 4, 2, true, NT>();
+    if (kb == 2 && vb == 2 && !vg) return mid_info<DT, D, 2, 2, false, NT>();
+    return MidKernelInfo{nullptr, 0, 0};
+}
+
+template <int DT>
+static MidKernelInfo select_mid_d(int D, int NT, int kb, int vb, bool vg) {
+    if (D == 128) return NT == 1 ? select_mid<DT, 128, 1>(kb, vb, vg) : select_mid<DT, 128, 2>(kb, vb, vg);
+    if (D == 64) return NT == 1 ? select_mid<DT, 64, 1>(kb, vb, vg) : select_mid<DT, 64, 2>(kb, vb, vg);
+    return MidKernelInfo{nullptr, 0, 0};
+}
+
+template <int DT>
+static void* select_tier0(int D, int NT) {
+    if (D == 128) return NT == 1 ? (void*)&tier0_merge_kernel<DT, 128, 1> : (void*)&tier0_merge_kernel<DT, 128, 2>;
+    if (D == 64) return NT == 1 ? (void*)&tier0_merge_kernel<DT, 64, 1> : (void*)&tier0_merge_kernel<DT, 64, 2>;
+    return nullptr;
+}
+
+struct Plan {
+    int rows, NT, g;
+    int mid_idx;         // index of the quantised segment or -1
+    int kb, vb;
+    bool vg;
+    int units_per_z;     // uniform
+    int64_t max_units;   // sizing bound
+    int n_ctas;
+    size_t off_err, off_qrot, off_ml, off_o, total;
+    MidKernelInfo mk;
+};
+
+static int make_plan(const fade_decode_desc* d, Plan* pl) {
+    if (!d) return FADE_ERR_INVALID_ARG;
+    if (d->dtype != FADE_F16 && d->dtype != FADE_BF16) return FADE_ERR_UNSUPPORTED;
+    if (d->B < 0 || d->Hq <= 0 || d->Hkv <= 0 || d->D <= 0 || d->n_q <= 0) return FADE_ERR_INVALID_ARG;
+    if (d->Hq % d->Hkv != 0) return FADE_ERR_INVALID_ARG;
+    if (d->D != 64 && d->D != 128) return FADE_ERR_UNSUPPORTED;
+    if (d->n_segments < 0 || d->n_segments > FADE_MAX_SEGMENTS) return FADE_ERR_INVALID_ARG;
+    pl->g = d->Hq / d->Hkv;
+    pl->rows = pl->g * d->n_q;
+    if (pl->rows > 16) return FADE_ERR_UNSUPPORTED;
+    pl->NT = pl->rows > 8 ? 2 : 1;
+    pl->mid_idx = -1;
+    for (int i = 0; i < d->n_segments; ++i) {
+        const fade_kv_segment& s = d->seg[i];
+        if (s.kind == FADE_SEG_FP) {
+            if (!s.k || !s.v) return FADE_ERR_INVALID_ARG;
+            continue;
+        }
+        if (pl->mid_idx >= 0) return FADE_ERR_UNSUPPORTED;  // one quantised tier per call
+        pl->mid_idx = i;
+        if (s.kind == FADE_SEG_INT4) { pl->kb = 4; pl->vb = 4; pl->vg = false; }
+        else if (s.kind == FADE_SEG_INT4K_INT2V) {
+            pl->kb = 4; pl->vb = 2; pl->vg = true;
+            if (s.group < 16 || s.group > kStageTokens || kStageTokens % s.group != 0) return FADE_ERR_UNSUPPORTED;
+        } else if (s.kind == FADE_SEG_ROT) {
+            if (s.bits != 2 && s.bits != 4) return FADE_ERR_UNSUPPORTED;
+            pl->kb = s.bits; pl->vb = s.bits; pl->vg = false;
+            if (!d->rotation) return FADE_ERR_INVALID_ARG;
+        } else return FADE_ERR_INVALID_ARG;
+        if (!s.k || !s.v || !s.k_scale || !s.v_scale) return FADE_ERR_INVALID_ARG;
+        if (!aligned16(s.k) || !aligned16(s.v)) return FADE_ERR_ALIGN;
+        if (s.lens && s.max_len <= 0 && !d->cu_units) return FADE_ERR_INVALID_ARG;
+    }
+    const int Z = d->B * d->Hkv;
+    pl->units_per_z = 0;
+    pl->max_units = 0;
+    pl->n_ctas = 0;
+    if (pl->mid_idx >= 0 && Z > 0) {
+        const fade_kv_segment& s = d->seg[pl->mid_idx];
+        const int64_t ml = s.lens ? s.max_len : s.len;
+        const int64_t upz = (ml + kStageTokens - 1) / kStageTokens;
+        pl->units_per_z = (int)upz;
+        pl->max_units = upz * Z;
+        int dt = d->dtype;
+        pl->mk = dt == FADE_F16 ? select_mid_d<FADE_F16>(d->D, pl->NT, pl->kb, pl->vb, pl->vg)
+                                : select_mid_d<FADE_BF16>(d->D, pl->NT, pl->kb, pl->vb, pl->vg);
+        if (!pl->mk.fn) return FADE_ERR_UNSUPPORTED;
+        int C = d->n_ctas > 0 ? d->n_ctas : sm_count() * pl->mk.occ;
+        if (!d->cu_units && pl->max_units < C) C = (int)pl->max_units;
+        if (C < 1) C = 1;
+        pl->n_ctas = C;
+    }
+    const bool rot = pl->mid_idx >= 0 && d->seg[pl->mid_idx].kind == FADE_SEG_ROT;
+    size_t off = 0;
+    pl->off_err = off; off += 256;
+    pl->off_qrot = off;
+    if (rot) off += ((size_t)d->B * d->Hq * d->n_q * d->D * 4 + 255) / 256 * 256;
+    pl->off_ml = off; off += ((size_t)pl->max_units * pl->rows * 2 * 4 + 255) / 256 * 256;
+    pl->off_o = off; off += (size_t)pl->max_units * pl->rows * d->D * 4;
+    pl->total = off;
+    return FADE_OK;
+}
+
+static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace fade
+
+using namespace fade;
+
+extern "C" size_t fade_decode_attn_workspace_size(const fade_decode_desc* d) {
+    Plan pl;
+    if (make_plan(d, &pl) != FADE_OK) return 0;
+    return pl.total;
+}
+
+extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size_t ws_bytes,
+                                void* stream) {
+    Plan pl;
+    int st = make_plan(d, &pl);
+    if (st != FADE_OK) return st;
+    if (d->B == 0) return FADE_OK;
+    if (!d->q || !d->out) return FADE_ERR_INVALID_ARG;
+    if (!workspace || ws_bytes < pl.total) return FADE_ERR_WORKSPACE;
+    cudaStream_t s = as_stream(stream);
+    uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+    const int Z = d->B * d->Hkv;
+    const bool has_mid = pl.mid_idx >= 0 && pl.max_units > 0;
+    const bool rot = has_mid && d->seg[pl.mid_idx].kind == FADE_SEG_ROT;
+    float* qrot = reinterpret_cast<float*>(ws + pl.off_qrot);
+    const float qk_scale = d->sm_scale * kLog2e;
+
+    if (rot) {
+        void* fn = d->dtype == FADE_F16 ? (void*)&rotate_queries_kernel<FADE_F16>
+                                        : (void*)&rotate_queries_kernel<FADE_BF16>;
+        const void* qp = d->q;
+        int Hq = d->Hq, nq = d->n_q, D = d->D;
+        int64_t a = d->q_sb, b2 = d->q_sh, c2 = d->q_ss;
+        const float* R = d->rotation;
+        void* args[] = {(void*)&qp, &Hq, &nq, &D, &a, &b2, &c2, (void*)&R, (void*)&qrot};
+        FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)(d->B * d->Hq * d->n_q)), dim3(128),
+                                 (size_t)d->D * 4, s, args));
+    }
+    if (has_mid) {
+        const fade_kv_segment& sg = d->seg[pl.mid_idx];
+        CUtensorMap tk, tv;
+        const int rbk = d->D * pl.kb / 8, rbv = d->D * pl.vb / 8;
+        // Rows the maps may address: reads past this extent are zero-filled by
+        // the TMA unit (and masked), never fetched from beyond the allocation.
+        const int64_t maxlen = sg.lens ? sg.max_len : sg.len;
+        int64_t n_rows = sg.n_rows;
+        if (n_rows <= 0) {
+            if (sg.row_base) return FADE_ERR_INVALID_ARG;
+            n_rows = (int64_t)(d->B - 1) * sg.row_sb + (int64_t)(d->Hkv - 1) * sg.row_sh + maxlen;
+        }
+        if (n_rows <= 0) n_rows = 1;
+        if (n_rows >= ((int64_t)1 << 31)) return FADE_ERR_UNSUPPORTED;
+        if ((st = make_row_map(&tk, sg.k, n_rows, rbk)) != FADE_OK) return st;
+        if ((st = make_row_map(&tv, sg.v, n_rows, rbv)) != FADE_OK) return st;
+        MidParams mp = {};
+        mp.dtype = d->dtype;
+        mp.B = d->B; mp.Hq = d->Hq; mp.Hkv = d->Hkv; mp.D = d->D; mp.n_q = d->n_q;
+        mp.g = pl.g; mp.rows = pl.rows;
+        mp.qk_scale = qk_scale;
+        if (rot) {
+            mp.q = qrot; mp.q_is_f32 = 1;
+            mp.q_ss = d->D; mp.q_sh = (int64_t)d->n_q * d->D; mp.q_sb = (int64_t)d->Hq * d->n_q * d->D;
+        } else {
+            mp.q = d->q; mp.q_is_f32 = 0;
+            mp.q_sb = d->q_sb; mp.q_sh = d->q_sh; mp.q_ss = d->q_ss;
+        }
+        mp.k_scale = sg.k_scale; mp.ks_sb = sg.ks_sb; mp.ks_sh = sg.ks_sh;
+        mp.v_scale = sg.v_scale;
+        mp.group = pl.vg ? sg.group : 0;
+        mp.row_sb = sg.row_sb; mp.row_sh = sg.row_sh; mp.row_base = sg.row_base;
+        mp.lens = sg.lens; mp.len = sg.len;
+        mp.cu_units = d->cu_units;
+        mp.units_per_z = pl.units_per_z;
+        mp.n_ctas = pl.n_ctas;
+        mp.ws_ml = reinterpret_cast<float*>(ws + pl.off_ml);
+        mp.ws_o = reinterpret_cast<float*>(ws + pl.off_o);
+        mp.ws_err = reinterpret_cast<int*>(ws + pl.off_err);
+        void* args[] = {(void*)&tk, (void*)&tv, (void*)&mp};
+        FADE_CUDA_TRY(launch_pdl(pl.mk.fn, dim3((unsigned)pl.n_ctas), dim3(kMidThreads),
+                                 (size_t)pl.mk.smem, s, args));
+    }
+    Tier0Params tp = {};
+    tp.B = d->B; tp.Hq = d->Hq; tp.Hkv = d->Hkv; tp.D = d->D; tp.n_q = d->n_q;
+    tp.g = pl.g; tp.rows = pl.rows; tp.qk_scale = qk_scale;
+    tp.q = d->q; tp.q_sb = d->q_sb; tp.q_sh = d->q_sh; tp.q_ss = d->q_ss;
+    tp.out = d->out; tp.o_sb = d->o_sb; tp.o_sh = d->o_sh; tp.o_ss = d->o_ss;
+    tp.n_fp = 0;
+    for (int i = 0; i < d->n_segments; ++i) {
+        const fade_kv_segment& sg = d->seg[i];
+        if (sg.kind != FADE_SEG_FP) continue;
+        FpSeg& f = tp.fp[tp.n_fp++];
+        f.k = sg.k; f.v = sg.v; f.row_sb = sg.row_sb; f.row_sh = sg.row_sh;
+        f.row_base = sg.row_base; f.lens = sg.lens; f.len = sg.len;
+    }
+    tp.has_mid = has_mid ? 1 : 0;
+    tp.rotation = rot ? d->rotation : nullptr;
+    tp.cu_units = d->cu_units;
+    tp.units_per_z = pl.units_per_z;
+    tp.n_ctas = pl.n_ctas;
+    tp.ws_ml = reinterpret_cast<const float*>(ws + pl.off_ml);
+    tp.ws_o = reinterpret_cast<const float*>(ws + pl.off_o);
+    void* fn = d->dtype == FADE_F16 ? select_tier0<FADE_F16>(d->D, pl.NT) : select_tier0<FADE_BF16>(d->D, pl.NT);
+    if (!fn) return FADE_ERR_UNSUPPORTED;
+    void* args[] = {(void*)&tp};
+    FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)Z), dim3(kTier0Threads), 0, s, args));
+    return FADE_OK;
+}
+
+extern "C" int fade_workspace_check(void* workspace, size_t ws_bytes, void* stream) {
+    if (!workspace || ws_bytes < 256) return FADE_ERR_WORKSPACE;
+    int h = 0;
+    cudaStream_t s = as_stream(stream);
+    FADE_CUDA_TRY(cudaMemcpyAsync(&h, workspace, sizeof(int), cudaMemcpyDeviceToHost, s));
+    FADE_CUDA_TRY(cudaStreamSynchronize(s));
+    if (h != 0) {
+        const int zero = 0;
+        FADE_CUDA_TRY(cudaMemcpyAsync(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice, s));
+        FADE_CUDA_TRY(cudaStreamSynchronize(s));
+        return FADE_ERR_TIMEOUT;
+    }
+    return FADE_OK;
+}

@@ -1,0 +1,597 @@
+// K1: symmetric quantisation + bit packing kernels, bit-exact with the
+// reference's torch arithmetic (fade/quant.py).  These run on tier
+// reassignment (per-layer, over the whole middle tier) and on age-out (one
+// token per (b, h) per decode step).
+//
+// Layout rules shared by every kernel here:
+//   * INT4 byte d of a row holds codes 2d (high nibble) and 2d+1 (low nibble),
+//     two's complement (fade/quant.py:26-43).
+//   * 2-bit byte j holds codes 4j..4j+3 at bit offsets 6,4,2,0
+//     (fade/rotated_quant.py:35-48).
+//   * A thread owns 8 consecutive channels of one token row when D % 8 == 0
+//     (one 16-byte load for 16-bit types), else 2 channels.
+#include "common.cuh"
+
+namespace fade {
+
+// ---------------------------------------------------------------------------
+// Strided element access
+// ---------------------------------------------------------------------------
+template <int DT, int E>
+__device__ __forceinline__ void load_elems(const typename Elem<DT>::T* base, int64_t sd,
+                                           bool vec, float (&out)[E]) {
+    using T = typename Elem<DT>::T;
+    if constexpr (E == 8 && DT != FADE_F32) {
+        if (vec) {
+            uint4 raw = __ldg(reinterpret_cast<const uint4*>(base));
+            const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) out[i] = Elem<DT>::to_f(e[i]);
+            return;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < E; ++i) out[i] = Elem<DT>::to_f(base[i * sd]);
+}
+
+__device__ __forceinline__ uint32_t pack_nibbles(int hi, int lo) {
+    return ((uint32_t)(hi & 0xF) << 4) | (uint32_t)(lo & 0xF);
+}
+
+__device__ __forceinline__ uint32_t pack_crumbs(int c0, int c1, int c2, int c3) {
+    return ((uint32_t)(c0 & 3) << 6) | ((uint32_t)(c1 & 3) << 4) | ((uint32_t)(c2 & 3) << 2) |
+           (uint32_t)(c3 & 3);
+}
+
+// Write E/2 packed INT4 bytes for E codes.
+template <int E>
+__device__ __forceinline__ void store_int4(uint8_t* dst, const int (&q)[E]) {
+    if constexpr (E == 8) {
+        uint32_t w = pack_nibbles(q[0], q[1]) | (pack_nibbles(q[2], q[3]) << 8) |
+                     (pack_nibbles(q[4], q[5]) << 16) | (pack_nibbles(q[6], q[7]) << 24);
+        *reinterpret_cast<uint32_t*>(dst) = w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < E / 2; ++i) dst[i] = (uint8_t)pack_nibbles(q[2 * i], q[2 * i + 1]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// quant_k_int4: per-channel absmax over S, one CTA per (b, h, channel block).
+// ---------------------------------------------------------------------------
+constexpr int kQuantThreads = 256;
+
+template <int DT, int E>
+__global__ void __launch_bounds__(kQuantThreads)
+quant_int4_k_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, int dims_per_cta,
+                    uint8_t* __restrict__ packed, typename Elem<DT>::T* __restrict__ scale,
+                    bool vec) {
+    using T = typename Elem<DT>::T;
+    const int z = blockIdx.x;
+    const int b = z / (int)v.H, h = z % (int)v.H;
+    const int d_lo = blockIdx.y * dims_per_cta;
+    const int D = (int)v.D;
+    const int tpr = dims_per_cta / E;           // threads per row
+    const int rows_per_iter = kQuantThreads / tpr;
+    const int slot = threadIdx.x / tpr;
+    const int dg = d_lo + (threadIdx.x % tpr) * E;
+    const bool active = slot < rows_per_iter && dg < D;
+    const T* xb = x + b * v.sb + h * v.sh + (int64_t)dg * v.sd;
+
+    float amax[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) amax[i] = 0.f;
+    if (active) {
+        for (int64_t s = slot; s < v.S; s += rows_per_iter) {
+            float e[E];
+            load_elems<DT, E>(xb + s * v.ss, v.sd, vec, e);
+#pragma unroll
+            for (int i = 0; i < E; ++i) amax[i] = fmaxf(amax[i], fabsf(e[i]));
+        }
+    }
+    // Reduce across row slots through shared memory: [rows_per_iter][dims].
+    __shared__ float red[kQuantThreads * 8];
+#pragma unroll
+    for (int i = 0; i < E; ++i) red[threadIdx.x * E + i] = amax[i];
+    __syncthreads();
+    __shared__ float s_inv[256], s_scale[256];
+    for (int c = threadIdx.x; c < dims_per_cta; c += kQuantThreads) {
+        const int t = c / E, i = c % E;
+        float m = 0.f;
+        for (int r = 0; r < rows_per_iter; ++r) m = fmaxf(m, red[(r * tpr + t) * E + i]);
+        // absmax.clamp(min=EPS) in the dtype; inv = 7/absmax; scale = absmax/7.
+        m = fmaxf(m, Elem<DT>::eps());
+        s_inv[c] = inv_scale<DT>(m, 7.f);
+        const float sc = Elem<DT>::rnd(__fdiv_rn(m, 7.f));
+        s_scale[c] = sc;
+        const int d = d_lo + c;
+        if (d < D) scale[(int64_t)z * D + d] = Elem<DT>::from_f(sc);
+    }
+    __syncthreads();
+    if (!active) return;
+    float inv[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) inv[i] = s_inv[dg - d_lo + i];
+    uint8_t* pb = packed + (int64_t)z * v.S * (D / 2) + dg / 2;
+    for (int64_t s = slot; s < v.S; s += rows_per_iter) {
+        float e[E];
+        load_elems<DT, E>(xb + s * v.ss, v.sd, vec, e);
+        int q[E];
+#pragma unroll
+        for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[i], inv[i])), -8.f, 7.f);
+        store_int4<E>(pb + s * (D / 2), q);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// quant_v_int4: per-token absmax over D.  A row is handled by D/E lanes of
+// one warp (D <= 256 with E = 8); rows are independent.
+// ---------------------------------------------------------------------------
+template <int DT, int E>
+__global__ void __launch_bounds__(kQuantThreads)
+quant_int4_v_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, int tpr_pow2,
+                    uint8_t* __restrict__ packed, typename Elem<DT>::T* __restrict__ scale,
+                    bool vec) {
+    const int D = (int)v.D;
+    const int tpr = tpr_pow2;  // power of two >= D / E, <= 32
+    const int64_t rows = v.B * v.H * v.S;
+    const int64_t row = (int64_t)blockIdx.x * (kQuantThreads / tpr) + threadIdx.x / tpr;
+    const int lane_in_row = threadIdx.x % tpr;
+    const bool active = row < rows;
+    const bool has_elems = lane_in_row * E < D;
+    float e[E];
+    float m = 0.f;
+    if (active && has_elems) {
+        const int64_t s = row % v.S, bh = row / v.S;
+        const int64_t b = bh / v.H, h = bh % v.H;
+        load_elems<DT, E>(x + b * v.sb + h * v.sh + s * v.ss + (int64_t)lane_in_row * E * v.sd,
+                          v.sd, vec, e);
+#pragma unroll
+        for (int i = 0; i < E; ++i) m = fmaxf(m, fabsf(e[i]));
+    }
+    for (int off = tpr / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (!active) return;
+    m = fmaxf(m, Elem<DT>::eps());
+    const float inv = inv_scale<DT>(m, 7.f);
+    if (lane_in_row == 0) scale[row] = Elem<DT>::from_f(Elem<DT>::rnd(__fdiv_rn(m, 7.f)));
+    if (!has_elems) return;
+    int q[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[i], inv)), -8.f, 7.f);
+    store_int4<E>(packed + row * (D / 2) + lane_in_row * (E / 2), q);
+}
+
+// ---------------------------------------------------------------------------
+// Grouped INT2 (fade/quant.py:95-112 / 130-150): one CTA per (b, h, group).
+// ---------------------------------------------------------------------------
+template <int DT, int E>
+__global__ void __launch_bounds__(kQuantThreads)
+quant_int2_grouped_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, int group,
+                          int8_t* __restrict__ codes_i8, uint8_t* __restrict__ codes_u8,
+                          typename Elem<DT>::T* __restrict__ scale, bool vec) {
+    using T = typename Elem<DT>::T;
+    const int D = (int)v.D;
+    const int64_t G = v.S / group;
+    const int64_t zg = blockIdx.x;               // (b*H + h) * G + g
+    const int64_t g = zg % G, bh = zg / G;
+    const int64_t b = bh / v.H, h = bh % v.H;
+    const int tpr = D / E;
+    const int rows_per_iter = kQuantThreads / tpr;
+    const int slot = threadIdx.x / tpr;
+    const int dg = (threadIdx.x % tpr) * E;
+    const bool active = slot < rows_per_iter;
+    const T* xb = x + b * v.sb + h * v.sh + (g * group) * v.ss + (int64_t)dg * v.sd;
+
+    float amax[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) amax[i] = 0.f;
+    if (active) {
+        for (int s = slot; s < group; s += rows_per_iter) {
+            float e[E];
+            load_elems<DT, E>(xb + s * v.ss, v.sd, vec, e);
+#pragma unroll
+            for (int i = 0; i < E; ++i) amax[i] = fmaxf(amax[i], fabsf(e[i]));
+        }
+    }
+    __shared__ float red[kQuantThreads * 8];
+#pragma unroll
+    for (int i = 0; i < E; ++i) red[threadIdx.x * E + i] = amax[i];
+    __syncthreads();
+    __shared__ float s_inv[512];
+    for (int c = threadIdx.x; c < D; c += kQuantThreads) {
+        const int t = c / E, i = c % E;
+        float m = 0.f;
+        for (int r = 0; r < rows_per_iter; ++r) m = fmaxf(m, red[(r * tpr + t) * E + i]);
+        m = fmaxf(m, Elem<DT>::eps());
+        s_inv[c] = inv_scale<DT>(m, 1.f);                  // 1 / absmax
+        scale[zg * D + c] = Elem<DT>::from_f(Elem<DT>::rnd(__fdiv_rn(m, 1.f)));
+    }
+    __syncthreads();
+    if (!active) return;
+    float inv[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) inv[i] = s_inv[dg + i];
+    const int64_t row0 = bh * v.S + g * group;
+    for (int s = slot; s < group; s += rows_per_iter) {
+        float e[E];
+        load_elems<DT, E>(xb + s * v.ss, v.sd, vec, e);
+        int q[E];
+#pragma unroll
+        for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[i], inv[i])), -2.f, 1.f);
+        const int64_t row = row0 + s;
+        if (codes_i8) {
+#pragma unroll
+            for (int i = 0; i < E; ++i) codes_i8[row * D + dg + i] = (int8_t)q[i];
+        }
+        if (codes_u8) {
+            if constexpr (E == 8) {
+                uint8_t* dst = codes_u8 + row * (D / 4) + dg / 4;
+                dst[0] = (uint8_t)pack_crumbs(q[0], q[1], q[2], q[3]);
+                dst[1] = (uint8_t)pack_crumbs(q[4], q[5], q[6], q[7]);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Pack / unpack / dequant (elementwise)
+// ---------------------------------------------------------------------------
+__global__ void pack_codes_kernel(const int8_t* __restrict__ q, int64_t n_out, int bits,
+                                  uint8_t* __restrict__ out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_out;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        if (bits == 4) {
+            out[i] = (uint8_t)pack_nibbles(q[2 * i], q[2 * i + 1]);
+        } else {
+            out[i] = (uint8_t)pack_crumbs(q[4 * i], q[4 * i + 1], q[4 * i + 2], q[4 * i + 3]);
+        }
+    }
+}
+
+__device__ __forceinline__ int sext(uint32_t u, int bits) {
+    const uint32_t sign = 1u << (bits - 1);
+    return (int)(u & (2 * sign - 1)) - (int)((u & sign) << 1);
+}
+
+__global__ void unpack_codes_kernel(const uint8_t* __restrict__ p, int64_t n_in, int bits,
+                                    int8_t* __restrict__ out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_in;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const uint32_t byte = p[i];
+        if (bits == 4) {
+            out[2 * i] = (int8_t)sext(byte >> 4, 4);
+            out[2 * i + 1] = (int8_t)sext(byte & 15u, 4);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) out[4 * i + j] = (int8_t)sext((byte >> (6 - 2 * j)) & 3u, 2);
+        }
+    }
+}
+
+__device__ __forceinline__ int code_at(const uint8_t* __restrict__ codes, int bits, int64_t row,
+                                       int64_t D, int64_t d) {
+    if (bits == 8) return (int)reinterpret_cast<const int8_t*>(codes)[row * D + d];
+    if (bits == 4) {
+        const uint32_t byte = codes[row * (D / 2) + d / 2];
+        return sext((d & 1) ? (byte & 15u) : (byte >> 4), 4);
+    }
+    const uint32_t byte = codes[row * (D / 4) + d / 4];
+    return sext((byte >> (6 - 2 * (d & 3))) & 3u, 2);
+}
+
+template <int DT>
+__global__ void dequant_kernel(const uint8_t* __restrict__ codes, int bits,
+                               const typename Elem<DT>::T* __restrict__ scale, int scale_mode,
+                               int group, int64_t H, int64_t S, int64_t D, int64_t n,
+                               typename Elem<DT>::T* __restrict__ out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t d = i % D, row = i / D;
+        const int64_t s = row % S, bh = row / S;
+        int64_t si;
+        if (scale_mode == 0) si = bh * D + d;
+        else if (scale_mode == 1) si = row;
+        else si = (bh * (S / group) + s / group) * D + d;
+        // q.to(dtype) is exact for these small integers; one rounded multiply.
+        const float q = (float)code_at(codes, bits, row, D, d);
+        out[i] = Elem<DT>::from_f(__fmul_rn(q, Elem<DT>::to_f(scale[si])));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Age-out: the oldest recent-ring token of every (b, h) joins the INT4 middle;
+// the new token takes its ring slot.  One CTA per batch row b, one warp per
+// kv head (strided); lane owns channel pairs.
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void age_out_int4_kernel(typename Elem<DT>::T* __restrict__ ring_k,
+                                    typename Elem<DT>::T* __restrict__ ring_v, int H, int D,
+                                    int64_t ring_cap, int64_t ring_sb, int64_t ring_sh,
+                                    int64_t ring_origin, uint8_t* __restrict__ k_packed,
+                                    uint8_t* __restrict__ v_packed,
+                                    typename Elem<DT>::T* __restrict__ v_scale,
+                                    const typename Elem<DT>::T* __restrict__ k_scale, int64_t mid_sb,
+                                    int64_t mid_sh, int64_t mid_cap, int32_t* __restrict__ mid_len,
+                                    const typename Elem<DT>::T* __restrict__ k_new,
+                                    const typename Elem<DT>::T* __restrict__ v_new, int64_t new_sb,
+                                    int64_t new_sh) {
+    griddep_wait();
+    const int b = blockIdx.x;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+    const int64_t n = mid_len[b];
+    const bool room = n < mid_cap;
+    int64_t slot = (n - ring_origin) % ring_cap;
+    if (slot < 0) slot += ring_cap;
+    for (int h = warp; h < H; h += nw) {
+        auto* ks = ring_k + b * ring_sb + h * ring_sh + slot * D;
+        auto* vs = ring_v + b * ring_sb + h * ring_sh + slot * D;
+        if (room) {
+            const auto* sc = k_scale + ((int64_t)b * H + h) * D;
+            const int64_t row = b * mid_sb + h * mid_sh + n;
+            float m = 0.f;
+            for (int d = lane; d < D; d += 32) m = fmaxf(m, fabsf(Elem<DT>::to_f(vs[d])));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            m = fmaxf(m, Elem<DT>::eps());
+            const float inv = inv_scale<DT>(m, 7.f);
+            if (lane == 0) v_scale[row] = Elem<DT>::from_f(Elem<DT>::rnd(__fdiv_rn(m, 7.f)));
+            for (int p = lane; p < D / 2; p += 32) {
+                int kq[2], vq[2];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int d = 2 * p + j;
+                    const float s = Elem<DT>::to_f(sc[d]);
+                    const float kx = Elem<DT>::to_f(ks[d]);
+                    kq[j] = (s > 0.f) ? quant_code(__fdiv_rn(kx, s), -8.f, 7.f) : 0;
+                    vq[j] = quant_code(Elem<DT>::rnd(__fmul_rn(Elem<DT>::to_f(vs[d]), inv)), -8.f, 7.f);
+                }
+                k_packed[row * (D / 2) + p] = (uint8_t)pack_nibbles(kq[0], kq[1]);
+                v_packed[row * (D / 2) + p] = (uint8_t)pack_nibbles(vq[0], vq[1]);
+            }
+        }
+        __syncwarp();
+        if (k_new && room) {
+            const auto* kn = k_new + b * new_sb + h * new_sh;
+            const auto* vn = v_new + b * new_sb + h * new_sh;
+            for (int d = lane; d < D; d += 32) {
+                ks[d] = kn[d];
+                vs[d] = vn[d];
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && room) mid_len[b] = (int32_t)(n + 1);
+    griddep_launch_dependents();
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+static bool view_ok(const fade_view4& v) {
+    return v.B >= 0 && v.H >= 0 && v.S >= 0 && v.D > 0;
+}
+
+static bool can_vec(const void* x, const fade_view4& v, int elem_bytes) {
+    return v.sd == 1 && aligned16(x) && ((v.sb * elem_bytes) % 16 == 0) &&
+           ((v.sh * elem_bytes) % 16 == 0) && ((v.ss * elem_bytes) % 16 == 0);
+}
+
+template <int DT>
+static int launch_quant_k(const void* x, const fade_view4& v, uint8_t* packed, void* scale,
+                          cudaStream_t st) {
+    using T = typename Elem<DT>::T;
+    const int64_t Z = v.B * v.H;
+    if (Z == 0 || v.S == 0) {
+        // Empty sequence axis: absmax is the clamped EPS for every channel.
+        if (Z == 0) return FADE_OK;
+    }
+    const bool e8 = (v.D % 8 == 0);
+    const int E = e8 ? 8 : 2;
+    int dims_per_cta = (int)(v.D < 256 ? v.D : 256);
+    // For few (b,h) pairs, split channels across CTAs to fill the machine.
+    while (Z * (v.D / dims_per_cta) < 148 && dims_per_cta > 8 * E && dims_per_cta % (2 * E) == 0 &&
+           (dims_per_cta / 2) % E == 0 && v.D % (dims_per_cta / 2) == 0)
+        dims_per_cta /= 2;
+    dim3 grid((unsigned)Z, (unsigned)((v.D + dims_per_cta - 1) / dims_per_cta));
+    const bool vec = e8 && can_vec(x, v, sizeof(T));
+    if (e8)
+        quant_int4_k_kernel<DT, 8><<<grid, kQuantThreads, 0, st>>>(
+            (const T*)x, v, dims_per_cta, packed, (T*)scale, vec);
+    else
+        quant_int4_k_kernel<DT, 2><<<grid, kQuantThreads, 0, st>>>(
+            (const T*)x, v, dims_per_cta, packed, (T*)scale, false);
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}
+
+template <int DT>
+static int launch_quant_v(const void* x, const fade_view4& v, uint8_t* packed, void* scale,
+                          cudaStream_t st) {
+    using T = typename Elem<DT>::T;
+    const int64_t rows = v.B * v.H * v.S;
+    if (rows == 0) return FADE_OK;
+    const int E = (v.D % 8 == 0) ? 8 : 2;
+    int tpr = 1;
+    while (tpr * E < v.D) tpr *= 2;
+    if (tpr > 32) return FADE_ERR_UNSUPPORTED;
+    const int rows_per_cta = kQuantThreads / tpr;
+    const unsigned grid = (unsigned)((rows + rows_per_cta - 1) / rows_per_cta);
+    if (E == 8)
+        quant_int4_v_kernel<DT, 8><<<grid, kQuantThreads, 0, st>>>(
+            (const T*)x, v, tpr, packed, (T*)scale, can_vec(x, v, sizeof(T)));
+    else
+        quant_int4_v_kernel<DT, 2><<<grid, kQuantThreads, 0, st>>>(
+            (const T*)x, v, tpr, packed, (T*)scale, false);
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}
+
+template <int DT>
+static int launch_int2(const void* x, const fade_view4& v, int group, int8_t* ci8, uint8_t* cu8,
+                       void* scale, cudaStream_t st) {
+    using T = typename Elem<DT>::T;
+    const int64_t n = v.B * v.H * (v.S / group);
+    if (n == 0) return FADE_OK;
+    if (v.D % 8 != 0 || v.D / 8 > kQuantThreads || v.D > 512) {
+        if (cu8) return FADE_ERR_UNSUPPORTED;
+        if (v.D / 2 > kQuantThreads) return FADE_ERR_UNSUPPORTED;
+        quant_int2_grouped_kernel<DT, 2><<<(unsigned)n, kQuantThreads, 0, st>>>(
+            (const T*)x, v, group, ci8, cu8, (T*)scale, false);
+    } else {
+        quant_int2_grouped_kernel<DT, 8><<<(unsigned)n, kQuantThreads, 0, st>>>(
+            (const T*)x, v, group, ci8, cu8, (T*)scale, can_vec(x, v, sizeof(T)));
+    }
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}
+
+static unsigned ew_grid(int64_t n) {
+    int64_t g = (n + 255) / 256;
+    if (g > 148 * 32) g = 148 * 32;
+    if (g < 1) g = 1;
+    return (unsigned)g;
+}
+
+}  // namespace fade
+
+using namespace fade;
+
+extern "C" int fade_quant_int4_k(const void* x, int dtype, fade_view4 xv, uint8_t* packed,
+                                 void* scale, void* stream) {
+    if (!view_ok(xv)) return FADE_ERR_INVALID_ARG;
+    if (xv.D % 2 != 0) return FADE_ERR_ODD_DIM;
+    if (xv.B * xv.H == 0) return FADE_OK;
+    if (!x || !packed || !scale) return FADE_ERR_INVALID_ARG;
+    if (xv.D > 4096) return FADE_ERR_UNSUPPORTED;
+    cudaStream_t st = as_stream(stream);
+    switch (dtype) {
+        case FADE_F16: return launch_quant_k<FADE_F16>(x, xv, packed, scale, st);
+        case FADE_BF16: return launch_quant_k<FADE_BF16>(x, xv, packed, scale, st);
+        case FADE_F32: return launch_quant_k<FADE_F32>(x, xv, packed, scale, st);
+    }
+    return FADE_ERR_INVALID_ARG;
+}
+
+extern "C" int fade_quant_int4_v(const void* x, int dtype, fade_view4 xv, uint8_t* packed,
+                                 void* scale, void* stream) {
+    if (!view_ok(xv)) return FADE_ERR_INVALID_ARG;
+    if (xv.D % 2 != 0) return FADE_ERR_ODD_DIM;
+    if (xv.B * xv.H * xv.S == 0) return FADE_OK;
+    if (!x || !packed || !scale) return FADE_ERR_INVALID_ARG;
+    cudaStream_t st = as_stream(stream);
+    switch (dtype) {
+        case FADE_F16: return launch_quant_v<FADE_F16>(x, xv, packed, scale, st);
+        case FADE_BF16: return launch_quant_v<FADE_BF16>(x, xv, packed, scale, st);
+        case FADE_F32: return launch_quant_v<FADE_F32>(x, xv, packed, scale, st);
+    }
+    return FADE_ERR_INVALID_ARG;
+}
+
+extern "C" int fade_quant_int2_grouped(const void* x, int dtype, fade_view4 xv, int group,
+                                       int8_t* codes_i8, uint8_t* codes_u8, void* scale,
+                                       void* stream) {
+    if (!view_ok(xv) || group < 1) return FADE_ERR_INVALID_ARG;
+    if (xv.S % group != 0) return FADE_ERR_GROUP;
+    if (codes_u8 && xv.D % 4 != 0) return FADE_ERR_ODD_DIM;
+    if (xv.B * xv.H * xv.S == 0) return FADE_OK;
+    if (!x || !scale || (!codes_i8 && !codes_u8)) return FADE_ERR_INVALID_ARG;
+    cudaStream_t st = as_stream(stream);
+    switch (dtype) {
+        case FADE_F16: return launch_int2<FADE_F16>(x, xv, group, codes_i8, codes_u8, scale, st);
+        case FADE_BF16: return launch_int2<FADE_BF16>(x, xv, group, codes_i8, codes_u8, scale, st);
+        case FADE_F32: return launch_int2<FADE_F32>(x, xv, group, codes_i8, codes_u8, scale, st);
+    }
+    return FADE_ERR_INVALID_ARG;
+}
+
+extern "C" int fade_pack_codes(const int8_t* q, int64_t rows, int64_t D, int bits, uint8_t* out,
+                               void* stream) {
+    if (rows < 0 || D < 0 || (bits != 4 && bits != 2)) return FADE_ERR_INVALID_ARG;
+    if (D % (8 / bits) != 0) return FADE_ERR_ODD_DIM;
+    const int64_t n_out = rows * D * bits / 8;
+    if (n_out == 0) return FADE_OK;
+    if (!q || !out) return FADE_ERR_INVALID_ARG;
+    pack_codes_kernel<<<ew_grid(n_out), 256, 0, as_stream(stream)>>>(q, n_out, bits, out);
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}
+
+extern "C" int fade_unpack_codes(const uint8_t* packed, int64_t rows, int64_t D, int bits,
+                                 int8_t* out, void* stream) {
+    if (rows < 0 || D < 0 || (bits != 4 && bits != 2)) return FADE_ERR_INVALID_ARG;
+    if (D % (8 / bits) != 0) return FADE_ERR_ODD_DIM;
+    const int64_t n_in = rows * D * bits / 8;
+    if (n_in == 0) return FADE_OK;
+    if (!packed || !out) return FADE_ERR_INVALID_ARG;
+    unpack_codes_kernel<<<ew_grid(n_in), 256, 0, as_stream(stream)>>>(packed, n_in, bits, out);
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}
+
+extern "C" int fade_dequant(const void* codes, int bits, const void* scale, int scale_mode,
+                            int group, int dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+                            void* out, void* stream) {
+    if (B < 0 || H < 0 || S < 0 || D <= 0) return FADE_ERR_INVALID_ARG;
+    if (bits != 8 && bits != 4 && bits != 2) return FADE_ERR_INVALID_ARG;
+    if (scale_mode < 0 || scale_mode > 2) return FADE_ERR_INVALID_ARG;
+    if (scale_mode == 2 && (group < 1)) return FADE_ERR_INVALID_ARG;
+    if (scale_mode == 2 && S % group != 0) return FADE_ERR_GROUP;
+    if (D % (8 / (bits == 8 ? 8 : bits)) != 0) return FADE_ERR_ODD_DIM;
+    const int64_t n = B * H * S * D;
+    if (n == 0) return FADE_OK;
+    if (!codes || !scale || !out) return FADE_ERR_INVALID_ARG;
+    const auto* c = reinterpret_cast<const uint8_t*>(codes);
+    cudaStream_t st = as_stream(stream);
+    switch (dtype) {
+        case FADE_F16:
+            dequant_kernel<FADE_F16><<<ew_grid(n), 256, 0, st>>>(
+                c, bits, (const __half*)scale, scale_mode, group, H, S, D, n, (__half*)out);
+            break;
+        case FADE_BF16:
+            dequant_kernel<FADE_BF16><<<ew_grid(n), 256, 0, st>>>(
+                c, bits, (const __nv_bfloat16*)scale, scale_mode, group, H, S, D, n,
+                (__nv_bfloat16*)out);
+            break;
+        case FADE_F32:
+            dequant_kernel<FADE_F32><<<ew_grid(n), 256, 0, st>>>(
+                c, bits, (const float*)scale, scale_mode, group, H, S, D, n, (float*)out);
+            break;
+        default: return FADE_ERR_INVALID_ARG;
+    }
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}
+
+extern "C" int fade_age_out_int4(void* ring_k, void* ring_v, int dtype, int64_t B, int64_t H,
+                                 int64_t D, int64_t ring_cap, int64_t ring_sb, int64_t ring_sh,
+                                 int64_t ring_origin, uint8_t* k_packed, uint8_t* v_packed,
+                                 void* v_scale, const void* k_scale, int64_t mid_sb, int64_t mid_sh,
+                                 int64_t mid_cap, int32_t* mid_len, const void* k_new,
+                                 const void* v_new, int64_t new_sb, int64_t new_sh, void* stream) {
+    if (B < 0 || H < 0 || D <= 0 || ring_cap <= 0 || mid_cap < 0) return FADE_ERR_INVALID_ARG;
+    if (D % 2 != 0) return FADE_ERR_ODD_DIM;
+    if (B * H == 0) return FADE_OK;
+    if (!ring_k || !ring_v || !k_packed || !v_packed || !v_scale || !k_scale || !mid_len)
+        return FADE_ERR_INVALID_ARG;
+    if ((k_new == nullptr) != (v_new == nullptr)) return FADE_ERR_INVALID_ARG;
+    const int threads = (int)(H < 8 ? (H < 1 ? 1 : H) : 8) * 32;
+    cudaStream_t st = as_stream(stream);
+    switch (dtype) {
+        case FADE_F16:
+            age_out_int4_kernel<FADE_F16><<<(unsigned)B, threads, 0, st>>>(
+                (__half*)ring_k, (__half*)ring_v, (int)H, (int)D, ring_cap, ring_sb, ring_sh,
+                ring_origin, k_packed, v_packed, (__half*)v_scale, (const __half*)k_scale, mid_sb,
+                mid_sh, mid_cap, mid_len, (const __half*)k_new, (const __half*)v_new, new_sb, new_sh);
+            break;
+        case FADE_BF16:
+            age_out_int4_kernel<FADE_BF16><<<(unsigned)B, threads, 0, st>>>(
+                (__nv_bfloat16*)ring_k, (__nv_bfloat16*)ring_v, (int)H, (int)D, ring_cap, ring_sb,
+                ring_sh, ring_origin, k_packed, v_packed, (__nv_bfloat16*)v_scale,
+                (const __nv_bfloat16*)k_scale, mid_sb, mid_sh, mid_cap, mid_len,
+                (const __nv_bfloat16*)k_new, (const __nv_bfloat16*)v_new, new_sb, new_sh);
+            break;
+        default: return FADE_ERR_INVALID_ARG;
+    }
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}

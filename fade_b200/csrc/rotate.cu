@@ -1,0 +1,264 @@
+// Rotated quantisation (fade/rotated_quant.py): x_rot = x @ R^T in fp32, then
+// symmetric quantisation at 2/3/4 bits with fp32 math, K per-channel over S,
+// V per-token.  The dot products accumulate e = 0..D-1 sequentially with
+// separately rounded products and sums (no FMA contraction), a fixed order the
+// CPU oracle restates exactly.  The reference's CPU matmul (MKL) sums in its
+// own order, so codes match it except where a rotated value sits within an
+// fp32 ulp of a rounding boundary.
+#include "common.cuh"
+
+namespace fade {
+
+constexpr int kRotTokens = 32;   // tokens per CTA
+constexpr int kRotThreads = 256;
+
+__device__ __forceinline__ void qrange(int bits, float& lo, float& hi) {
+    lo = (float)(-(1 << (bits - 1)));
+    hi = (float)((1 << (bits - 1)) - 1);
+}
+
+// Rotate kRotTokens rows of (b,h) into xs (fp32 [kRotTokens][D]).
+template <int DT>
+__device__ void rotate_tile(const typename Elem<DT>::T* __restrict__ x, const fade_view4& v, int64_t b,
+                            int64_t h, int64_t t0, int nt, const float* __restrict__ Rt, float* xin,
+                            float* xs) {
+    const int D = (int)v.D;
+    for (int i = threadIdx.x; i < kRotTokens * D; i += blockDim.x) {
+        const int t = i / D, e = i % D;
+        xin[i] = (t < nt) ? Elem<DT>::to_f(x[b * v.sb + h * v.sh + (t0 + t) * v.ss + (int64_t)e * v.sd]) : 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kRotTokens * D; i += blockDim.x) {
+        const int t = i / D, d = i % D;
+        float acc = 0.f;
+        for (int e = 0; e < D; ++e) acc = __fadd_rn(acc, __fmul_rn(xin[t * D + e], Rt[e * D + d]));
+        xs[i] = acc;
+    }
+    __syncthreads();
+}
+
+// pass 0 (K only): per-channel absmax of x_rot into amax (float bits, atomicMax).
+// pass 1: quantise.  kind 0 = K (per-channel scale from amax), 1 = V (per-token).
+template <int DT>
+__global__ void __launch_bounds__(kRotThreads)
+rotated_quant_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, const float* __restrict__ R,
+                     int bits, int kind, int pass, float* __restrict__ amax, uint8_t* __restrict__ packed,
+                     typename Elem<DT>::T* __restrict__ scale) {
+    extern __shared__ float sm[];
+    const int D = (int)v.D;
+    float* Rt = sm;                    // [D][D] transposed: Rt[e][d] = R[d][e]
+    float* xin = Rt + D * D;           // [kRotTokens][D]
+    float* xs = xin + kRotTokens * D;  // [kRotTokens][D]
+    float* tsc = xs + kRotTokens * D;  // [kRotTokens] per-token inv
+    const int64_t tiles = (v.S + kRotTokens - 1) / kRotTokens;
+    const int64_t bh = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+    const int64_t b = bh / v.H, h = bh % v.H;
+    const int64_t t0 = tile * kRotTokens;
+    const int nt = (int)min((int64_t)kRotTokens, v.S - t0);
+    for (int i = threadIdx.x; i < D * D; i += blockDim.x) {
+        const int d = i / D, e = i % D;
+        Rt[e * D + d] = R[i];
+    }
+    __syncthreads();
+    rotate_tile<DT>(x, v, b, h, t0, nt, Rt, xin, xs);
+    float lo, hi;
+    qrange(bits, lo, hi);
+    if (kind == 0 && pass == 0) {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) {
+            float m = 0.f;
+            for (int t = 0; t < nt; ++t) m = fmaxf(m, fabsf(xs[t * D + d]));
+            atomicMax(reinterpret_cast<int*>(amax) + bh * D + d, __float_as_int(m));
+        }
+        return;
+    }
+    if (kind == 1) {
+        // per-token absmax over D
+        for (int t = threadIdx.x / 32; t < nt; t += blockDim.x / 32) {
+            float m = 0.f;
+            for (int d = threadIdx.x % 32; d < D; d += 32) m = fmaxf(m, fabsf(xs[t * D + d]));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            m = fmaxf(m, 1e-8f);
+            if (threadIdx.x % 32 == 0) {
+                tsc[t] = inv_scale<FADE_F32>(m, hi);
+                scale[bh * v.S + t0 + t] = Elem<DT>::from_f(__fdiv_rn(m, hi));
+            }
+        }
+        __syncthreads();
+    } else if (tile == 0) {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) {
+            const float m = fmaxf(amax[bh * D + d], 1e-8f);
+            scale[bh * D + d] = Elem<DT>::from_f(__fdiv_rn(m, hi));
+        }
+    }
+    // quantise + pack: one thread per output byte
+    const int per_byte = (bits == 4) ? 2 : (bits == 2 ? 4 : 1);
+    const int row_bytes = D / per_byte;
+    for (int i = threadIdx.x; i < nt * row_bytes; i += blockDim.x) {
+        const int t = i / row_bytes, j = i % row_bytes;
+        uint32_t byte = 0;
+        for (int k = 0; k < per_byte; ++k) {
+            const int d = j * per_byte + k;
+            const float inv = (kind == 1) ? tsc[t] : inv_scale<FADE_F32>(fmaxf(amax[bh * D + d], 1e-8f), hi);
+            const int q = quant_code(__fmul_rn(xs[t * D + d], inv), lo, hi);
+            if (bits == 4) byte |= (uint32_t)(q & 15) << (4 - 4 * k);
+            else if (bits == 2) byte |= (uint32_t)(q & 3) << (6 - 2 * k);
+            else byte = (uint32_t)(q & 255);
+        }
+        packed[(bh * v.S + t0 + t) * row_bytes + j] = (uint8_t)byte;
+    }
+}
+
+__device__ __forceinline__ int unpack_code(const uint8_t* __restrict__ p, int bits, int64_t row, int D, int d) {
+    if (bits == 4) {
+        const uint32_t byte = p[row * (D / 2) + d / 2];
+        const uint32_t u = (d & 1) ? (byte & 15u) : (byte >> 4);
+        return (int)(u & 7u) - (int)(u & 8u);
+    }
+    if (bits == 2) {
+        const uint32_t byte = p[row * (D / 4) + d / 4];
+        const uint32_t u = (byte >> (6 - 2 * (d & 3))) & 3u;
+        return (int)(u & 1u) - (int)(u & 2u);
+    }
+    return (int)reinterpret_cast<const int8_t*>(p)[row * D + d];
+}
+
+// out = rnd_dt( sum_e rnd_dt(q*scale)[e] * R[e][d] )
+template <int DT>
+__global__ void __launch_bounds__(kRotThreads)
+rotated_dequant_kernel(const uint8_t* __restrict__ packed, int bits, const typename Elem<DT>::T* __restrict__ scale,
+                       int scale_mode, const float* __restrict__ R, int64_t H, int64_t S, int D,
+                       typename Elem<DT>::T* __restrict__ out) {
+    extern __shared__ float sm[];
+    float* Rs = sm;               // [D][D] as given (row e, col d)
+    float* xs = Rs + D * D;       // [kRotTokens][D]
+    const int64_t tiles = (S + kRotTokens - 1) / kRotTokens;
+    const int64_t bh = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+    const int64_t t0 = tile * kRotTokens;
+    const int nt = (int)min((int64_t)kRotTokens, S - t0);
+    for (int i = threadIdx.x; i < D * D; i += blockDim.x) Rs[i] = R[i];
+    for (int i = threadIdx.x; i < kRotTokens * D; i += blockDim.x) {
+        const int t = i / D, e = i % D;
+        float val = 0.f;
+        if (t < nt) {
+            const int64_t row = bh * S + t0 + t;
+            const float sc = Elem<DT>::to_f(scale_mode == 0 ? scale[bh * D + e] : scale[row]);
+            val = Elem<DT>::rnd(__fmul_rn((float)unpack_code(packed, bits, row, D, e), sc));
+        }
+        xs[i] = val;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * D; i += blockDim.x) {
+        const int t = i / D, d = i % D;
+        float acc = 0.f;
+        for (int e = 0; e < D; ++e) acc = __fadd_rn(acc, __fmul_rn(xs[t * D + e], Rs[e * D + d]));
+        out[(bh * S + t0 + t) * D + d] = Elem<DT>::from_f(acc);
+    }
+}
+
+}  // namespace fade
+
+using namespace fade;
+
+extern "C" int fade_rotated_quant(const void* x, int dtype, fade_view4 xv, const float* R, int bits,
+                                  int kind, uint8_t* packed, void* scale, void* workspace,
+                                  size_t ws_bytes, void* stream) {
+    if (xv.B < 0 || xv.H < 0 || xv.S < 0 || xv.D <= 0) return FADE_ERR_INVALID_ARG;
+    if (bits != 2 && bits != 3 && bits != 4) return FADE_ERR_INVALID_ARG;
+    if (kind != 0 && kind != 1) return FADE_ERR_INVALID_ARG;
+    if ((bits == 4 && xv.D % 2) || (bits == 2 && xv.D % 4)) return FADE_ERR_ODD_DIM;
+    if (xv.D > 128) return FADE_ERR_UNSUPPORTED;
+    const int64_t Z = xv.B * xv.H;
+    if (Z == 0 || xv.S == 0) return FADE_OK;
+    if (!x || !R || !packed || !scale) return FADE_ERR_INVALID_ARG;
+    const size_t need = (size_t)Z * xv.D * 4;
+    if (kind == 0 && (!workspace || ws_bytes < need)) return FADE_ERR_WORKSPACE;
+    cudaStream_t st = as_stream(stream);
+    const int D = (int)xv.D;
+    const size_t smem = ((size_t)D * D + 2 * kRotTokens * D + kRotTokens) * 4;
+    const int64_t tiles = (xv.S + kRotTokens - 1) / kRotTokens;
+    const unsigned grid = (unsigned)(Z * tiles);
+    float* amax = reinterpret_cast<float*>(workspace);
+    switch (dtype) {
+        case FADE_F16: {
+            auto k = rotated_quant_kernel<FADE_F16>;
+            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            if (kind == 0) {
+                FADE_CUDA_TRY(cudaMemsetAsync(amax, 0, need, st));
+                k<<<grid, kRotThreads, smem, st>>>((const __half*)x, xv, R, bits, kind, 0, amax, packed, (__half*)scale);
+                FADE_LAUNCH_CHECK();
+            }
+            k<<<grid, kRotThreads, smem, st>>>((const __half*)x, xv, R, bits, kind, 1, amax, packed, (__half*)scale);
+            break;
+        }
+        case FADE_BF16: {
+            auto k = rotated_quant_kernel<FADE_BF16>;
+            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            if (kind == 0) {
+                FADE_CUDA_TRY(cudaMemsetAsync(amax, 0, need, st));
+                k<<<grid, kRotThreads, smem, st>>>((const __nv_bfloat16*)x, xv, R, bits, kind, 0, amax, packed,
+                                                   (__nv_bfloat16*)scale);
+                FADE_LAUNCH_CHECK();
+            }
+            k<<<grid, kRotThreads, smem, st>>>((const __nv_bfloat16*)x, xv, R, bits, kind, 1, amax, packed,
+                                               (__nv_bfloat16*)scale);
+            break;
+        }
+        case FADE_F32: {
+            auto k = rotated_quant_kernel<FADE_F32>;
+            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            if (kind == 0) {
+                FADE_CUDA_TRY(cudaMemsetAsync(amax, 0, need, st));
+                k<<<grid, kRotThreads, smem, st>>>((const float*)x, xv, R, bits, kind, 0, amax, packed, (float*)scale);
+                FADE_LAUNCH_CHECK();
+            }
+            k<<<grid, kRotThreads, smem, st>>>((const float*)x, xv, R, bits, kind, 1, amax, packed, (float*)scale);
+            break;
+        }
+        default: return FADE_ERR_INVALID_ARG;
+    }
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}
+
+extern "C" int fade_rotated_dequant(const uint8_t* packed, int bits, const void* scale, int scale_mode,
+                                    const float* R, int dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+                                    void* out, void* stream) {
+    if (B < 0 || H < 0 || S < 0 || D <= 0) return FADE_ERR_INVALID_ARG;
+    if (bits != 2 && bits != 3 && bits != 4) return FADE_ERR_INVALID_ARG;
+    if (scale_mode != 0 && scale_mode != 1) return FADE_ERR_INVALID_ARG;
+    if (D > 128) return FADE_ERR_UNSUPPORTED;
+    const int64_t Z = B * H;
+    if (Z == 0 || S == 0) return FADE_OK;
+    if (!packed || !scale || !R || !out) return FADE_ERR_INVALID_ARG;
+    const size_t smem = ((size_t)D * D + kRotTokens * D) * 4;
+    const int64_t tiles = (S + kRotTokens - 1) / kRotTokens;
+    const unsigned grid = (unsigned)(Z * tiles);
+    cudaStream_t st = as_stream(stream);
+    switch (dtype) {
+        case FADE_F16: {
+            auto k = rotated_dequant_kernel<FADE_F16>;
+            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            k<<<grid, kRotThreads, smem, st>>>(packed, bits, (const __half*)scale, scale_mode, R, H, S, (int)D,
+                                               (__half*)out);
+            break;
+        }
+        case FADE_BF16: {
+            auto k = rotated_dequant_kernel<FADE_BF16>;
+            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            k<<<grid, kRotThreads, smem, st>>>(packed, bits, (const __nv_bfloat16*)scale, scale_mode, R, H, S,
+                                               (int)D, (__nv_bfloat16*)out);
+            break;
+        }
+        case FADE_F32: {
+            auto k = rotated_dequant_kernel<FADE_F32>;
+            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            k<<<grid, kRotThreads, smem, st>>>(packed, bits, (const float*)scale, scale_mode, R, H, S, (int)D,
+                                               (float*)out);
+            break;
+        }
+        default: return FADE_ERR_INVALID_ARG;
+    }
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}

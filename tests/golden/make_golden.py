@@ -1,0 +1,221 @@
+"""Generate the golden fixtures in tests/golden/ by running the REFERENCE.
+
+Usage (needs the reference checkout; it is not present on the GPU box, which
+only reads the committed .npz files):
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /path/to/fade-reference
+
+Every fixture stores raw storage bits (uint16 for fp16/bf16) so comparisons
+are bit-exact.  Inputs are seeded synthetic tensors with the shapes and value
+distributions of the benchmark configs (N(0,1) with per-head outlier
+channels scaled x8, keys RoPE'd at their positions).
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+OUT = Path(__file__).resolve().parent
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    if t.dtype in (torch.float16, torch.bfloat16):
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+    if t.dtype == torch.float32:
+        return t.contiguous().numpy().view(np.uint32).copy()
+    return t.contiguous().numpy().copy()
+
+
+def outlier_tensor(shape, gen, n_out=4, mult=8.0):
+    x = torch.randn(*shape, generator=gen)
+    H, D = shape[1], shape[-1]
+    for h in range(H):
+        ch = torch.randperm(D, generator=gen)[:n_out]
+        x[:, h, :, ch] *= mult
+    return x
+
+
+def main(ref: str) -> None:
+    sys.path.insert(0, ref)
+    import torch.nn.functional as F
+    from fade.cache import TieredKVCache
+    from fade.policy import _assign_one_layer
+    from fade.quant import quant_k_int2, quant_k_int4, quant_v_int2, quant_v_int4
+    from fade.rope import Vanilla
+    from fade.rotated_quant import (_random_orthogonal, rotated_dequant_k, rotated_dequant_v,
+                                    rotated_quant_k, rotated_quant_v)
+    from fade.backends import RotatedINT4Backend
+
+    dts = {"f16": torch.float16, "bf16": torch.bfloat16}
+
+    # ------------------------------------------------------------------ quant
+    g = torch.Generator().manual_seed(1234)
+    q = {}
+    for name, dt in dts.items():
+        x = outlier_tensor((2, 3, 37, 64), g).to(dt)
+        x[0, 0, :, 5] = 0          # an all-zero channel (K scale 0 in fp16)
+        x[0, 1, 7, :] = 0          # an all-zero token (V scale 0 in fp16)
+        x[1, 0, :, 9] *= 1e-6      # tiny channel (subnormal range in fp16)
+        x[1, 2, 3, :] *= 1e-6      # tiny token
+        x[1, 1, :, 11] *= 300.0    # large channel
+        kp, ks = quant_k_int4(x)
+        vp, vs = quant_v_int4(x)
+        q[f"{name}_x"] = bits(x)
+        q[f"{name}_k_packed"] = kp.numpy()
+        q[f"{name}_k_scale"] = bits(ks)
+        q[f"{name}_v_packed"] = vp.numpy()
+        q[f"{name}_v_scale"] = bits(vs)
+        x2 = outlier_tensor((2, 2, 128, 64), g).to(dt)
+        x2[0, 1, :32, 3] = 0
+        q[f"{name}_x2"] = bits(x2)
+        for G in (32, 64):
+            kq, kss = quant_k_int2(x2, group_size=G)
+            vq, vss = quant_v_int2(x2, group_size=G)
+            q[f"{name}_k2_g{G}_codes"] = kq.numpy()
+            q[f"{name}_k2_g{G}_scale"] = bits(kss)
+            q[f"{name}_v2_g{G}_codes"] = vq.numpy()
+            q[f"{name}_v2_g{G}_scale"] = bits(vss)
+    np.savez_compressed(OUT / "quant.npz", **q)
+
+    # --------------------------------------------------------------- rotated
+    r = {}
+    for D in (64, 128):
+        R = _random_orthogonal(D, 42)
+        r[f"R{D}"] = R.numpy()
+        for name, dt in dts.items():
+            x = outlier_tensor((1, 2, 40, D), g).to(dt)
+            r[f"{name}_D{D}_x"] = bits(x)
+            for b in (2, 4):
+                kp, ks = rotated_quant_k(x, R, bits=b)
+                vp, vs = rotated_quant_v(x, R, bits=b)
+                r[f"{name}_D{D}_b{b}_k_packed"] = kp.numpy()
+                r[f"{name}_D{D}_b{b}_k_scale"] = bits(ks)
+                r[f"{name}_D{D}_b{b}_v_packed"] = vp.numpy()
+                r[f"{name}_D{D}_b{b}_v_scale"] = bits(vs)
+                r[f"{name}_D{D}_b{b}_k_deq"] = bits(rotated_dequant_k(kp, ks, R, bits=b, dtype=dt))
+                r[f"{name}_D{D}_b{b}_v_deq"] = bits(rotated_dequant_v(vp, vs, R, bits=b, dtype=dt))
+    np.savez_compressed(OUT / "rotated.npz", **r)
+
+    # ------------------------------------------------------------------ rope
+    ro = {}
+    for name, dt in dts.items():
+        S, D = 48, 64
+        scheme = Vanilla(theta=1e6, head_dim=D)
+        pos = torch.arange(S)
+        keep = torch.tensor([0, 1, 2, 3, 7, 8, 15, 20, 21, 30, 40, 44, 45, 46, 47])
+        new_pos = torch.arange(keep.numel())
+        c_old, s_old = scheme.compute_cos_sin(pos, torch.device("cpu"), model_dtype=dt)
+        c_new, s_new = scheme.compute_cos_sin(new_pos, torch.device("cpu"), model_dtype=dt)
+        k_pre = torch.randn(1, 2, S, D, generator=g).to(dt)
+        k = TieredKVCache._apply_rope(k_pre, c_old, s_old)
+        k_un = TieredKVCache._inverse_rope(k, c_old, s_old)
+        out = TieredKVCache._apply_rope(k_un.index_select(-2, keep).contiguous(), c_new, s_new)
+        ro[f"{name}_k"] = bits(k)
+        ro[f"{name}_keep"] = keep.numpy()
+        ro[f"{name}_cos_old"] = c_old[0, 0].numpy()
+        ro[f"{name}_sin_old"] = s_old[0, 0].numpy()
+        ro[f"{name}_cos_new"] = c_new[0, 0].numpy()
+        ro[f"{name}_sin_new"] = s_new[0, 0].numpy()
+        ro[f"{name}_out"] = bits(out)
+    np.savez_compressed(OUT / "rope.npz", **ro)
+
+    # ------------------------------------------- decode: config 1 (Qwen-0.5B)
+    gen = torch.Generator().manual_seed(1)
+    B, Hq, Hkv, D, S = 1, 14, 2, 64, 2048
+    dt = torch.float16
+    scheme = Vanilla(theta=1e6, head_dim=D)
+    k_pre = outlier_tensor((B, Hkv, S, D), gen)
+    v = outlier_tensor((B, Hkv, S, D), gen).to(dt)
+    c, s = scheme.compute_cos_sin(torch.arange(S), torch.device("cpu"), model_dtype=dt)
+    k = TieredKVCache._apply_rope(k_pre.to(dt), c, s)
+    qv = torch.randn(B, Hq, 1, D, generator=gen).to(dt)
+    cache = TieredKVCache(n_sink=4, recent_window=64, int4_budget=None, dtype=dt, rope_theta=1e6, head_dim=D)
+    cache.update(k, v, 0)
+    tiers = _assign_one_layer(S, torch.arange(S, dtype=torch.float32), 4, 64, None, 0)
+    cache.apply_tier_assignment(0, tiers)
+    st = cache._layers[0]
+    K, V = cache._materialize(0)
+    out = F.scaled_dot_product_attention(qv, K, V, enable_gqa=True)
+    out32 = F.scaled_dot_product_attention(qv.float(), K.float(), V.float(), enable_gqa=True)
+    d1 = {
+        "q": bits(qv), "k_roped": bits(k), "v": bits(v),
+        "sink_k": bits(st.sink_k), "sink_v": bits(st.sink_v),
+        "recent_k": bits(st.fp16_k), "recent_v": bits(st.fp16_v),
+        "int4_kq": st.int4_kq.numpy(), "int4_ks": bits(st.int4_ks),
+        "int4_vq": st.int4_vq.numpy(), "int4_vs": bits(st.int4_vs),
+        "out_ref": bits(out), "out_ref32": bits(out32),
+    }
+    np.savez_compressed(OUT / "decode_cfg1.npz", **d1)
+
+    # ------------------- decode: config 3 shape, small (K INT4, V INT2, evict)
+    gen = torch.Generator().manual_seed(3)
+    B, Hq, Hkv, D, S = 2, 8, 2, 128, 512
+    dt = torch.float16
+    scheme = Vanilla(theta=1e6, head_dim=D)
+    k_pre = outlier_tensor((B, Hkv, S, D), gen)
+    v = outlier_tensor((B, Hkv, S, D), gen).to(dt)
+    c, s = scheme.compute_cos_sin(torch.arange(S), torch.device("cpu"), model_dtype=dt)
+    k = TieredKVCache._apply_rope(k_pre.to(dt), c, s)
+    qv = torch.randn(B, Hq, 1, D, generator=gen).to(dt)
+    cache = TieredKVCache(n_sink=4, recent_window=64, int4_budget=100, dtype=dt, rope_theta=1e6,
+                          head_dim=D, middle_v_bits=2, rope_scheme=scheme)
+    cache.update(k, v, 0)
+    torch.manual_seed(3)
+    scores = torch.distributions.Dirichlet(torch.full((S,), 0.1)).sample((Hkv,)).sum(0)
+    tiers = _assign_one_layer(S, scores, 4, 64, 100, 0)
+    cache.apply_tier_assignment(0, tiers)
+    st = cache._layers[0]
+    K, V = cache._materialize(0)
+    out = F.scaled_dot_product_attention(qv, K, V, enable_gqa=True)
+    out32 = F.scaled_dot_product_attention(qv.float(), K.float(), V.float(), enable_gqa=True)
+    d3 = {
+        "q": bits(qv), "k_roped": bits(k), "v": bits(v), "tiers": tiers.numpy(),
+        "sink_k": bits(st.sink_k), "sink_v": bits(st.sink_v),
+        "recent_k": bits(st.fp16_k), "recent_v": bits(st.fp16_v),
+        "int4_kq": st.int4_kq.numpy(), "int4_ks": bits(st.int4_ks),
+        "int4_vq2": st.int4_vq.numpy(), "int4_vs2": bits(st.int4_vs),
+        "n_mid": np.int64(st.int4_pos.shape[0]), "next_position": np.int64(st.next_position),
+        "out_ref": bits(out), "out_ref32": bits(out32),
+    }
+    np.savez_compressed(OUT / "decode_cfg3_small.npz", **d3)
+
+    # --------------------- decode: rotated 2-bit backend (config 4 shape), bf16
+    gen = torch.Generator().manual_seed(4)
+    B, Hq, Hkv, D, S = 1, 7, 1, 128, 300
+    dt = torch.bfloat16
+    k = outlier_tensor((B, Hkv, S, D), gen).to(dt)
+    v = outlier_tensor((B, Hkv, S, D), gen).to(dt)
+    qv = torch.randn(B, Hq, 1, D, generator=gen).to(dt)
+    backend = RotatedINT4Backend(head_dim=D, bits=2, seed=42)
+    cache = TieredKVCache(n_sink=4, recent_window=64, int4_budget=None, dtype=dt, head_dim=D,
+                          quant_backend=backend)
+    cache.update(k, v, 0)
+    tiers = _assign_one_layer(S, torch.arange(S, dtype=torch.float32), 4, 64, None, 0)
+    cache.apply_tier_assignment(0, tiers)
+    st = cache._layers[0]
+    K, V = cache._materialize(0)
+    out = F.scaled_dot_product_attention(qv, K, V, enable_gqa=True)
+    out32 = F.scaled_dot_product_attention(qv.float(), K.float(), V.float(), enable_gqa=True)
+    d4 = {
+        "q": bits(qv), "k": bits(k), "v": bits(v), "R": _random_orthogonal(D, 42).numpy(),
+        "sink_k": bits(st.sink_k), "sink_v": bits(st.sink_v),
+        "recent_k": bits(st.fp16_k), "recent_v": bits(st.fp16_v),
+        "rot_kq": st.backend_k["packed"].numpy(), "rot_ks": bits(st.backend_k["scale"]),
+        "rot_vq": st.backend_v["packed"].numpy(), "rot_vs": bits(st.backend_v["scale"]),
+        "out_ref": bits(out), "out_ref32": bits(out32),
+    }
+    np.savez_compressed(OUT / "decode_rot_small.npz", **d4)
+    print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    import os
+
+    ref_path = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FADE_REFERENCE_PATH")
+    if not ref_path:
+        raise SystemExit("usage: make_golden.py <path to the reference checkout>")
+    main(ref_path)

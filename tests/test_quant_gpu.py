@@ -1,0 +1,230 @@
+"""K1 quantisers on the GPU: bit-exact against the reference's golden vectors
+and the CPU oracle (codes, packed bytes and scales compared as raw bits)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from gpu_util import np_to_dt_tensor, seeded_outliers, t_bits, t_from_bits, t_vals
+from oracle import quant as oq
+from oracle import rope as orope
+from oracle.numerics import from_bits, to_bits
+
+pytestmark = pytest.mark.gpu
+DTS = ("f16", "bf16")
+
+
+@pytest.mark.parametrize("dt", DTS)
+def test_int4_golden(cuda_device, dt):
+    from fade_b200.quant import quant_k_int4, quant_v_int4
+
+    g = golden("quant")
+    x = t_from_bits(g[f"{dt}_x"], dt)
+    kp, ks = quant_k_int4(x)
+    vp, vs = quant_v_int4(x)
+    np.testing.assert_array_equal(kp.cpu().numpy(), g[f"{dt}_k_packed"])
+    np.testing.assert_array_equal(t_bits(ks), g[f"{dt}_k_scale"])
+    np.testing.assert_array_equal(vp.cpu().numpy(), g[f"{dt}_v_packed"])
+    np.testing.assert_array_equal(t_bits(vs), g[f"{dt}_v_scale"])
+
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("G", (32, 64))
+def test_int2_golden(cuda_device, dt, G):
+    from fade_b200.quant import quant_int2_grouped_packed, quant_k_int2, quant_v_int2
+
+    g = golden("quant")
+    x = t_from_bits(g[f"{dt}_x2"], dt)
+    kq, ks = quant_k_int2(x, group_size=G)
+    vq, vs = quant_v_int2(x, group_size=G)
+    np.testing.assert_array_equal(kq.cpu().numpy(), g[f"{dt}_k2_g{G}_codes"])
+    np.testing.assert_array_equal(t_bits(ks), g[f"{dt}_k2_g{G}_scale"])
+    np.testing.assert_array_equal(vq.cpu().numpy(), g[f"{dt}_v2_g{G}_codes"])
+    np.testing.assert_array_equal(t_bits(vs), g[f"{dt}_v2_g{G}_scale"])
+    qp, sp = quant_int2_grouped_packed(x, G)
+    np.testing.assert_array_equal(qp.cpu().numpy(), oq.pack2(g[f"{dt}_v2_g{G}_codes"]))
+    np.testing.assert_array_equal(t_bits(sp), g[f"{dt}_v2_g{G}_scale"])
+
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("shape", [(2, 4, 1000, 128), (1, 2, 2048, 64), (3, 1, 7, 96), (1, 1, 1, 6)])
+def test_int4_vs_oracle_random(cuda_device, dt, shape):
+    from fade_b200.quant import quant_k_int4, quant_v_int4
+
+    x = seeded_outliers(shape, seed=sum(shape), dt=dt)
+    xt = np_to_dt_tensor(x, dt)
+    kp, ks = quant_k_int4(xt)
+    vp, vs = quant_v_int4(xt)
+    okp, oks = oq.quant_k_int4(x, dt)
+    ovp, ovs = oq.quant_v_int4(x, dt)
+    np.testing.assert_array_equal(kp.cpu().numpy(), okp)
+    np.testing.assert_array_equal(t_bits(ks), to_bits(oks, dt))
+    np.testing.assert_array_equal(vp.cpu().numpy(), ovp)
+    np.testing.assert_array_equal(t_bits(vs), to_bits(ovs, dt))
+
+
+def test_int4_strided_input(cuda_device):
+    """Non-contiguous views (e.g. an index_select-free slice of a bigger cache)."""
+    from fade_b200.quant import quant_k_int4, quant_v_int4
+
+    x = seeded_outliers((2, 3, 300, 128), seed=5, dt="f16")
+    big = np_to_dt_tensor(x, "f16")
+    view = big[:, :, 17:250]          # strided along S (still contiguous rows)
+    tview = big.transpose(1, 2).contiguous().transpose(1, 2)[:, :, 17:250]  # exotic strides
+    for t in (view, tview):
+        kp, ks = quant_k_int4(t)
+        vp, vs = quant_v_int4(t)
+        okp, oks = oq.quant_k_int4(x[:, :, 17:250], "f16")
+        ovp, ovs = oq.quant_v_int4(x[:, :, 17:250], "f16")
+        np.testing.assert_array_equal(kp.cpu().numpy(), okp)
+        np.testing.assert_array_equal(t_bits(ks), to_bits(oks, "f16"))
+        np.testing.assert_array_equal(vp.cpu().numpy(), ovp)
+        np.testing.assert_array_equal(t_bits(vs), to_bits(ovs, "f16"))
+
+
+def test_errors_match_reference_messages(cuda_device):
+    from fade_b200.quant import _pack_int4_last_dim, quant_k_int2, quant_k_int4
+
+    x = torch.zeros(1, 1, 4, 3, dtype=torch.float16, device="cuda")
+    with pytest.raises(ValueError, match="last dim must be even for INT4 packing, got 3"):
+        quant_k_int4(x)
+    with pytest.raises(ValueError, match="last dim must be even for INT4 packing"):
+        _pack_int4_last_dim(torch.zeros(2, 5, dtype=torch.int8, device="cuda"))
+    with pytest.raises(ValueError, match="S=10 must be divisible by group_size=4"):
+        quant_k_int2(torch.zeros(1, 1, 10, 8, dtype=torch.float16, device="cuda"), group_size=4)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        quant_k_int4(torch.zeros(1, 1, 4, 4, dtype=torch.float16))
+
+
+def test_zero_and_nan_edge_cases(cuda_device):
+    """fp16 all-zero channel -> scale 0 and code 0 (0*inf = NaN -> 0), like torch on CPU."""
+    from fade_b200.quant import quant_k_int4, quant_v_int4
+
+    x = torch.zeros(1, 2, 5, 8, dtype=torch.float16, device="cuda")
+    kp, ks = quant_k_int4(x)
+    vp, vs = quant_v_int4(x)
+    assert int(kp.abs().sum()) == 0 and float(ks.abs().sum()) == 0.0
+    assert int(vp.abs().sum()) == 0 and float(vs.abs().sum()) == 0.0
+
+
+@pytest.mark.parametrize("dt", DTS)
+def test_pack_unpack_dequant(cuda_device, dt):
+    from fade_b200.quant import (_pack_int2_last_dim, _pack_int4_last_dim, _unpack_int2_last_dim,
+                                 _unpack_int4_last_dim, dequant_int2_packed, dequant_int4,
+                                 dequant_v_int2, quant_k_int4, quant_v_int2, quant_v_int4)
+
+    rng = np.random.default_rng(3)
+    q4 = torch.from_numpy(rng.integers(-8, 8, size=(2, 3, 33, 64)).astype(np.int8)).cuda()
+    p4 = _pack_int4_last_dim(q4)
+    np.testing.assert_array_equal(p4.cpu().numpy(), oq.pack_int4(q4.cpu().numpy()))
+    assert torch.equal(_unpack_int4_last_dim(p4), q4)
+    q2 = torch.from_numpy(rng.integers(-2, 2, size=(2, 3, 33, 64)).astype(np.int8)).cuda()
+    p2 = _pack_int2_last_dim(q2)
+    np.testing.assert_array_equal(p2.cpu().numpy(), oq.pack2(q2.cpu().numpy()))
+    assert torch.equal(_unpack_int2_last_dim(p2), q2)
+
+    x = seeded_outliers((2, 3, 64, 64), seed=9, dt=dt)
+    xt = np_to_dt_tensor(x, dt)
+    kp, ks = quant_k_int4(xt)
+    vp, vs = quant_v_int4(xt)
+    okp, oks = oq.quant_k_int4(x, dt)
+    ovp, ovs = oq.quant_v_int4(x, dt)
+    np.testing.assert_array_equal(t_bits(dequant_int4(kp, ks, dtype=xt.dtype)), to_bits(oq.dequant_int4(okp, oks, dt), dt))
+    np.testing.assert_array_equal(t_bits(dequant_int4(vp, vs, dtype=xt.dtype)), to_bits(oq.dequant_int4(ovp, ovs, dt), dt))
+    q, s = quant_v_int2(xt, group_size=32)
+    oqq, oss = oq.quant_int2_grouped(x, 32, dt)
+    ref = to_bits(oq.dequant_grouped(oqq, oss, 32, dt), dt)
+    np.testing.assert_array_equal(t_bits(dequant_v_int2(q, s, group_size=32, dtype=xt.dtype)), ref)
+    np.testing.assert_array_equal(t_bits(dequant_int2_packed(_pack_int2_last_dim(q), s, 32, dtype=xt.dtype)), ref)
+
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("D", (64, 128))
+@pytest.mark.parametrize("bits", (2, 4))
+def test_rotated_quant(cuda_device, dt, D, bits):
+    """Bit-exact vs the oracle (same fp32 summation order); near-exact vs the reference."""
+    from fade_b200.rotated_quant import rotated_dequant_k, rotated_dequant_v, rotated_quant_k, rotated_quant_v
+
+    g = golden("rotated")
+    R = g[f"R{D}"]
+    Rt = torch.from_numpy(R).cuda()
+    xb = g[f"{dt}_D{D}_x"]
+    x = from_bits(xb, dt)
+    xt = t_from_bits(xb, dt)
+    for kind, qf, dqf in (("k", rotated_quant_k, rotated_dequant_k), ("v", rotated_quant_v, rotated_dequant_v)):
+        p, s = qf(xt, Rt, bits=bits)
+        op, os_ = oq.rotated_quant(x, R, bits, kind, dt)
+        np.testing.assert_array_equal(p.cpu().numpy(), op)
+        np.testing.assert_array_equal(t_bits(s), to_bits(os_, dt))
+        deq = dqf(p, s, Rt, bits=bits, dtype=xt.dtype)
+        np.testing.assert_array_equal(t_bits(deq), to_bits(oq.rotated_dequant(op, os_, R, bits, dt), dt))
+        unpack = oq.unpack_int4 if bits == 4 else oq.unpack2
+        diff = np.abs(unpack(p.cpu().numpy()).astype(int) - unpack(g[f"{dt}_D{D}_b{bits}_{kind}_packed"]).astype(int))
+        assert diff.max() <= 1 and (diff != 0).mean() < 2e-3
+
+
+@pytest.mark.parametrize("dt", DTS)
+def test_rerope_golden(cuda_device, dt):
+    from fade_b200.rope_kernels import rerope_gather
+
+    g = golden("rope")
+    k = t_from_bits(g[f"{dt}_k"], dt)
+    keep = torch.from_numpy(g[f"{dt}_keep"]).cuda()
+    tabs = [torch.from_numpy(g[f"{dt}_{n}"]).cuda() for n in ("cos_old", "sin_old", "cos_new", "sin_new")]
+    v = torch.randn_like(k.float()).to(k.dtype)
+    ko, vo = rerope_gather(k, v, keep, *tabs)
+    np.testing.assert_array_equal(t_bits(ko), g[f"{dt}_out"])
+    assert torch.equal(vo, v.index_select(2, keep))
+
+
+@pytest.mark.parametrize("dt", DTS)
+def test_rerope_vs_oracle_large(cuda_device, dt):
+    from fade_b200.rope_kernels import rerope_gather
+
+    B, H, S, D = 2, 8, 4096, 128
+    x = seeded_outliers((B, H, S, D), seed=11, dt=dt)
+    rng = np.random.default_rng(1)
+    keep = np.sort(rng.choice(S, size=468, replace=False))
+    co, so = orope.vanilla_cos_sin(np.arange(S), D, 1e6, dt)
+    cn, sn = orope.vanilla_cos_sin(np.arange(468), D, 1e6, dt)
+    ref = orope.rerope_gather(x, keep, co, so, cn, sn, dt)
+    xt = np_to_dt_tensor(x, dt)
+    tabs = [torch.from_numpy(a).cuda() for a in (co, so, cn, sn)]
+    ko, _ = rerope_gather(xt, None, torch.from_numpy(keep).cuda(), *tabs)
+    np.testing.assert_array_equal(t_bits(ko), to_bits(ref, dt))
+
+
+@pytest.mark.parametrize("dt", DTS)
+def test_age_out_vs_oracle(cuda_device, dt):
+    from fade_b200.decoder import age_out_int4
+
+    B, H, D, R, cap = 3, 4, 128, 8, 40
+    rng = np.random.default_rng(7)
+    ring = seeded_outliers((B, H, R, D), seed=1, dt=dt)
+    ringv = seeded_outliers((B, H, R, D), seed=2, dt=dt)
+    ks = np.abs(seeded_outliers((B, H, 1, D), seed=3, dt=dt))[:, :, 0] / 7
+    ks = from_bits(to_bits(ks, dt), dt)
+    ks[0, 0, 3] = 0.0
+    new_k = seeded_outliers((B, H, 1, D), seed=4, dt=dt)[:, :, 0]
+    new_v = seeded_outliers((B, H, 1, D), seed=5, dt=dt)[:, :, 0]
+    n0 = np.array([5, 9, 0], dtype=np.int32)
+    origin = 2
+    rk, rv = np_to_dt_tensor(ring, dt), np_to_dt_tensor(ringv, dt)
+    kpk = torch.zeros(B, H, cap, D // 2, dtype=torch.uint8, device="cuda")
+    vpk = torch.zeros_like(kpk)
+    vsc = torch.zeros(B, H, cap, 1, dtype=rk.dtype, device="cuda")
+    mid_len = torch.from_numpy(n0.copy()).cuda()
+    age_out_int4(rk, rv, kpk, vpk, vsc, np_to_dt_tensor(ks, dt), mid_len, ring_origin=origin,
+                 k_new=np_to_dt_tensor(new_k, dt), v_new=np_to_dt_tensor(new_v, dt))
+    assert mid_len.cpu().tolist() == [6, 10, 1]
+    for b in range(B):
+        slot = (n0[b] - origin) % R
+        okp, ovp, ovs = oq.age_out_int4(ring[b, :, slot], ringv[b, :, slot], ks[b], dt)
+        np.testing.assert_array_equal(kpk[b, :, n0[b]].cpu().numpy(), okp)
+        np.testing.assert_array_equal(vpk[b, :, n0[b]].cpu().numpy(), ovp)
+        np.testing.assert_array_equal(t_bits(vsc[b, :, n0[b], 0]), to_bits(ovs, dt))
+        np.testing.assert_array_equal(t_vals(rk[b, :, slot]), new_k[b])
+        np.testing.assert_array_equal(t_vals(rv[b, :, slot]), new_v[b])
