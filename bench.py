@@ -72,7 +72,8 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, bus_ids):
-        self.bus_ids = {b.lower() for b in bus_ids}
+        # torch reports the PCI bus number as an int; nvidia-smi as "dddddddd:bb:dd.f"
+        self.bus_ids = {int(b) for b in bus_ids if b is not None}
         self.proc = None
         self.tmp = None
 
@@ -101,8 +102,11 @@ class ClockSampler:
             r = [x.strip() for x in r]
             if len(r) < 10:
                 continue
-            bus = r[1].lower()
-            if any(bus.endswith(b[-12:]) or b.endswith(bus[-12:]) for b in self.bus_ids):
+            try:
+                bus = int(r[1].split(":")[1], 16)
+            except (IndexError, ValueError):
+                continue
+            if bus in self.bus_ids:
                 mine.append(r)
         if not mine:
             mine = [[x.strip() for x in r] for r in rows if len(r) >= 10]
@@ -231,11 +235,11 @@ def run_fade(args, ws, rank, local):
 
     props = torch.cuda.get_device_properties(dev)
     bus = getattr(props, "pci_bus_id", None)
-    bus_ids = [bus] if bus else []
+    bus_ids = [bus] if bus is not None else []
     if ws > 1:
         gathered = [None] * ws
         dist.all_gather_object(gathered, bus)
-        bus_ids = [b for b in gathered if b]
+        bus_ids = [b for b in gathered if b is not None]
     sampler = ClockSampler(bus_ids) if rank == 0 else None
 
     # ---------------- timed region: K graph replays ----------------
@@ -339,7 +343,7 @@ def run_fade(args, ws, rank, local):
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": K, "warmup": W,
         "ms_per_step": round(step_ms, 4), "us_per_step": round(step_ms * 1e3, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4 codes x bf16 (f16 MMA, f32 accumulate)", "data": "synthetic", "config": config_block(ws),
+        "dtype": "int4 codes -> bf16 (bf16 MMA, f32 accumulate)", "data": "synthetic", "config": config_block(ws),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "fade_decode_attn (middle_kernel + tier0_merge_kernel) per layer",

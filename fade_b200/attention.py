@@ -192,8 +192,10 @@ class DecodePlan:
                 keep += _fill_mid(d.seg[n], t, D, dtype)
                 if isinstance(t, RotTier):
                     R = t.rotation
-                    if R.dtype != torch.float32 or not R.is_contiguous() or tuple(R.shape) != (D, D):
-                        raise ValueError("rotation must be a contiguous float32 [D, D] tensor")
+                    if tuple(R.shape) != (D, D):
+                        raise ValueError("rotation must be a [D, D] tensor")
+                    R = R.to(device=dev, dtype=torch.float32).contiguous()
+                    keep.append(R)
                     d.rotation = R.data_ptr()
             if Hkv is None:
                 Hkv = h

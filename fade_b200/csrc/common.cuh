@@ -86,9 +86,9 @@ __device__ __forceinline__ int code_from_float(float v) {
 // q = clamp(rint(x), lo, hi) with NaN -> 0; rintf rounds half to even like
 // torch.round.
 __device__ __forceinline__ int quant_code(float x, float lo, float hi) {
-    float r = rintf(x);
-    r = fminf(fmaxf(r, lo), hi);
-    return code_from_float(r);
+    const float r = rintf(x);
+    if (r != r) return 0;  // torch.clamp keeps NaN; NaN -> int8 gives 0
+    return (int)fminf(fmaxf(r, lo), hi);
 }
 
 // The reference's `qmax / absmax` is torch's __rtruediv__, i.e.

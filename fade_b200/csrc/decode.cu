@@ -132,103 +132,128 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
     asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
     return d;
 }
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-    __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&h);
-}
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 // ---------------------------------------------------------------------------
-// Code -> fp16 conversion.  u = code XOR sign bit is the offset-binary value;
-// (x & mask) ^ (0x6400 | sign-bits & mask) = fp16(1024 + u * 2^shift).
-// Subtracting (1024 + bias * 2^shift) leaves code * 2^shift exactly.
+// Model-dtype packed math (f16x2 / bf16x2) and the MMA in the model dtype.
 // ---------------------------------------------------------------------------
-struct Int4Conv {
-    // returns 4 half2: [0]=(n1,n5) x1, [1]=(n0,n4) x16, [2]=(n3,n7) x1, [3]=(n2,n6) x16
-    // where n_i are the nibbles in element order of the 4 bytes of x
-    // (byte j = (hi: element 2j, lo: element 2j+1)).
-    __device__ __forceinline__ static void conv(uint32_t x, uint32_t (&h)[4]) {
-        const uint32_t x8 = x >> 8;
-        h[0] = hadd2_u32(lop3_and_xor(x, 0x000F000Fu, 0x64086408u), 0xE408E408u);   // -1032
-        h[1] = hadd2_u32(lop3_and_xor(x, 0x00F000F0u, 0x64806480u), 0xE480E480u);   // -1152
-        h[2] = hadd2_u32(lop3_and_xor(x8, 0x000F000Fu, 0x64086408u), 0xE408E408u);
-        h[3] = hadd2_u32(lop3_and_xor(x8, 0x00F000F0u, 0x64806480u), 0xE480E480u);
+template <int DT> struct Pk;
+template <> struct Pk<FADE_F16> {
+    __device__ __forceinline__ static uint32_t sub(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+        __half2 h = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    __device__ __forceinline__ static float unpack_lo(uint32_t v) {
+        return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu)));
+    }
+    // magic exponent: (x & 0xF) ^ 0x6408 = fp16(1024 + u), u = nibble ^ 8 = code + 8
+    static constexpr uint32_t K4 = 0x64086408u, B4 = 0x64086408u;   // bias 1032
+    static constexpr uint32_t K2 = 0x64026402u, B2 = 0x64026402u;   // bias 1026
+    __device__ __forceinline__ static void mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
     }
 };
-struct Int2Conv {
-    // 8 half2 from 4 bytes; field f (0..3) of a byte sits at bit 6-2f.
-    // [0]=f3 x1, [1]=f2 x4, [2]=f1 x16, [3]=f0 x64 for bytes (0,2);
-    // [4..7] the same for bytes (1,3).
-    __device__ __forceinline__ static void conv(uint32_t x, uint32_t (&h)[8]) {
-        const uint32_t x8 = x >> 8;
-        h[0] = hadd2_u32(lop3_and_xor(x, 0x00030003u, 0x64026402u), 0xE402E402u);   // -1026
-        h[1] = hadd2_u32(lop3_and_xor(x, 0x000C000Cu, 0x64086408u), 0xE408E408u);   // -1032
-        h[2] = hadd2_u32(lop3_and_xor(x, 0x00300030u, 0x64206420u), 0xE420E420u);   // -1056
-        h[3] = hadd2_u32(lop3_and_xor(x, 0x00C000C0u, 0x64806480u), 0xE480E480u);   // -1152
-        h[4] = hadd2_u32(lop3_and_xor(x8, 0x00030003u, 0x64026402u), 0xE402E402u);
-        h[5] = hadd2_u32(lop3_and_xor(x8, 0x000C000Cu, 0x64086408u), 0xE408E408u);
-        h[6] = hadd2_u32(lop3_and_xor(x8, 0x00300030u, 0x64206420u), 0xE420E420u);
-        h[7] = hadd2_u32(lop3_and_xor(x8, 0x00C000C0u, 0x64806480u), 0xE480E480u);
+template <> struct Pk<FADE_BF16> {
+    __device__ __forceinline__ static uint32_t sub(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    __device__ __forceinline__ static float unpack_lo(uint32_t v) { return __uint_as_float(v << 16); }
+    // bf16(128 + u): exponent of 128, 7 mantissa bits hold u in 0..15
+    static constexpr uint32_t K4 = 0x43084308u, B4 = 0x43084308u;   // bias 136
+    static constexpr uint32_t K2 = 0x43024302u, B2 = 0x43024302u;   // bias 130
+    __device__ __forceinline__ static void mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
     }
 };
 
 // ---------------------------------------------------------------------------
-// Channel maps.  For a K operand (QK^T, B = q fragment) of thread lane
-// t = lane % 4, k-step ks, slot s in {0,1,2,3} = (b0, b1, b2, b3), kdim()
-// gives the channel and kfac() the power of two the converted code carries.
-// For the V operand (O^T rows), m-tile mi and row half hr (0: row gid,
-// 1: row gid+8) of thread gid = lane / 4, vdim()/vfac() likewise.
+// Code -> exact model-dtype integers ("LUT-free" magic-exponent conversion, as
+// in FasterTransformer's mixed-precision GEMMs): every field is shifted to the
+// low bits, (x & mask) ^ K forms the float 2^k + (code + bias) with the sign
+// bit of the two's-complement field flipped (offset binary), and one packed
+// subtraction of 2^k + bias leaves the code exactly.  The caller then
+// multiplies by the scale with one packed multiply, which rounds exactly like
+// the reference's `q.to(dtype) * scale.to(dtype)` (fade/quant.py:124-127).
+// ---------------------------------------------------------------------------
+template <int DT> struct Conv {
+    // INT4: bytes b0..b3 of x hold elements (2j: high nibble, 2j+1: low).
+    // h[0]=(e1,e5) h[1]=(e0,e4) h[2]=(e3,e7) h[3]=(e2,e6)
+    __device__ __forceinline__ static void int4(uint32_t x, uint32_t (&h)[4]) {
+        h[0] = Pk<DT>::sub(lop3_and_xor(x, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+        h[1] = Pk<DT>::sub(lop3_and_xor(x >> 4, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+        h[2] = Pk<DT>::sub(lop3_and_xor(x >> 8, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+        h[3] = Pk<DT>::sub(lop3_and_xor(x >> 12, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+    }
+    // 2-bit: field f of a byte sits at bit 6-2f.  h[0..3] = fields 3,2,1,0 of
+    // bytes (0,2); h[4..7] = fields 3,2,1,0 of bytes (1,3).
+    __device__ __forceinline__ static void int2(uint32_t x, uint32_t (&h)[8]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            h[i] = Pk<DT>::sub(lop3_and_xor(x >> (2 * i), 0x00030003u, Pk<DT>::K2), Pk<DT>::B2);
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Channel maps.  For the K operand, k-step ks and slot s in {0,1,2,3} (= the
+// A/B fragment k indices 2t, 2t+1, 2t+8, 2t+9) of thread t = lane % 4,
+// kdim() is the channel.  For the V operand (O^T rows), m-tile mi and row half
+// hr (0: row gid, 1: row gid+8), gid = lane / 4, vdim() is the channel.
+// The orders follow the conversion outputs above, so no data is shuffled.
 // ---------------------------------------------------------------------------
 template <int BITS> struct ChanMap;
 template <> struct ChanMap<4> {
     __device__ __forceinline__ static int kdim(int ks, int s, int t) {
         const int cb = ks >> 1, u = ks & 1;
-        // u=0: (n1,n5 | n0,n4), u=1: (n3,n7 | n2,n6)
         const int off[2][4] = {{1, 5, 0, 4}, {3, 7, 2, 6}};
         return 32 * cb + 8 * t + off[u][s];
     }
-    __device__ __forceinline__ static float kfac(int ks, int s) { return s >= 2 ? 16.f : 1.f; }
     __device__ __forceinline__ static int vdim(int mi, int hr, int gid) {
         const int cb = mi >> 1, j = mi & 1;
         return 32 * cb + 4 * gid + 2 * j + hr;
     }
-    __device__ __forceinline__ static float vfac(int mi, int hr) { return hr == 0 ? 16.f : 1.f; }
 };
 template <> struct ChanMap<2> {
     __device__ __forceinline__ static int kdim(int ks, int s, int t) {
         const int cb = ks >> 2, u = ks & 3;
-        // pairs M_{2u}, M_{2u+1}; M_i for bytes (0,2) (i<4) or (1,3) (i>=4)
         const int off[4][4] = {{3, 11, 2, 10}, {1, 9, 0, 8}, {7, 15, 6, 14}, {5, 13, 4, 12}};
         return 64 * cb + 16 * t + off[u][s];
-    }
-    __device__ __forceinline__ static float kfac(int ks, int s) {
-        const int u = ks & 3;
-        const float f[4][2] = {{1.f, 4.f}, {16.f, 64.f}, {1.f, 4.f}, {16.f, 64.f}};
-        return f[u][s >> 1];
     }
     __device__ __forceinline__ static int vdim(int mi, int hr, int gid) {
         const int cb = mi >> 2, j = mi & 3;
         return 64 * cb + 8 * gid + 2 * j + hr;
-    }
-    __device__ __forceinline__ static float vfac(int mi, int hr) {
-        const int j = mi & 3;
-        const float f[4][2] = {{64.f, 16.f}, {4.f, 1.f}, {64.f, 16.f}, {4.f, 1.f}};
-        return f[j][hr];
     }
 };
 
@@ -293,9 +318,9 @@ struct MidLayout {
     static constexpr int NCHV = RBV / 16;
     static constexpr int K_BYTES = kStageTokens * RBK;
     static constexpr int V_BYTES = kStageTokens * RBV;
-    // scale region: per-token (normalised) scales + per-slice max, or grouped
-    // scales for up to kStageTokens/16 groups.
-    static constexpr int SC_BYTES = VGROUP ? (kStageTokens / 16) * D * 4 : kStageTokens * 4 + 64;
+    // scale region: per-token V scales (raw dtype bits), or grouped V scales
+    // stored as duplicated pairs (s, s) for up to kStageTokens/16 groups.
+    static constexpr int SC_BYTES = VGROUP ? (kStageTokens / 16) * D * 4 : kStageTokens * 2;
     // [K0 V0 K1 V1 ...] (each region a multiple of 1024 B, so every TMA
     // destination keeps the 1024-B alignment the swizzle modes need), then
     // the per-stage scale regions.
@@ -320,19 +345,59 @@ template <int DT>
 __device__ __forceinline__ float load_f(const void* p, int64_t i) {
     return Elem<DT>::to_f(reinterpret_cast<const typename Elem<DT>::T*>(p)[i]);
 }
+template <int DT>
+__device__ __forceinline__ uint16_t load_bits(const void* p, int64_t i) {
+    return reinterpret_cast<const uint16_t*>(p)[i];
+}
+
+// Load the 2*NCH ldmatrix tiles (token block tb, 16-byte chunk cb) of one
+// 16-token m-tile: r[tb][cb].  TRANS selects the transposing form (V).
+template <int NCH, bool TRANS>
+__device__ __forceinline__ void load_tiles(uint32_t base, int trow0, int rb, uint32_t smask, int lane,
+                                           uint32_t (&r)[2][NCH]) {
+    constexpr int NMAT = 2 * NCH;
+    if constexpr (NMAT >= 4) {
+#pragma unroll
+        for (int x = 0; x < NMAT / 4; ++x) {
+            const int mi = x * 4 + lane / 8;
+            const int tb = mi / NCH, cb = mi % NCH;
+            const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * rb + cb * 16);
+            uint32_t r4[4];
+            if constexpr (TRANS) ldsm_x4_t(base + swz(off, smask), r4);
+            else ldsm_x4(base + swz(off, smask), r4);
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                const int mj = x * 4 + y;
+                r[mj / NCH][mj % NCH] = r4[y];
+            }
+        }
+    } else {
+        const int tb = (lane / 8) & 1;
+        const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * rb);
+        uint32_t r2[2];
+        if constexpr (TRANS) ldsm_x2_t(base + swz(off, smask), r2);
+        else ldsm_x2(base + swz(off, smask), r2);
+        r[0][0] = r2[0];
+        r[1][0] = r2[1];
+    }
+}
 
 // ---------------------------------------------------------------------------
 // k1: middle tier, persistent stream-K
+// QSPLIT: the query is fp32 (rotated tiers) and is fed to the MMA as a
+// hi + lo pair of model-dtype values (two MMAs per k-step).
 // ---------------------------------------------------------------------------
-template <int DT, int D, int KB, int VB, bool VGROUP, int NT>
+template <int DT, int D, int KB, int VB, bool VGROUP, int NT, bool QSPLIT>
 __global__ void __launch_bounds__(kMidThreads)
 middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
               MidParams p) {
     using L = MidLayout<D, KB, VB, VGROUP, NT>;
     using KMap = ChanMap<KB>;
     using VMap = ChanMap<VB>;
+    using P = Pk<DT>;
     constexpr int KSTEPS = D / 16;   // k-steps of the QK product
     constexpr int MT = D / 16;       // m-tiles of the PV product (rows = channels)
+    constexpr int NQ = QSPLIT ? 2 : 1;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -392,34 +457,26 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 tma_load_2d(smem_u32(st + L::K_OFF), &tmap_k, 0, (int)row0, full_bar(s), policy);
                 tma_load_2d(smem_u32(st + L::V_OFF), &tmap_v, 0, (int)row0, full_bar(s), policy);
             }
-            float* sc = reinterpret_cast<float*>(smem + L::SC_BASE + s * L::SC_BYTES);
             if constexpr (!VGROUP) {
-                // per-token scales, normalised by the max of each warp's 32-token slice
-                float v[4];
-                float mx = 0.f;
+                // per-token scales (raw dtype bits); 0 past the length
+                uint16_t* sc = reinterpret_cast<uint16_t*>(smem + L::SC_BASE + s * L::SC_BYTES);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int tt = lane * 4 + j;
-                    v[j] = (tok0 + tt < len) ? fabsf(load_f<DT>(p.v_scale, row0 + tt)) : 0.f;
-                    mx = fmaxf(mx, v[j]);
+                    sc[tt] = (tok0 + tt < len) ? load_bits<DT>(p.v_scale, row0 + tt) : (uint16_t)0;
                 }
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                const float inv = mx > 0.f ? 1.f / mx : 0.f;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) sc[lane * 4 + j] = v[j] * inv;
-                if ((lane & 7) == 0) sc[kStageTokens + lane / 8] = mx;
             } else {
                 // grouped scales: row r uses group r / G.  Stage rows start on a
                 // group boundary (G divides 128 and row bases are group aligned).
+                uint32_t* sc = reinterpret_cast<uint32_t*>(smem + L::SC_BASE + s * L::SC_BYTES);
                 const int G = p.group;
                 const int ngr = kStageTokens / G;
                 const int64_t g0 = row0 / G;
                 for (int e = lane; e < ngr * D; e += 32) {
                     const int gi = e / D, d = e % D;
                     const bool ok = tok0 + (int64_t)gi * G < len;
-                    sc[e] = ok ? load_f<DT>(p.v_scale, (g0 + gi) * D + d) : 0.f;
+                    const uint32_t b = ok ? load_bits<DT>(p.v_scale, (g0 + gi) * D + d) : 0u;
+                    sc[e] = b | (b << 16);
                 }
             }
             mbar_arrive(full_bar(s));
@@ -438,8 +495,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // ------------------------------ consumers ------------------------------
     const int gid = lane >> 2, t = lane & 3;
     const int ctid = threadIdx.x;  // 0..127
-    uint32_t qf[NT][KSTEPS][2];
-    float qn[NT][2];
+    uint32_t qf[NQ][NT][KSTEPS][2];  // B fragments (exact model-dtype query)
+    uint32_t ksc[KSTEPS][2];         // K scale pairs matching the A pairs
     float m_run[NT][2], l_run[NT][2];
     float o[NT][MT][4];
     int cur_z = -1;
@@ -447,45 +504,39 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 
     auto setup_z = [&](int z) {
         const int b = z / p.Hkv, h = z % p.Hkv;
-        const void* ksb = p.k_scale;
         const int64_t ks_off = (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
+#pragma unroll
+        for (int ks = 0; ks < KSTEPS; ++ks)
+#pragma unroll
+            for (int hs = 0; hs < 2; ++hs) {
+                const uint32_t lo = load_bits<DT>(p.k_scale, ks_off + KMap::kdim(ks, 2 * hs, t));
+                const uint32_t hi = load_bits<DT>(p.k_scale, ks_off + KMap::kdim(ks, 2 * hs + 1, t));
+                ksc[ks][hs] = lo | (hi << 16);
+            }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int r = nt * 8 + gid;
-            float prod[KSTEPS][4];
-            float amax = 0.f;
             const bool rv = r < p.rows;
             const int j = rv ? r / p.n_q : 0, sq = rv ? r % p.n_q : 0;
             const int64_t qoff = (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss;
 #pragma unroll
-            for (int ks = 0; ks < KSTEPS; ++ks) {
+            for (int ks = 0; ks < KSTEPS; ++ks)
 #pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const int d = KMap::kdim(ks, s, t);
-                    float qv = 0.f;
-                    if (rv) {
-                        qv = p.q_is_f32 ? reinterpret_cast<const float*>(p.q)[qoff + d]
-                                        : load_f<DT>(p.q, qoff + d);
+                for (int hs = 0; hs < 2; ++hs) {
+                    if constexpr (QSPLIT) {
+                        const float* qf32 = reinterpret_cast<const float*>(p.q);
+                        const float v0 = rv ? qf32[qoff + KMap::kdim(ks, 2 * hs, t)] : 0.f;
+                        const float v1 = rv ? qf32[qoff + KMap::kdim(ks, 2 * hs + 1, t)] : 0.f;
+                        const uint32_t hp = P::pack(v0, v1);
+                        const float h0 = P::unpack_lo(hp), h1 = P::unpack_lo(hp >> 16);
+                        qf[0][nt][ks][hs] = hp;
+                        qf[NQ - 1][nt][ks][hs] = P::pack(v0 - h0, v1 - h1);
+                    } else {
+                        const uint32_t lo = rv ? load_bits<DT>(p.q, qoff + KMap::kdim(ks, 2 * hs, t)) : 0u;
+                        const uint32_t hi = rv ? load_bits<DT>(p.q, qoff + KMap::kdim(ks, 2 * hs + 1, t)) : 0u;
+                        qf[0][nt][ks][hs] = lo | (hi << 16);
                     }
-                    const float v = qv * load_f<DT>(ksb, ks_off + d) * p.qk_scale;
-                    prod[ks][s] = v;
-                    amax = fmaxf(amax, fabsf(v));
                 }
-            }
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-            const float inv = amax > 0.f ? 1.f / amax : 0.f;
-#pragma unroll
-            for (int ks = 0; ks < KSTEPS; ++ks) {
-                qf[nt][ks][0] = pack_h2(prod[ks][0] * inv / KMap::kfac(ks, 0),
-                                        prod[ks][1] * inv / KMap::kfac(ks, 1));
-                qf[nt][ks][1] = pack_h2(prod[ks][2] * inv / KMap::kfac(ks, 2),
-                                        prod[ks][3] * inv / KMap::kfac(ks, 3));
-            }
-            // qn for the two score columns this thread owns (rows 2t, 2t+1 of
-            // the n-tile) is held by lanes gid = 2t, 2t+1.
-            qn[nt][0] = __shfl_sync(0xffffffffu, amax, (2 * t) * 4);
-            qn[nt][1] = __shfl_sync(0xffffffffu, amax, (2 * t + 1) * 4);
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -542,19 +593,18 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     for (int mi = 0; mi < MT; ++mi)
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const int hr = e >> 1;
-                            const int col = e & 1;
-                            const int r = nt * 8 + 2 * t + col;
-                            const int d = VMap::vdim(mi, hr, gid);
-                            const float v = o[nt][mi][e] * f[nt][col] / VMap::vfac(mi, hr);
+                            const int r = nt * 8 + 2 * t + (e & 1);
+                            const int d = VMap::vdim(mi, e >> 1, gid);
+                            const float v = o[nt][mi][e] * f[nt][e & 1];
                             if (pass == 0) obuf[r * D + d] = v; else obuf[r * D + d] += v;
                         }
             }
             named_bar_sync(1, kConsumerWarps * 32);
         }
-        // 3) write the CTA partial for z to its slot
+        // 3) write the CTA partial for z to its slot: the first unit of z this
+        //    CTA processed (unique per CTA, inside z's unit range)
         const int zb = units_begin(p, z);
-        const int slot = zb + (c - cta_of_unit(zb, C, U));
+        const int slot = zb > ub ? zb : ub;
         float* go = p.ws_o + (int64_t)slot * p.rows * D;
         for (int i = ctid; i < p.rows * D; i += kConsumerWarps * 32) go[i] = obuf[i];
         if (ctid < p.rows) {
@@ -575,6 +625,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     int zb = units_begin(p, z), ze = units_begin(p, z + 1);
     const uint32_t smask_k = (uint32_t)(L::NCHK - 1);
     const uint32_t smask_v = (uint32_t)(L::NCHV - 1);
+
     for (int u = ub, i = 0; u < ue; ++u, ++i) {
         while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
         if (z != cur_z) {
@@ -589,10 +640,10 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         const uint8_t* st = smem + s * L::STAGE_BYTES;
         const uint32_t kbase = smem_u32(st + L::K_OFF);
         const uint32_t vbase = smem_u32(st + L::V_OFF);
-        const float* sc = reinterpret_cast<const float*>(smem + L::SC_BASE + s * L::SC_BYTES);
+        const uint8_t* scb = smem + L::SC_BASE + s * L::SC_BYTES;
 
         if (ready && tok_w < cur_len) {
-            // ---- S^T = K . q^T for the warp's 2 m-tiles ----
+            // ---- S^T = K_deq . q^T for the warp's 2 m-tiles ----
             float sacc[2][NT][4];
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
@@ -600,58 +651,43 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = 0.f;
-                const int trow0 = warp * 32 + mt * 16;  // tile row within the stage
-                // matrices (tb, cb) -> regs kr[tb][cb]
                 uint32_t kr[2][L::NCHK];
-                constexpr int NMAT = 2 * L::NCHK;
-                if constexpr (NMAT >= 4) {
-#pragma unroll
-                    for (int x = 0; x < NMAT / 4; ++x) {
-                        const int mi = x * 4 + lane / 8;
-                        const int tb = mi / L::NCHK, cb = mi % L::NCHK;
-                        const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * L::RBK + cb * 16);
-                        uint32_t r4[4];
-                        ldsm_x4(kbase + swz(off, smask_k), r4);
-#pragma unroll
-                        for (int y = 0; y < 4; ++y) {
-                            const int mj = x * 4 + y;
-                            kr[mj / L::NCHK][mj % L::NCHK] = r4[y];
-                        }
-                    }
-                } else {
-                    const int mi = (lane / 8) & 1;
-                    const int tb = mi / L::NCHK, cb = mi % L::NCHK;
-                    const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * L::RBK + cb * 16);
-                    uint32_t r2[2];
-                    ldsm_x2(kbase + swz(off, smask_k), r2);
-                    kr[0][0] = r2[0];
-                    kr[1][0] = r2[1];
-                }
+                load_tiles<L::NCHK, false>(kbase, warp * 32 + mt * 16, L::RBK, smask_k, lane, kr);
 #pragma unroll
                 for (int cb = 0; cb < L::NCHK; ++cb) {
                     if constexpr (KB == 4) {
                         uint32_t h0[4], h1[4];
-                        Int4Conv::conv(kr[0][cb], h0);
-                        Int4Conv::conv(kr[1][cb], h1);
+                        Conv<DT>::int4(kr[0][cb], h0);
+                        Conv<DT>::int4(kr[1][cb], h1);
 #pragma unroll
                         for (int u2 = 0; u2 < 2; ++u2) {
                             const int ks = cb * 2 + u2;
+                            const uint32_t a0 = P::mul(h0[2 * u2], ksc[ks][0]);
+                            const uint32_t a1 = P::mul(h1[2 * u2], ksc[ks][0]);
+                            const uint32_t a2 = P::mul(h0[2 * u2 + 1], ksc[ks][1]);
+                            const uint32_t a3 = P::mul(h1[2 * u2 + 1], ksc[ks][1]);
 #pragma unroll
-                            for (int nt = 0; nt < NT; ++nt)
-                                mma16816(sacc[mt][nt], h0[2 * u2], h1[2 * u2], h0[2 * u2 + 1],
-                                         h1[2 * u2 + 1], qf[nt][ks][0], qf[nt][ks][1]);
+                            for (int qs = 0; qs < NQ; ++qs)
+#pragma unroll
+                                for (int nt = 0; nt < NT; ++nt)
+                                    P::mma(sacc[mt][nt], a0, a1, a2, a3, qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     } else {
                         uint32_t h0[8], h1[8];
-                        Int2Conv::conv(kr[0][cb], h0);
-                        Int2Conv::conv(kr[1][cb], h1);
+                        Conv<DT>::int2(kr[0][cb], h0);
+                        Conv<DT>::int2(kr[1][cb], h1);
 #pragma unroll
                         for (int u4 = 0; u4 < 4; ++u4) {
                             const int ks = cb * 4 + u4;
+                            const uint32_t a0 = P::mul(h0[2 * u4], ksc[ks][0]);
+                            const uint32_t a1 = P::mul(h1[2 * u4], ksc[ks][0]);
+                            const uint32_t a2 = P::mul(h0[2 * u4 + 1], ksc[ks][1]);
+                            const uint32_t a3 = P::mul(h1[2 * u4 + 1], ksc[ks][1]);
 #pragma unroll
-                            for (int nt = 0; nt < NT; ++nt)
-                                mma16816(sacc[mt][nt], h0[2 * u4], h1[2 * u4], h0[2 * u4 + 1],
-                                         h1[2 * u4 + 1], qf[nt][ks][0], qf[nt][ks][1]);
+                            for (int qs = 0; qs < NQ; ++qs)
+#pragma unroll
+                                for (int nt = 0; nt < NT; ++nt)
+                                    P::mma(sacc[mt][nt], a0, a1, a2, a3, qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     }
                 }
@@ -666,7 +702,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int tok = (int)tok_w + mt * 16 + gid + ((e >> 1) << 3);
-                        float v = sacc[mt][nt][e] * qn[nt][e & 1];
+                        float v = sacc[mt][nt][e] * p.qk_scale;
                         if (tok >= cur_len) v = -INFINITY;
                         sacc[mt][nt][e] = v;
                         mx[e & 1] = fmaxf(mx[e & 1], v);
@@ -696,105 +732,80 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         l_run[nt][e & 1] += pe;
                         pv[e] = pe;
                     }
-                    if constexpr (!VGROUP) {
-                        const int tr = warp * 32 + mt * 16 + gid;
-                        const float s0 = sc[tr], s1 = sc[tr + 8];
-                        pv[0] *= s0; pv[1] *= s0; pv[2] *= s1; pv[3] *= s1;
-                    }
-                    pb[mt][nt][0] = movmatrix_t(pack_h2(pv[0], pv[1]));
-                    pb[mt][nt][1] = movmatrix_t(pack_h2(pv[2], pv[3]));
+                    pb[mt][nt][0] = movmatrix_t(P::pack(pv[0], pv[1]));
+                    pb[mt][nt][1] = movmatrix_t(P::pack(pv[2], pv[3]));
                 }
             }
-            // ---- O^T += V^T . P^T ----
-            float vmul = 1.f;
-            if constexpr (!VGROUP) vmul = sc[kStageTokens + warp];
+            // ---- O^T += V_deq^T . P^T ----
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
                 const int trow0 = warp * 32 + mt * 16;
                 uint32_t vr[2][L::NCHV];
-                constexpr int NMAT = 2 * L::NCHV;
-                if constexpr (NMAT >= 4) {
-#pragma unroll
-                    for (int x = 0; x < NMAT / 4; ++x) {
-                        const int mi = x * 4 + lane / 8;
-                        const int tb = mi / L::NCHV, cb = mi % L::NCHV;
-                        const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * L::RBV + cb * 16);
-                        uint32_t r4[4];
-                        ldsm_x4_t(vbase + swz(off, smask_v), r4);
-#pragma unroll
-                        for (int y = 0; y < 4; ++y) {
-                            const int mj = x * 4 + y;
-                            vr[mj / L::NCHV][mj % L::NCHV] = r4[y];
-                        }
-                    }
+                load_tiles<L::NCHV, true>(vbase, trow0, L::RBV, smask_v, lane, vr);
+                uint32_t vs0 = 0, vs1 = 0;
+                const uint32_t* gsc = nullptr;
+                if constexpr (!VGROUP) {
+                    const uint32_t* sc32 = reinterpret_cast<const uint32_t*>(scb);
+                    vs0 = sc32[(trow0 + 2 * t) >> 1];       // tokens 2t, 2t+1
+                    vs1 = sc32[(trow0 + 8 + 2 * t) >> 1];   // tokens 8+2t, 9+2t
                 } else {
-                    const int mi = (lane / 8) & 1;
-                    const int tb = mi / L::NCHV, cb = mi % L::NCHV;
-                    const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * L::RBV + cb * 16);
-                    uint32_t r2[2];
-                    ldsm_x2_t(vbase + swz(off, smask_v), r2);
-                    vr[0][0] = r2[0];
-                    vr[1][0] = r2[1];
+                    gsc = reinterpret_cast<const uint32_t*>(scb) + (trow0 / p.group) * D;
                 }
-                float tacc[NT][MT][4];
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int mi = 0; mi < MT; ++mi)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) tacc[nt][mi][e] = 0.f;
 #pragma unroll
                 for (int cb = 0; cb < L::NCHV; ++cb) {
                     if constexpr (VB == 4) {
                         uint32_t h0[4], h1[4];
-                        Int4Conv::conv(vr[0][cb], h0);   // tokens 2t,2t+1
-                        Int4Conv::conv(vr[1][cb], h1);   // tokens 8+2t, 9+2t
-                        // m-tile j=0: rows (gid: n0 x16 -> h[1]), (gid+8: n1 -> h[0])
-                        // m-tile j=1: rows (gid: n2 x16 -> h[3]), (gid+8: n3 -> h[2])
+                        Conv<DT>::int4(vr[0][cb], h0);   // tokens 2t,2t+1
+                        Conv<DT>::int4(vr[1][cb], h1);   // tokens 8+2t, 9+2t
+                        // m-tile j: rows (gid: e_{2j} -> h[2j+1]), (gid+8: e_{2j+1} -> h[2j])
 #pragma unroll
                         for (int j = 0; j < 2; ++j) {
                             const int mi = cb * 2 + j;
+                            uint32_t a0, a1, a2, a3;
+                            if constexpr (!VGROUP) {
+                                a0 = P::mul(h0[2 * j + 1], vs0);
+                                a1 = P::mul(h0[2 * j], vs0);
+                                a2 = P::mul(h1[2 * j + 1], vs1);
+                                a3 = P::mul(h1[2 * j], vs1);
+                            } else {
+                                const uint32_t g0 = gsc[VMap::vdim(mi, 0, gid)], g1 = gsc[VMap::vdim(mi, 1, gid)];
+                                a0 = P::mul(h0[2 * j + 1], g0);
+                                a1 = P::mul(h0[2 * j], g1);
+                                a2 = P::mul(h1[2 * j + 1], g0);
+                                a3 = P::mul(h1[2 * j], g1);
+                            }
 #pragma unroll
                             for (int nt = 0; nt < NT; ++nt)
-                                mma16816(tacc[nt][mi], h0[2 * j + 1], h0[2 * j], h1[2 * j + 1], h1[2 * j],
-                                         pb[mt][nt][0], pb[mt][nt][1]);
+                                P::mma(o[nt][mi], a0, a1, a2, a3, pb[mt][nt][0], pb[mt][nt][1]);
                         }
                     } else {
                         uint32_t h0[8], h1[8];
-                        Int2Conv::conv(vr[0][cb], h0);
-                        Int2Conv::conv(vr[1][cb], h1);
-                        // 8 channels: +0 (h[3],x64) +1 (h[2],x16) +2 (h[1],x4) +3 (h[0],x1)
-                        //             +4 (h[7],x64) +5 (h[6],x16) +6 (h[5],x4) +7 (h[4],x1)
+                        Conv<DT>::int2(vr[0][cb], h0);
+                        Conv<DT>::int2(vr[1][cb], h1);
+                        // channels +0 h[3], +1 h[2], +2 h[1], +3 h[0], +4 h[7], +5 h[6], +6 h[5], +7 h[4]
                         const int lo[4] = {3, 1, 7, 5};
                         const int hi[4] = {2, 0, 6, 4};
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             const int mi = cb * 4 + j;
+                            uint32_t a0, a1, a2, a3;
+                            if constexpr (!VGROUP) {
+                                a0 = P::mul(h0[lo[j]], vs0);
+                                a1 = P::mul(h0[hi[j]], vs0);
+                                a2 = P::mul(h1[lo[j]], vs1);
+                                a3 = P::mul(h1[hi[j]], vs1);
+                            } else {
+                                const uint32_t g0 = gsc[VMap::vdim(mi, 0, gid)], g1 = gsc[VMap::vdim(mi, 1, gid)];
+                                a0 = P::mul(h0[lo[j]], g0);
+                                a1 = P::mul(h0[hi[j]], g1);
+                                a2 = P::mul(h1[lo[j]], g0);
+                                a3 = P::mul(h1[hi[j]], g1);
+                            }
 #pragma unroll
                             for (int nt = 0; nt < NT; ++nt)
-                                mma16816(tacc[nt][mi], h0[lo[j]], h0[hi[j]], h1[lo[j]], h1[hi[j]],
-                                         pb[mt][nt][0], pb[mt][nt][1]);
+                                P::mma(o[nt][mi], a0, a1, a2, a3, pb[mt][nt][0], pb[mt][nt][1]);
                         }
                     }
-                }
-                if constexpr (VGROUP) {
-                    // grouped scales: channel d of this m-tile's group
-                    const int gi = (trow0) / p.group;
-                    const float* gs = sc + gi * D;
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int mi = 0; mi < MT; ++mi)
-#pragma unroll
-                            for (int e = 0; e < 4; ++e)
-                                o[nt][mi][e] += tacc[nt][mi][e] * gs[VMap::vdim(mi, e >> 1, gid)];
-                } else {
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int mi = 0; mi < MT; ++mi)
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) o[nt][mi][e] += tacc[nt][mi][e] * vmul;
                 }
             }
         }
@@ -991,19 +1002,15 @@ tier0_merge_kernel(Tier0Params p) {
         const int U = p.cu_units ? p.cu_units[Z] : Z * p.units_per_z;
         const int zb = p.cu_units ? p.cu_units[z] : z * p.units_per_z;
         const int ze = p.cu_units ? p.cu_units[z + 1] : (z + 1) * p.units_per_z;
-        int nslots = 0;
-        if (ze > zb) {
-            const int c0 = cta_of_unit(zb, p.n_ctas, U);
-            const int c1 = cta_of_unit(ze - 1, p.n_ctas, U);
-            nslots = c1 - c0 + 1;
-        }
-        // A CTA inside [c0, c1] owns units of z unless its whole unit range is
-        // empty (possible when the grid is larger than the unit count); empty
-        // CTAs wrote no partial, so their slots are skipped.
-        const int c0 = (ze > zb) ? cta_of_unit(zb, p.n_ctas, U) : 0;
+        // A k1 CTA stores its partial for z at the first unit of z it
+        // processed.  Unit zb+s2 holds a partial iff it is z's first unit or
+        // its owning CTA's range starts there.
+        const int nslots = ze - zb;
         auto slot_live = [&](int s2) {
-            const int c = c0 + s2;
-            return (int64_t)c * U / p.n_ctas < (int64_t)(c + 1) * U / p.n_ctas;
+            const int u = zb + s2;
+            if (s2 == 0) return true;
+            const int owner = cta_of_unit(u, p.n_ctas, U);
+            return (int)((int64_t)owner * U / p.n_ctas) == u;
         };
         // Per row: global max / sum over the FP part and every slot.
         __shared__ float mid_w[64][ROWS];  // weight per slot (nslots <= 64 handled in chunks)
@@ -1132,7 +1139,7 @@ struct MidKernelInfo {
 // Function attributes are per device: configure each (kernel, device) once.
 constexpr int kMaxDevices = 64;
 
-template <int DT, int D, int KB, int VB, bool VG, int NT>
+template <int DT, int D, int KB, int VB, bool VG, int NT, bool QS>
 static MidKernelInfo mid_info() {
     static MidKernelInfo info[kMaxDevices] = {};
     static std::mutex mu;
@@ -1143,29 +1150,30 @@ static MidKernelInfo mid_info() {
     MidKernelInfo& i = info[dev];
     if (!i.fn) {
         i.smem = MidLayout<D, KB, VB, VG, NT>::SMEM_BYTES;
-        cudaFuncSetAttribute(&middle_kernel<DT, D, KB, VB, VG, NT>,
+        cudaFuncSetAttribute(&middle_kernel<DT, D, KB, VB, VG, NT, QS>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, i.smem);
         int occ = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, &middle_kernel<DT, D, KB, VB, VG, NT>,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, &middle_kernel<DT, D, KB, VB, VG, NT, QS>,
                                                       kMidThreads, i.smem);
         i.occ = occ > 0 ? occ : 1;
-        i.fn = reinterpret_cast<void*>(&middle_kernel<DT, D, KB, VB, VG, NT>);
+        i.fn = reinterpret_cast<void*>(&middle_kernel<DT, D, KB, VB, VG, NT, QS>);
     }
     return i;
 }
 
 template <int DT, int D, int NT>
-static MidKernelInfo select_mid(int kb, int vb, bool vg) {
-    if (kb == 4 && vb == 4 && !vg) return mid_info<DT, D, 4, 4, false, NT>();
-    if (kb == 4 && vb == 2 && vg) return mid_info<DT, D, 4, 2, true, NT>();
-    if (kb == 2 && vb == 2 && !vg) return mid_info<DT, D, 2, 2, false, NT>();
+static MidKernelInfo select_mid(int kb, int vb, bool vg, bool rot) {
+    if (!rot && kb == 4 && vb == 4 && !vg) return mid_info<DT, D, 4, 4, false, NT, false>();
+    if (!rot && kb == 4 && vb == 2 && vg) return mid_info<DT, D, 4, 2, true, NT, false>();
+    if (rot && kb == 4 && vb == 4 && !vg) return mid_info<DT, D, 4, 4, false, NT, true>();
+    if (rot && kb == 2 && vb == 2 && !vg) return mid_info<DT, D, 2, 2, false, NT, true>();
     return MidKernelInfo{nullptr, 0, 0};
 }
 
 template <int DT>
-static MidKernelInfo select_mid_d(int D, int NT, int kb, int vb, bool vg) {
-    if (D == 128) return NT == 1 ? select_mid<DT, 128, 1>(kb, vb, vg) : select_mid<DT, 128, 2>(kb, vb, vg);
-    if (D == 64) return NT == 1 ? select_mid<DT, 64, 1>(kb, vb, vg) : select_mid<DT, 64, 2>(kb, vb, vg);
+static MidKernelInfo select_mid_d(int D, int NT, int kb, int vb, bool vg, bool rot) {
+    if (D == 128) return NT == 1 ? select_mid<DT, 128, 1>(kb, vb, vg, rot) : select_mid<DT, 128, 2>(kb, vb, vg, rot);
+    if (D == 64) return NT == 1 ? select_mid<DT, 64, 1>(kb, vb, vg, rot) : select_mid<DT, 64, 2>(kb, vb, vg, rot);
     return MidKernelInfo{nullptr, 0, 0};
 }
 
@@ -1232,8 +1240,9 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
         pl->units_per_z = (int)upz;
         pl->max_units = upz * Z;
         int dt = d->dtype;
-        pl->mk = dt == FADE_F16 ? select_mid_d<FADE_F16>(d->D, pl->NT, pl->kb, pl->vb, pl->vg)
-                                : select_mid_d<FADE_BF16>(d->D, pl->NT, pl->kb, pl->vb, pl->vg);
+        const bool rot = s.kind == FADE_SEG_ROT;
+        pl->mk = dt == FADE_F16 ? select_mid_d<FADE_F16>(d->D, pl->NT, pl->kb, pl->vb, pl->vg, rot)
+                                : select_mid_d<FADE_BF16>(d->D, pl->NT, pl->kb, pl->vb, pl->vg, rot);
         if (!pl->mk.fn) return FADE_ERR_UNSUPPORTED;
         int C = d->n_ctas > 0 ? d->n_ctas : sm_count() * pl->mk.occ;
         if (!d->cu_units && pl->max_units < C) C = (int)pl->max_units;

@@ -47,3 +47,28 @@ def seeded_outliers(shape, seed: int, dt: str, n_out=4, mult=8.0) -> np.ndarray:
         ch = rng.permutation(D)[:n_out]
         x[:, h, :, ch] *= mult
     return from_bits(to_bits(x, dt), dt) if dt != "f32" else x
+
+
+def dtype_ulp(x: np.ndarray, dt: str) -> np.ndarray:
+    """Spacing of the dtype's representable values at |x|."""
+    mb = {"f16": 10, "bf16": 7, "f32": 23}[dt]
+    tiny = {"f16": 2.0 ** -24, "bf16": 2.0 ** -133, "f32": 2.0 ** -149}[dt]
+    a = np.abs(np.asarray(x, dtype=np.float64))
+    e = np.floor(np.log2(np.maximum(a, 1e-300)))
+    return np.maximum(2.0 ** (e - mb), tiny)
+
+
+def assert_attn_close(out: np.ndarray, ref: np.ndarray, dt: str, atol: float) -> float:
+    """Attention parity criterion: |out - ref| <= max(atol, 1 ulp of the output
+    dtype at |ref|) element-wise.  atol is the north-star tolerance (2e-3 fp16,
+    1e-2 bf16); the ulp term is the unavoidable rounding of a result stored in
+    the dtype (two correctly computed outputs can land one ulp apart when the
+    exact value is near a rounding boundary, which exceeds atol once |ref| >= 4
+    in fp16 or >= 2 in bf16).  Returns the worst err / limit."""
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    lim = np.maximum(atol, dtype_ulp(ref, dt))
+    ratio = np.abs(out - ref) / lim
+    worst = float(ratio.max()) if ratio.size else 0.0
+    assert worst <= 1.0, f"max |out-ref| {np.abs(out - ref).max():.3e}, worst err/limit {worst:.3f}"
+    return worst

@@ -8,13 +8,13 @@ import pytest
 import torch
 
 from conftest import golden
-from gpu_util import np_to_dt_tensor, seeded_outliers, t_from_bits, t_vals
+from gpu_util import assert_attn_close, np_to_dt_tensor, seeded_outliers, t_from_bits, t_vals
 from oracle import attention as oa
 from oracle import quant as oq
 from oracle.numerics import from_bits
 
 pytestmark = pytest.mark.gpu
-TOL = {"f16": 2e-3, "bf16": 1e-2}
+TOL = {"f16": 2e-3, "bf16": 1e-2}   # north-star max-abs tolerances (see assert_attn_close)
 
 
 def _fp(g, name, dt):
@@ -37,8 +37,8 @@ def test_cfg1_golden(cuda_device):
     out = t_vals(tiered_decode_attention(q, tiers))
     ref = from_bits(g["out_ref"], dt)
     ref32 = g["out_ref32"].view(np.float32)
-    assert np.abs(out - ref).max() < TOL[dt]
-    assert np.abs(out - ref32).max() < TOL[dt]
+    assert_attn_close(out, ref, dt, TOL[dt])
+    assert_attn_close(out, ref32, dt, TOL[dt])
 
 
 def test_cfg3_small_golden(cuda_device):
@@ -61,8 +61,8 @@ def test_cfg3_small_golden(cuda_device):
         FPTier(_fp(g, "recent_k", dt), _fp(g, "recent_v", dt)),
     ]
     out = t_vals(tiered_decode_attention(q, tiers))
-    assert np.abs(out - from_bits(g["out_ref"], dt)).max() < TOL[dt]
-    assert np.abs(out - g["out_ref32"].view(np.float32)).max() < TOL[dt]
+    assert_attn_close(out, from_bits(g["out_ref"], dt), dt, TOL[dt])
+    assert_attn_close(out, g["out_ref32"].view(np.float32), dt, TOL[dt])
 
 
 def test_rot2_golden(cuda_device):
@@ -80,8 +80,8 @@ def test_rot2_golden(cuda_device):
         FPTier(_fp(g, "recent_k", dt), _fp(g, "recent_v", dt)),
     ]
     out = t_vals(tiered_decode_attention(q, tiers))
-    assert np.abs(out - from_bits(g["out_ref"], dt)).max() < TOL[dt]
-    assert np.abs(out - g["out_ref32"].view(np.float32)).max() < TOL[dt]
+    assert_attn_close(out, from_bits(g["out_ref"], dt), dt, TOL[dt])
+    assert_attn_close(out, g["out_ref32"].view(np.float32), dt, TOL[dt])
 
 
 def _random_int4_case(B, Hq, Hkv, D, n_sink, n_mid, n_rec, dt, seed, n_q=1):
@@ -90,8 +90,12 @@ def _random_int4_case(B, Hq, Hkv, D, n_sink, n_mid, n_rec, dt, seed, n_q=1):
     rng = np.random.default_rng(seed + 2)
     q = from_bits_dt(rng.standard_normal((B, Hq, n_q, D)).astype(np.float32), dt)
     mk, mv = x[:, :, n_sink:n_sink + n_mid], v[:, :, n_sink:n_sink + n_mid]
-    kp, ks = oq.quant_k_int4(mk, dt)
-    vp, vs = oq.quant_v_int4(mv, dt)
+    if n_mid:
+        kp, ks = oq.quant_k_int4(mk, dt)
+        vp, vs = oq.quant_v_int4(mv, dt)
+    else:
+        kp = vp = np.zeros((B, Hkv, 0, D // 2), np.uint8)
+        ks, vs = np.zeros((B, Hkv, 1, D), np.float32), np.zeros((B, Hkv, 0, 1), np.float32)
     tiers = {"sink_k": x[:, :, :n_sink], "sink_v": v[:, :, :n_sink],
              "int4_kq": kp, "int4_ks": ks, "int4_vq": vp, "int4_vs": vs,
              "recent_k": x[:, :, n_sink + n_mid:], "recent_v": v[:, :, n_sink + n_mid:]}
@@ -137,8 +141,7 @@ def test_random_vs_oracle(cuda_device, B, Hq, Hkv, D, n_sink, n_mid, n_rec, dt, 
     q, tiers = _random_int4_case(B, Hq, Hkv, D, n_sink, n_mid, n_rec, dt, seed=B * 1000 + n_mid, n_q=n_q)
     ref = oa.tiered_attention(q, tiers, dt)
     out = t_vals(tiered_decode_attention(np_to_dt_tensor(q, dt), _torch_tiers(tiers, dt)))
-    err = np.abs(out - ref).max()
-    assert err < TOL[dt], err
+    assert_attn_close(out, ref, dt, TOL[dt])
 
 
 def test_forced_cta_counts_agree(cuda_device):
@@ -151,7 +154,7 @@ def test_forced_cta_counts_agree(cuda_device):
     ref = oa.tiered_attention(q, tiers, "bf16")
     for n in (1, 7, 64, 300, 2000):
         out = t_vals(tiered_decode_attention(qt, tt, n_ctas=n))
-        assert np.abs(out - ref).max() < TOL["bf16"], n
+        assert_attn_close(out, ref, "bf16", TOL["bf16"])
 
 
 def test_device_lengths_and_ragged(cuda_device):
@@ -192,7 +195,7 @@ def test_device_lengths_and_ragged(cuda_device):
             t = {"sink_k": sink[b:b + 1], "sink_v": sink[b:b + 1], "int4_kq": kp[b:b + 1, :, :n],
                  "int4_ks": ks[b:b + 1], "int4_vq": vp[b:b + 1, :, :n], "int4_vs": vs[b:b + 1, :, :n]}
             ref = oa.tiered_attention(q[b:b + 1], t, dt)
-            assert np.abs(out[b:b + 1] - ref).max() < TOL[dt], (use_cu, b)
+            assert_attn_close(out[b:b + 1], ref, dt, TOL[dt])
 
 
 def test_repeat_calls_are_stable(cuda_device):
@@ -250,5 +253,5 @@ def test_decoder_step_matches_oracle(cuda_device):
             tiers = {"sink_k": s["sink_k"], "sink_v": s["sink_v"], "int4_kq": s["mid_kq"], "int4_ks": s["mid_ks"],
                      "int4_vq": s["mid_vq"], "int4_vs": s["mid_vs"], "recent_k": s["ring_k"], "recent_v": s["ring_v"]}
             ref = oa.tiered_attention(q[l], tiers, dt)
-            assert np.abs(out[l] - ref).max() < TOL[dt], (step, l)
+            assert_attn_close(out[l], ref, dt, TOL[dt])
     assert dec.mid_lengths() == [S - 68 + 4] * L
