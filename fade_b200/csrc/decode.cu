@@ -8,11 +8,14 @@
 // merged: the token order of the reference's cat() does not matter.
 //
 // Launch sequence (one stream, chained with programmatic dependent launch):
-//   k0  rotate_queries      (only with a rotated tier): q_rot = q @ R^T, fp32.
-//   k1  middle_kernel       persistent stream-K over the quantised middle tier.
-//   k2  tier0_merge_kernel  one CTA per (b, kv-head): attention over the FP
-//                           sink/recent tiers, then (after griddepcontrol.wait)
-//                           merges k1's split-K partials and writes `out`.
+//   k0  rotate_queries   (only with a rotated tier): q_rot = q @ R^T, fp32.
+//   kf  fp_tier_kernel   one CTA per (b, kv-head): attention over the FP
+//                        sink/recent tiers -> an un-normalised partial (or the
+//                        final output when there is no quantised middle).
+//   k1  middle_kernel    persistent stream-K over the quantised middle; every
+//                        CTA writes one partial per (b, kv-head) it touched and
+//                        counts its arrival; the CTA that completes a row merges
+//                        the FP partial with all middle partials and writes `out`.
 //
 // k1 data path per CTA (5 warps):
 //   warp 4 (producer): 2-D TMA (cp.async.bulk.tensor, no multicast) of 128
@@ -33,6 +36,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -43,7 +47,7 @@ constexpr int kConsumerWarps = 4;
 constexpr int kMidThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
 constexpr int kStages = 4;
-constexpr int kTier0Threads = 128;
+constexpr int kFpThreads = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polling
 
@@ -97,6 +101,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
         " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_1d(uint32_t dst, const CUtensorMap* map, int x, uint32_t bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.1d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2}], [%3], %4;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(bar), "l"(policy)
         : "memory");
 }
 __device__ __forceinline__ uint64_t evict_first_policy() {
@@ -281,6 +293,14 @@ struct MidParams {
     float* ws_ml;                   // [U][rows][2]
     float* ws_o;                    // [U][rows][D]
     int* ws_err;
+    int* counters;                  // [Z] arrivals per row (zeroed by fp_tier_kernel)
+    int scale_tma;                  // V scales arrive by TMA (row starts 8-aligned)
+    int q_vec;                      // q / k_scale rows allow 16-byte loads
+    const float* fp_ml;             // FP-tier partial [Z][rows][2] or null
+    const float* fp_o;              // [Z][rows][D]
+    void* out;                      // [B,Hq,n_q,D] model dtype
+    int64_t o_sb, o_sh, o_ss;
+    const float* rotation;          // rotated middle: out = fp + mid @ R
 };
 
 __device__ __forceinline__ int64_t seg_len(const MidParams& p, int b) {
@@ -318,9 +338,13 @@ struct MidLayout {
     static constexpr int NCHV = RBV / 16;
     static constexpr int K_BYTES = kStageTokens * RBK;
     static constexpr int V_BYTES = kStageTokens * RBV;
-    // scale region: per-token V scales (raw dtype bits), or grouped V scales
-    // stored as duplicated pairs (s, s) for up to kStageTokens/16 groups.
-    static constexpr int SC_BYTES = VGROUP ? (kStageTokens / 16) * D * 4 : kStageTokens * 2;
+    // scale region: per-token V scales or grouped V scales [groups][D], raw
+    // dtype bits, for up to kStageTokens/16 groups.
+    static constexpr int SC_BYTES = VGROUP ? (kStageTokens / 16) * D * 2 : kStageTokens * 2;
+    // bytes the scale TMA box of one stage carries (grouped: kStageTokens/G groups)
+    __host__ __device__ static constexpr int sc_box_bytes(int group) {
+        return VGROUP ? (kStageTokens / group) * D * 2 : kStageTokens * 2;
+    }
     // [K0 V0 K1 V1 ...] (each region a multiple of 1024 B, so every TMA
     // destination keeps the 1024-B alignment the swizzle modes need), then
     // the per-stage scale regions.
@@ -349,6 +373,8 @@ template <int DT>
 __device__ __forceinline__ uint16_t load_bits(const void* p, int64_t i) {
     return reinterpret_cast<const uint16_t*>(p)[i];
 }
+
+__device__ __forceinline__ uint32_t dup16(uint16_t v) { return (uint32_t)v | ((uint32_t)v << 16); }
 
 // Load the 2*NCH ldmatrix tiles (token block tb, 16-byte chunk cb) of one
 // 16-token m-tile: r[tb][cb].  TRANS selects the transposing form (V).
@@ -388,9 +414,9 @@ __device__ __forceinline__ void load_tiles(uint32_t base, int trow0, int rb, uin
 // hi + lo pair of model-dtype values (two MMAs per k-step).
 // ---------------------------------------------------------------------------
 template <int DT, int D, int KB, int VB, bool VGROUP, int NT, bool QSPLIT>
-__global__ void __launch_bounds__(kMidThreads)
+__global__ void __launch_bounds__(kMidThreads, (NT == 1 ? 3 : 1))
 middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-              MidParams p) {
+              const __grid_constant__ CUtensorMap tmap_s, MidParams p) {
     using L = MidLayout<D, KB, VB, VGROUP, NT>;
     using KMap = ChanMap<KB>;
     using VMap = ChanMap<VB>;
@@ -410,8 +436,11 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int Z = p.B * p.Hkv;
     const int U = total_units(p, Z);
-    const int C = p.n_ctas;
+    // Never more CTAs than units, so every working CTA owns at least one unit
+    // (the merge counts arrivals per row by CTA range).
+    const int C = p.n_ctas < U ? p.n_ctas : U;
     const int c = blockIdx.x;
+    if (c >= C) return;
     const int ub = (int)((int64_t)c * U / C), ue = (int)((int64_t)(c + 1) * U / C);
 
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::FLAG_OFF);
@@ -427,7 +456,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     __syncthreads();
     // Inputs may be produced by the previous kernel in the stream (age-out,
     // query rotation): wait for it before touching global memory, then let the
-    // next kernel (tier0/merge) start its independent prologue.
+    // next kernel in the stream start its prologue.
     griddep_wait();
     griddep_launch_dependents();
     if (ub >= ue) return;
@@ -438,6 +467,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         if (lane == 0) {
             prefetch_tmap(&tmap_k);
             prefetch_tmap(&tmap_v);
+            if (p.scale_tma) prefetch_tmap(&tmap_s);
         }
         int z = z_of_unit(p, Z, ub);
         int zb = units_begin(p, z), ze = units_begin(p, z + 1);
@@ -452,31 +482,36 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             uint8_t* st = smem + s * L::STAGE_BYTES;
             // Units past this row's length (uniform grid over a capacity bound)
             // carry no tokens: complete the stage without a copy.
+            uint8_t* scs = smem + L::SC_BASE + s * L::SC_BYTES;
             if (lane == 0 && tok0 < len) {
-                mbar_expect_tx(full_bar(s), (uint32_t)(L::K_BYTES + L::V_BYTES));
+                const uint32_t sc_bytes = p.scale_tma ? (uint32_t)L::sc_box_bytes(p.group) : 0u;
+                mbar_expect_tx(full_bar(s), (uint32_t)(L::K_BYTES + L::V_BYTES) + sc_bytes);
                 tma_load_2d(smem_u32(st + L::K_OFF), &tmap_k, 0, (int)row0, full_bar(s), policy);
                 tma_load_2d(smem_u32(st + L::V_OFF), &tmap_v, 0, (int)row0, full_bar(s), policy);
-            }
-            if constexpr (!VGROUP) {
-                // per-token scales (raw dtype bits); 0 past the length
-                uint16_t* sc = reinterpret_cast<uint16_t*>(smem + L::SC_BASE + s * L::SC_BYTES);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int tt = lane * 4 + j;
-                    sc[tt] = (tok0 + tt < len) ? load_bits<DT>(p.v_scale, row0 + tt) : (uint16_t)0;
+                if (p.scale_tma) {
+                    // per-token: 1-D map over rows; grouped: 2-D map [groups][D].
+                    // Past the map's extent the TMA unit writes zeros.
+                    if constexpr (!VGROUP) tma_load_1d(smem_u32(scs), &tmap_s, (int)row0, full_bar(s), policy);
+                    else tma_load_2d(smem_u32(scs), &tmap_s, 0, (int)(row0 / p.group), full_bar(s), policy);
                 }
-            } else {
-                // grouped scales: row r uses group r / G.  Stage rows start on a
-                // group boundary (G divides 128 and row bases are group aligned).
-                uint32_t* sc = reinterpret_cast<uint32_t*>(smem + L::SC_BASE + s * L::SC_BYTES);
-                const int G = p.group;
-                const int ngr = kStageTokens / G;
-                const int64_t g0 = row0 / G;
-                for (int e = lane; e < ngr * D; e += 32) {
-                    const int gi = e / D, d = e % D;
-                    const bool ok = tok0 + (int64_t)gi * G < len;
-                    const uint32_t b = ok ? load_bits<DT>(p.v_scale, (g0 + gi) * D + d) : 0u;
-                    sc[e] = b | (b << 16);
+            }
+            if (!p.scale_tma && tok0 < len) {
+                uint16_t* sc = reinterpret_cast<uint16_t*>(scs);
+                if constexpr (!VGROUP) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int tt = lane * 4 + j;
+                        sc[tt] = (tok0 + tt < len) ? load_bits<DT>(p.v_scale, row0 + tt) : (uint16_t)0;
+                    }
+                } else {
+                    const int G = p.group;
+                    const int ngr = kStageTokens / G;
+                    const int64_t g0 = row0 / G;
+                    for (int e = lane; e < ngr * D; e += 32) {
+                        const int gi = e / D, d = e % D;
+                        sc[e] = (tok0 + (int64_t)gi * G < len) ? load_bits<DT>(p.v_scale, (g0 + gi) * D + d)
+                                                                : (uint16_t)0;
+                    }
                 }
             }
             mbar_arrive(full_bar(s));
@@ -502,17 +537,45 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     int cur_z = -1;
     int64_t cur_len = 0;
 
+    // Each thread's K channels form, per 16-byte chunk cb of a packed row, one
+    // contiguous block of CH channels starting at cb*CHW + CH*t; q and the K
+    // scales are fetched block-wise (16-byte loads when aligned) and placed in
+    // the fragment order given by KMap::kdim.
+    constexpr int CH = (KB == 4) ? 8 : 16;
+    constexpr int CHW = 4 * CH;
+    auto load_block_bits = [&](const void* base, int64_t off, uint16_t (&e)[CH]) {
+        const uint16_t* ptr = reinterpret_cast<const uint16_t*>(base) + off;
+        if (p.q_vec) {
+#pragma unroll
+            for (int c4 = 0; c4 < CH / 8; ++c4) {
+                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(ptr) + c4);
+                const uint16_t* r16 = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) e[c4 * 8 + j] = r16[j];
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) e[j] = ptr[j];
+        }
+    };
     auto setup_z = [&](int z) {
         const int b = z / p.Hkv, h = z % p.Hkv;
         const int64_t ks_off = (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
 #pragma unroll
-        for (int ks = 0; ks < KSTEPS; ++ks)
+        for (int cb = 0; cb < KSTEPS * 16 / CHW; ++cb) {
+            uint16_t e[CH];
+            load_block_bits(p.k_scale, ks_off + cb * CHW + CH * t, e);
 #pragma unroll
-            for (int hs = 0; hs < 2; ++hs) {
-                const uint32_t lo = load_bits<DT>(p.k_scale, ks_off + KMap::kdim(ks, 2 * hs, t));
-                const uint32_t hi = load_bits<DT>(p.k_scale, ks_off + KMap::kdim(ks, 2 * hs + 1, t));
-                ksc[ks][hs] = lo | (hi << 16);
+            for (int u = 0; u < CHW / 16; ++u) {
+                const int ks = cb * (CHW / 16) + u;
+#pragma unroll
+                for (int hs = 0; hs < 2; ++hs) {
+                    const int i0 = KMap::kdim(ks, 2 * hs, t) - cb * CHW - CH * t;
+                    const int i1 = KMap::kdim(ks, 2 * hs + 1, t) - cb * CHW - CH * t;
+                    ksc[ks][hs] = (uint32_t)e[i0] | ((uint32_t)e[i1] << 16);
+                }
             }
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int r = nt * 8 + gid;
@@ -520,23 +583,48 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             const int j = rv ? r / p.n_q : 0, sq = rv ? r % p.n_q : 0;
             const int64_t qoff = (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss;
 #pragma unroll
-            for (int ks = 0; ks < KSTEPS; ++ks)
+            for (int cb = 0; cb < KSTEPS * 16 / CHW; ++cb) {
+                if constexpr (QSPLIT) {
+                    float e[CH];
+                    const float* ptr = reinterpret_cast<const float*>(p.q) + qoff + cb * CHW + CH * t;
 #pragma unroll
-                for (int hs = 0; hs < 2; ++hs) {
-                    if constexpr (QSPLIT) {
-                        const float* qf32 = reinterpret_cast<const float*>(p.q);
-                        const float v0 = rv ? qf32[qoff + KMap::kdim(ks, 2 * hs, t)] : 0.f;
-                        const float v1 = rv ? qf32[qoff + KMap::kdim(ks, 2 * hs + 1, t)] : 0.f;
-                        const uint32_t hp = P::pack(v0, v1);
-                        const float h0 = P::unpack_lo(hp), h1 = P::unpack_lo(hp >> 16);
-                        qf[0][nt][ks][hs] = hp;
-                        qf[NQ - 1][nt][ks][hs] = P::pack(v0 - h0, v1 - h1);
-                    } else {
-                        const uint32_t lo = rv ? load_bits<DT>(p.q, qoff + KMap::kdim(ks, 2 * hs, t)) : 0u;
-                        const uint32_t hi = rv ? load_bits<DT>(p.q, qoff + KMap::kdim(ks, 2 * hs + 1, t)) : 0u;
-                        qf[0][nt][ks][hs] = lo | (hi << 16);
+                    for (int c4 = 0; c4 < CH / 4; ++c4) {
+                        const float4 v4 = rv ? __ldg(reinterpret_cast<const float4*>(ptr) + c4)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+                        e[4 * c4] = v4.x; e[4 * c4 + 1] = v4.y; e[4 * c4 + 2] = v4.z; e[4 * c4 + 3] = v4.w;
+                    }
+#pragma unroll
+                    for (int u = 0; u < CHW / 16; ++u) {
+                        const int ks = cb * (CHW / 16) + u;
+#pragma unroll
+                        for (int hs = 0; hs < 2; ++hs) {
+                            const float v0 = e[KMap::kdim(ks, 2 * hs, t) - cb * CHW - CH * t];
+                            const float v1 = e[KMap::kdim(ks, 2 * hs + 1, t) - cb * CHW - CH * t];
+                            const uint32_t hp = P::pack(v0, v1);
+                            const float h0 = P::unpack_lo(hp), h1 = P::unpack_lo(hp >> 16);
+                            qf[0][nt][ks][hs] = hp;
+                            qf[NQ - 1][nt][ks][hs] = P::pack(v0 - h0, v1 - h1);
+                        }
+                    }
+                } else {
+                    uint16_t e[CH];
+                    if (rv) load_block_bits(p.q, qoff + cb * CHW + CH * t, e);
+                    else {
+#pragma unroll
+                        for (int jj = 0; jj < CH; ++jj) e[jj] = 0;
+                    }
+#pragma unroll
+                    for (int u = 0; u < CHW / 16; ++u) {
+                        const int ks = cb * (CHW / 16) + u;
+#pragma unroll
+                        for (int hs = 0; hs < 2; ++hs) {
+                            const int i0 = KMap::kdim(ks, 2 * hs, t) - cb * CHW - CH * t;
+                            const int i1 = KMap::kdim(ks, 2 * hs + 1, t) - cb * CHW - CH * t;
+                            qf[0][nt][ks][hs] = (uint32_t)e[i0] | ((uint32_t)e[i1] << 16);
+                        }
                     }
                 }
+            }
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -548,6 +636,67 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 for (int e = 0; e < 4; ++e) o[nt][mi][e] = 0.f;
         }
         cur_len = seg_len(p, b);
+    };
+
+    volatile int* merge_flag = reinterpret_cast<volatile int*>(smem + L::FLAG_OFF + 4);
+    // Merge of row z (runs in the CTA whose arrival completed z): obuf and
+    // mlbuf are free again here.  Partial of CTA c lives at unit max(zb, ub(c)).
+    auto merge = [&](int z, int zb, int c0, int c1) {
+        const int rows = p.rows;
+        float* Mr = mlbuf;            // [16] row max
+        float* Lr = mlbuf + 16;       // [16] 1 / row sum
+        float* Fw = mlbuf + 32;       // [16] weight of the FP partial
+        if (ctid < rows) {
+            const int r = ctid;
+            float M = -INFINITY;
+            const float fm = p.fp_ml ? p.fp_ml[((int64_t)z * rows + r) * 2] : -INFINITY;
+            M = fmaxf(M, fm);
+            for (int cc = c0; cc <= c1; ++cc) {
+                const int ucc = (int)((int64_t)cc * U / C);
+                const int sl = ucc > zb ? ucc : zb;
+                M = fmaxf(M, p.ws_ml[((int64_t)sl * rows + r) * 2]);
+            }
+            float Ls = 0.f;
+            const float fw = (fm == -INFINITY) ? 0.f : ex2(fm - M);
+            if (p.fp_ml) Ls += fw * p.fp_ml[((int64_t)z * rows + r) * 2 + 1];
+            for (int cc = c0; cc <= c1; ++cc) {
+                const int ucc = (int)((int64_t)cc * U / C);
+                const int sl = ucc > zb ? ucc : zb;
+                const float ms = p.ws_ml[((int64_t)sl * rows + r) * 2];
+                if (ms != -INFINITY) Ls += ex2(ms - M) * p.ws_ml[((int64_t)sl * rows + r) * 2 + 1];
+            }
+            Mr[r] = M;
+            Lr[r] = Ls > 0.f ? 1.f / Ls : 0.f;
+            Fw[r] = fw;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+        for (int i = ctid; i < rows * D; i += kConsumerWarps * 32) {
+            const int r = i / D;
+            float acc = 0.f;
+            for (int cc = c0; cc <= c1; ++cc) {
+                const int ucc = (int)((int64_t)cc * U / C);
+                const int sl = ucc > zb ? ucc : zb;
+                const float ms = p.ws_ml[((int64_t)sl * rows + r) * 2];
+                if (ms != -INFINITY) acc = fmaf(ex2(ms - Mr[r]), p.ws_o[(int64_t)sl * rows * D + i], acc);
+            }
+            obuf[i] = acc;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+        const int b = z / p.Hkv, h = z % p.Hkv;
+        auto* out = reinterpret_cast<typename Elem<DT>::T*>(p.out);
+        for (int i = ctid; i < rows * D; i += kConsumerWarps * 32) {
+            const int r = i / D, d = i % D;
+            float mid = obuf[i];
+            if (p.rotation) {
+                mid = 0.f;
+                for (int e = 0; e < D; ++e) mid = fmaf(obuf[r * D + e], p.rotation[(int64_t)e * D + d], mid);
+            }
+            float v = mid;
+            if (p.fp_o) v = fmaf(Fw[r], p.fp_o[(int64_t)z * rows * D + i], v);
+            v *= Lr[r];
+            const int j = r / p.n_q, sq = r % p.n_q;
+            out[(int64_t)b * p.o_sb + (int64_t)(h * p.g + j) * p.o_sh + (int64_t)sq * p.o_ss + d] = Elem<DT>::from_f(v);
+        }
     };
 
     auto flush = [&](int z) {
@@ -618,6 +767,22 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             p.ws_ml[((int64_t)slot * p.rows + r) * 2 + 0] = M;
             p.ws_ml[((int64_t)slot * p.rows + r) * 2 + 1] = Ls;
         }
+        // 4) count the arrival; the last CTA of row z merges every partial of
+        //    z (FP tiers + one per middle CTA) and writes the output.  No CTA
+        //    ever waits for another: the merge runs where the count completes.
+        __threadfence();
+        named_bar_sync(1, kConsumerWarps * 32);
+        const int ze = units_begin(p, z + 1);
+        const int c0 = cta_of_unit(zb, C, U), c1 = cta_of_unit(ze - 1, C, U);
+        if (ctid == 0) {
+            const int old = atomicAdd(p.counters + z, 1);
+            *merge_flag = (old == c1 - c0) ? 1 : 0;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+        if (*merge_flag) {
+            __threadfence();
+            merge(z, zb, c0, c1);
+        }
         named_bar_sync(1, kConsumerWarps * 32);
     };
 
@@ -644,13 +809,15 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 
         if (ready && tok_w < cur_len) {
             // ---- S^T = K_deq . q^T for the warp's 2 m-tiles ----
-            float sacc[2][NT][4];
+            // two accumulators per m-tile (even / odd k-steps) halve the
+            // dependent MMA chain; summed before the softmax
+            float sacc[2][NT][4], sacc2[2][NT][4];
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = 0.f;
+                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = sacc2[mt][nt][e] = 0.f;
                 uint32_t kr[2][L::NCHK];
                 load_tiles<L::NCHK, false>(kbase, warp * 32 + mt * 16, L::RBK, smask_k, lane, kr);
 #pragma unroll
@@ -670,7 +837,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
                                 for (int nt = 0; nt < NT; ++nt)
-                                    P::mma(sacc[mt][nt], a0, a1, a2, a3, qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
+                                    P::mma((ks & 1) ? sacc2[mt][nt] : sacc[mt][nt], a0, a1, a2, a3,
+                                           qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     } else {
                         uint32_t h0[8], h1[8];
@@ -687,11 +855,18 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
                                 for (int nt = 0; nt < NT; ++nt)
-                                    P::mma(sacc[mt][nt], a0, a1, a2, a3, qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
+                                    P::mma((ks & 1) ? sacc2[mt][nt] : sacc[mt][nt], a0, a1, a2, a3,
+                                           qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     }
                 }
             }
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] += sacc2[mt][nt][e];
             // ---- online softmax over the 32 tokens (log2 domain) ----
             uint32_t pb[2][NT][2];
 #pragma unroll
@@ -742,14 +917,25 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 const int trow0 = warp * 32 + mt * 16;
                 uint32_t vr[2][L::NCHV];
                 load_tiles<L::NCHV, true>(vbase, trow0, L::RBV, smask_v, lane, vr);
+                // tokens of this m-tile past the length: their scales may be
+                // stale bytes (NaN * 0 must not reach the MMA), so zero them;
+                // a tile entirely past the length is skipped.
+                const int64_t tile_tok = tok_w - warp * 32 + trow0;
+                if (tile_tok >= cur_len) continue;
                 uint32_t vs0 = 0, vs1 = 0;
-                const uint32_t* gsc = nullptr;
+                const uint16_t* gsc = nullptr;
                 if constexpr (!VGROUP) {
                     const uint32_t* sc32 = reinterpret_cast<const uint32_t*>(scb);
                     vs0 = sc32[(trow0 + 2 * t) >> 1];       // tokens 2t, 2t+1
                     vs1 = sc32[(trow0 + 8 + 2 * t) >> 1];   // tokens 8+2t, 9+2t
+                    const int64_t rem = cur_len - tile_tok;  // valid tokens in this tile (> 0)
+                    if (rem < 16) {
+                        const int t0 = 2 * t, t1 = 8 + 2 * t;
+                        vs0 &= (t0 < rem ? 0x0000FFFFu : 0u) | (t0 + 1 < rem ? 0xFFFF0000u : 0u);
+                        vs1 &= (t1 < rem ? 0x0000FFFFu : 0u) | (t1 + 1 < rem ? 0xFFFF0000u : 0u);
+                    }
                 } else {
-                    gsc = reinterpret_cast<const uint32_t*>(scb) + (trow0 / p.group) * D;
+                    gsc = reinterpret_cast<const uint16_t*>(scb) + (trow0 / p.group) * D;
                 }
 #pragma unroll
                 for (int cb = 0; cb < L::NCHV; ++cb) {
@@ -768,7 +954,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                                 a2 = P::mul(h1[2 * j + 1], vs1);
                                 a3 = P::mul(h1[2 * j], vs1);
                             } else {
-                                const uint32_t g0 = gsc[VMap::vdim(mi, 0, gid)], g1 = gsc[VMap::vdim(mi, 1, gid)];
+                                const uint32_t g0 = dup16(gsc[VMap::vdim(mi, 0, gid)]);
+                                const uint32_t g1 = dup16(gsc[VMap::vdim(mi, 1, gid)]);
                                 a0 = P::mul(h0[2 * j + 1], g0);
                                 a1 = P::mul(h0[2 * j], g1);
                                 a2 = P::mul(h1[2 * j + 1], g0);
@@ -795,7 +982,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                                 a2 = P::mul(h1[lo[j]], vs1);
                                 a3 = P::mul(h1[hi[j]], vs1);
                             } else {
-                                const uint32_t g0 = gsc[VMap::vdim(mi, 0, gid)], g1 = gsc[VMap::vdim(mi, 1, gid)];
+                                const uint32_t g0 = dup16(gsc[VMap::vdim(mi, 0, gid)]);
+                                const uint32_t g1 = dup16(gsc[VMap::vdim(mi, 1, gid)]);
                                 a0 = P::mul(h0[lo[j]], g0);
                                 a1 = P::mul(h0[hi[j]], g1);
                                 a2 = P::mul(h1[lo[j]], g0);
@@ -839,7 +1027,12 @@ __global__ void rotate_queries_kernel(const void* q, int Hq, int n_q, int D, int
 }
 
 // ---------------------------------------------------------------------------
-// k2: FP tiers (SIMT) + split-K merge + output, one CTA per (b, kv-head)
+// k_fp: attention over the FP (model-dtype) tiers -- sinks and the recent
+// window -- one CTA per (b, kv-head).  With a quantised middle it writes an
+// un-normalised partial (m, l, O) that the middle kernel's merge consumes;
+// otherwise (or for a row with no middle units) it writes the final output.
+// Lanes of a warp take 8 tokens x 4 channel quarters for q.k (16-byte loads)
+// and own D/32 channels each for p.v (coalesced rows).
 // ---------------------------------------------------------------------------
 struct FpSeg {
     const void* k;
@@ -849,7 +1042,7 @@ struct FpSeg {
     const int32_t* lens;
     int64_t len;
 };
-struct Tier0Params {
+struct FpParams {
     int B, Hq, Hkv, D, n_q, g, rows;
     float qk_scale;
     const void* q;
@@ -859,37 +1052,63 @@ struct Tier0Params {
     int n_fp;
     FpSeg fp[FADE_MAX_SEGMENTS];
     int has_mid;
-    const float* rotation;          // non-null: middle partials are in rotated space
-    const int32_t* cu_units;
+    const int32_t* cu_units;        // middle units per row (ragged) or null
     int units_per_z;
-    int n_ctas;
-    const float* ws_ml;
-    const float* ws_o;
+    float* ws_fpml;                 // [Z][rows][2]
+    float* ws_fpo;                  // [Z][rows][D]
+    int* counters;                  // [Z] middle-kernel arrival counters (zeroed here)
+    int vec;                        // FP rows 16-byte aligned: vector loads
 };
 
+template <int DT, int N>
+__device__ __forceinline__ void load_row_part(const typename Elem<DT>::T* src, bool vec, bool valid,
+                                              float (&dst)[N]) {
+    if (!valid) {
+#pragma unroll
+        for (int e = 0; e < N; ++e) dst[e] = 0.f;
+        return;
+    }
+    if constexpr (N % 8 == 0) {
+        if (vec) {
+#pragma unroll
+            for (int c = 0; c < N / 8; ++c) {
+                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src) + c);
+                const auto* e8 = reinterpret_cast<const typename Elem<DT>::T*>(&raw);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) dst[c * 8 + e] = Elem<DT>::to_f(e8[e]);
+            }
+            return;
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < N; ++e) dst[e] = Elem<DT>::to_f(src[e]);
+}
+
 template <int DT, int D, int NT>
-__global__ void __launch_bounds__(kTier0Threads)
-tier0_merge_kernel(Tier0Params p) {
+__global__ void __launch_bounds__(kFpThreads)
+fp_tier_kernel(FpParams p) {
     constexpr int ROWS = NT * 8;
-    constexpr int DPL = D / 32;  // channels per lane in the PV accumulation
-    constexpr int DQ = D / 4;    // channels per lane in the QK dot product
-    // With a middle tier the preceding grid is k1, which only let this grid
-    // start after its own griddepcontrol.wait, so q and the FP tiers are final
-    // and the FP pass can overlap k1.  Without one, wait for the predecessor.
-    if (!p.has_mid) griddep_wait();
+    constexpr int DPL = D / 32;      // channels per lane in p.v
+    constexpr int DQ = D / 4;        // channels per lane in q.k
+    constexpr int QS = DQ + 4;       // padded quarter stride: quarters hit different banks
+    constexpr int RS = 4 * QS;
+    constexpr int NW = kFpThreads / 32;
+    griddep_wait();
     griddep_launch_dependents();
-    __shared__ float qsm[ROWS * D];
+    __shared__ __align__(16) float qsm[ROWS * RS];
     __shared__ float osm[ROWS * D];
-    __shared__ float msm[kTier0Threads / 32][ROWS], lsm[kTier0Threads / 32][ROWS];
+    __shared__ float msm[NW][ROWS], lsm[NW][ROWS];
     __shared__ float fin_m[ROWS], fin_l[ROWS];
 
     const int z = blockIdx.x;
     const int b = z / p.Hkv, h = z % p.Hkv;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int nw = kTier0Threads / 32;
     const int rows = p.rows;
+    // The middle kernel (next in the stream, started only after this grid
+    // completes) counts arrivals per row here; start every call from zero.
+    if (threadIdx.x == 0 && p.counters) p.counters[z] = 0;
 
-    for (int i = threadIdx.x; i < ROWS * D; i += kTier0Threads) {
+    for (int i = threadIdx.x; i < ROWS * D; i += kFpThreads) {
         const int r = i / D, d = i % D;
         float v = 0.f;
         if (r < rows) {
@@ -897,7 +1116,7 @@ tier0_merge_kernel(Tier0Params p) {
             v = load_f<DT>(p.q, (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss + d) *
                 p.qk_scale;
         }
-        qsm[i] = v;
+        qsm[r * RS + (d / DQ) * QS + d % DQ] = v;
         osm[i] = 0.f;
     }
     __syncthreads();
@@ -910,26 +1129,40 @@ tier0_merge_kernel(Tier0Params p) {
 #pragma unroll
         for (int e = 0; e < DPL; ++e) o[r][e] = 0.f;
     }
-    const int tk = lane >> 2, qd = lane & 3;  // QK layout: token tk (0..7), quarter qd
+    const int tk = lane >> 2, qd = lane & 3;
     for (int si = 0; si < p.n_fp; ++si) {
         const FpSeg& sg = p.fp[si];
         const int64_t len = sg.lens ? (int64_t)sg.lens[b] : sg.len;
         const int64_t row0 = sg.row_base ? sg.row_base[z] : (int64_t)b * sg.row_sb + (int64_t)h * sg.row_sh;
         const auto* K = reinterpret_cast<const typename Elem<DT>::T*>(sg.k);
         const auto* V = reinterpret_cast<const typename Elem<DT>::T*>(sg.v);
-        for (int64_t t0 = (int64_t)warp * 8; t0 < len; t0 += (int64_t)nw * 8) {
+        for (int64_t t0 = (int64_t)warp * 8; t0 < len; t0 += (int64_t)NW * 8) {
             const int64_t tok = t0 + tk;
             const bool tv = tok < len;
             float kd[DQ];
-            const auto* kr = K + (row0 + (tv ? tok : 0)) * D + qd * DQ;
+            load_row_part<DT, DQ>(K + (row0 + (tv ? tok : 0)) * D + qd * DQ, p.vec != 0, tv, kd);
+            // the group's 8 V rows are requested together with K (one latency)
+            float vv[8][DPL];
 #pragma unroll
-            for (int e = 0; e < DQ; ++e) kd[e] = tv ? Elem<DT>::to_f(kr[e]) : 0.f;
+            for (int tt = 0; tt < 8; ++tt) {
+                const int64_t tk2 = t0 + tt;
+                const auto* vr = V + (row0 + (tk2 < len ? tk2 : 0)) * D + lane * DPL;
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) vv[tt][e] = tk2 < len ? Elem<DT>::to_f(vr[e]) : 0.f;
+            }
             float sc[ROWS];
 #pragma unroll
             for (int r = 0; r < ROWS; ++r) {
+                const float4* qv = reinterpret_cast<const float4*>(qsm + r * RS + qd * QS);
                 float acc = 0.f;
 #pragma unroll
-                for (int e = 0; e < DQ; ++e) acc = fmaf(qsm[r * D + qd * DQ + e], kd[e], acc);
+                for (int e4 = 0; e4 < DQ / 4; ++e4) {
+                    const float4 q4 = qv[e4];
+                    acc = fmaf(q4.x, kd[4 * e4], acc);
+                    acc = fmaf(q4.y, kd[4 * e4 + 1], acc);
+                    acc = fmaf(q4.z, kd[4 * e4 + 2], acc);
+                    acc = fmaf(q4.w, kd[4 * e4 + 3], acc);
+                }
                 acc += __shfl_xor_sync(0xffffffffu, acc, 1);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 2);
                 sc[r] = tv ? acc : -INFINITY;
@@ -953,25 +1186,17 @@ tier0_merge_kernel(Tier0Params p) {
 #pragma unroll
                 for (int e = 0; e < DPL; ++e) o[r][e] *= corr;
             }
-            // PV: lane owns channels lane*DPL .. +DPL
 #pragma unroll
             for (int tt = 0; tt < 8; ++tt) {
-                const int64_t tk2 = t0 + tt;
-                if (tk2 >= len) break;
-                const auto* vr = V + (row0 + tk2) * D + lane * DPL;
-                float vv[DPL];
-#pragma unroll
-                for (int e = 0; e < DPL; ++e) vv[e] = Elem<DT>::to_f(vr[e]);
 #pragma unroll
                 for (int r = 0; r < ROWS; ++r) {
                     const float pt = __shfl_sync(0xffffffffu, pr[r], tt * 4);
 #pragma unroll
-                    for (int e = 0; e < DPL; ++e) o[r][e] = fmaf(pt, vv[e], o[r][e]);
+                    for (int e = 0; e < DPL; ++e) o[r][e] = fmaf(pt, vv[tt][e], o[r][e]);
                 }
             }
         }
     }
-    // combine warps -> (fin_m, fin_l, osm) for the FP tiers
     if (lane == 0) {
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) { msm[warp][r] = m[r]; lsm[warp][r] = l[r]; }
@@ -980,8 +1205,8 @@ tier0_merge_kernel(Tier0Params p) {
     if (threadIdx.x < ROWS) {
         const int r = threadIdx.x;
         float M = -INFINITY, Ls = 0.f;
-        for (int w = 0; w < nw; ++w) M = fmaxf(M, msm[w][r]);
-        for (int w = 0; w < nw; ++w)
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, msm[w][r]);
+        for (int w = 0; w < NW; ++w)
             if (msm[w][r] != -INFINITY) Ls += ex2(msm[w][r] - M) * lsm[w][r];
         fin_m[r] = M;
         fin_l[r] = Ls;
@@ -994,98 +1219,22 @@ tier0_merge_kernel(Tier0Params p) {
         for (int e = 0; e < DPL; ++e) atomicAdd(&osm[r * D + lane * DPL + e], o[r][e] * f);
     }
     __syncthreads();
-
-    // ---- merge with the middle tier's split-K partials ----
-    if (p.has_mid) {
-        griddep_wait();
-        const int Z = p.B * p.Hkv;
-        const int U = p.cu_units ? p.cu_units[Z] : Z * p.units_per_z;
-        const int zb = p.cu_units ? p.cu_units[z] : z * p.units_per_z;
-        const int ze = p.cu_units ? p.cu_units[z + 1] : (z + 1) * p.units_per_z;
-        // A k1 CTA stores its partial for z at the first unit of z it
-        // processed.  Unit zb+s2 holds a partial iff it is z's first unit or
-        // its owning CTA's range starts there.
-        const int nslots = ze - zb;
-        auto slot_live = [&](int s2) {
-            const int u = zb + s2;
-            if (s2 == 0) return true;
-            const int owner = cta_of_unit(u, p.n_ctas, U);
-            return (int)((int64_t)owner * U / p.n_ctas) == u;
-        };
-        // Per row: global max / sum over the FP part and every slot.
-        __shared__ float mid_w[64][ROWS];  // weight per slot (nslots <= 64 handled in chunks)
-        __shared__ float fp_w[ROWS], inv_L[ROWS];
-        if (threadIdx.x < ROWS) {
-            const int r = threadIdx.x;
-            float M = fin_m[r];
-            for (int s2 = 0; s2 < nslots; ++s2)
-                if (slot_live(s2)) M = fmaxf(M, p.ws_ml[((int64_t)(zb + s2) * rows + r) * 2]);
-            float Ls = (fin_m[r] == -INFINITY) ? 0.f : ex2(fin_m[r] - M) * fin_l[r];
-            fp_w[r] = (fin_m[r] == -INFINITY) ? 0.f : ex2(fin_m[r] - M);
-            for (int s2 = 0; s2 < nslots; ++s2) {
-                if (!slot_live(s2)) continue;
-                const float ms = p.ws_ml[((int64_t)(zb + s2) * rows + r) * 2];
-                if (ms != -INFINITY) Ls += ex2(ms - M) * p.ws_ml[((int64_t)(zb + s2) * rows + r) * 2 + 1];
-            }
-            inv_L[r] = (Ls > 0.f) ? 1.f / Ls : 0.f;
-            fin_m[r] = M;
+    int units_z = 0;
+    if (p.has_mid) units_z = p.cu_units ? p.cu_units[z + 1] - p.cu_units[z] : p.units_per_z;
+    if (units_z > 0) {
+        for (int i = threadIdx.x; i < rows * D; i += kFpThreads) p.ws_fpo[(int64_t)z * rows * D + i] = osm[i];
+        if (threadIdx.x < rows) {
+            p.ws_fpml[((int64_t)z * rows + threadIdx.x) * 2 + 0] = fin_m[threadIdx.x];
+            p.ws_fpml[((int64_t)z * rows + threadIdx.x) * 2 + 1] = fin_l[threadIdx.x];
         }
-        __syncthreads();
-        // qsm is reused as the merged middle accumulator
-        for (int i = threadIdx.x; i < ROWS * D; i += kTier0Threads) qsm[i] = 0.f;
-        for (int base = 0; base < nslots; base += 64) {
-            const int nb = min(64, nslots - base);
-            __syncthreads();
-            for (int i = threadIdx.x; i < nb * ROWS; i += kTier0Threads) {
-                const int s2 = i / ROWS, r = i % ROWS;
-                float w = 0.f;
-                if (r < rows && slot_live(base + s2)) {
-                    const float ms = p.ws_ml[((int64_t)(zb + base + s2) * rows + r) * 2];
-                    w = (ms == -INFINITY) ? 0.f : ex2(ms - fin_m[r]);
-                }
-                mid_w[s2][r] = w;
-            }
-            __syncthreads();
-            for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
-                const int r = i / D;
-                float acc = qsm[i];
-                for (int s2 = 0; s2 < nb; ++s2) {
-                    const float w = mid_w[s2][r];
-                    if (w != 0.f) acc = fmaf(w, p.ws_o[(int64_t)(zb + base + s2) * rows * D + i], acc);
-                }
-                qsm[i] = acc;
-            }
-        }
-        __syncthreads();
-        if (p.rotation) {
-            // out = fp + mid @ R
-            for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
-                const int r = i / D, d = i % D;
-                float acc = 0.f;
-                for (int e = 0; e < D; ++e) acc = fmaf(qsm[r * D + e], p.rotation[(int64_t)e * D + d], acc);
-                osm[i] = osm[i] * fp_w[r] + acc;
-            }
-        } else {
-            for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
-                const int r = i / D;
-                osm[i] = osm[i] * fp_w[r] + qsm[i];
-            }
-        }
-        __syncthreads();
-        for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) osm[i] *= inv_L[i / D];
     } else {
-        for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
-            const int r = i / D;
-            osm[i] = fin_l[r] > 0.f ? osm[i] / fin_l[r] : 0.f;
+        auto* out = reinterpret_cast<typename Elem<DT>::T*>(p.out);
+        for (int i = threadIdx.x; i < rows * D; i += kFpThreads) {
+            const int r = i / D, d = i % D;
+            const int j = r / p.n_q, sq = r % p.n_q;
+            const float v = fin_l[r] > 0.f ? osm[i] / fin_l[r] : 0.f;
+            out[(int64_t)b * p.o_sb + (int64_t)(h * p.g + j) * p.o_sh + (int64_t)sq * p.o_ss + d] = Elem<DT>::from_f(v);
         }
-    }
-    __syncthreads();
-    auto* out = reinterpret_cast<typename Elem<DT>::T*>(p.out);
-    for (int i = threadIdx.x; i < rows * D; i += kTier0Threads) {
-        const int r = i / D, d = i % D;
-        const int j = r / p.n_q, sq = r % p.n_q;
-        out[(int64_t)b * p.o_sb + (int64_t)(h * p.g + j) * p.o_sh + (int64_t)sq * p.o_ss + d] =
-            Elem<DT>::from_f(osm[i]);
     }
 }
 
@@ -1120,6 +1269,34 @@ static int make_row_map(CUtensorMap* m, const void* base, int64_t n_rows, int ro
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FADE_OK : FADE_ERR_ALIGN;
+}
+
+// V scales: per-token -> 1-D map over rows (box = one stage of rows);
+// grouped -> 2-D map [groups][D] (box = the stage's groups).  UINT16 elements:
+// the bits are copied, not converted.
+static int make_scale_map(CUtensorMap* m, const void* base, int64_t n_rows, bool grouped, int D, int G) {
+    auto enc = encode_fn();
+    if (!enc) return FADE_ERR_CUDA;
+    CUresult r;
+    if (!grouped) {
+        cuuint64_t dims[1] = {(cuuint64_t)n_rows};
+        cuuint64_t strides[1] = {2};
+        cuuint32_t box[1] = {(cuuint32_t)kStageTokens};
+        cuuint32_t estr[1] = {1};
+        r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 1, const_cast<void*>(base), dims, strides + 1, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const int64_t n_groups = (n_rows + G - 1) / G;
+        cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)n_groups};
+        cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+        cuuint32_t box[2] = {(cuuint32_t)D, (cuuint32_t)(kStageTokens / G)};
+        cuuint32_t estr[2] = {1, 1};
+        r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
     return r == CUDA_SUCCESS ? FADE_OK : FADE_ERR_ALIGN;
 }
 
@@ -1178,9 +1355,9 @@ static MidKernelInfo select_mid_d(int D, int NT, int kb, int vb, bool vg, bool r
 }
 
 template <int DT>
-static void* select_tier0(int D, int NT) {
-    if (D == 128) return NT == 1 ? (void*)&tier0_merge_kernel<DT, 128, 1> : (void*)&tier0_merge_kernel<DT, 128, 2>;
-    if (D == 64) return NT == 1 ? (void*)&tier0_merge_kernel<DT, 64, 1> : (void*)&tier0_merge_kernel<DT, 64, 2>;
+static void* select_fp(int D, int NT) {
+    if (D == 128) return NT == 1 ? (void*)&fp_tier_kernel<DT, 128, 1> : (void*)&fp_tier_kernel<DT, 128, 2>;
+    if (D == 64) return NT == 1 ? (void*)&fp_tier_kernel<DT, 64, 1> : (void*)&fp_tier_kernel<DT, 64, 2>;
     return nullptr;
 }
 
@@ -1192,7 +1369,8 @@ struct Plan {
     int units_per_z;     // uniform
     int64_t max_units;   // sizing bound
     int n_ctas;
-    size_t off_err, off_qrot, off_ml, off_o, total;
+    int n_fp;
+    size_t off_err, off_qrot, off_cnt, off_fpml, off_fpo, off_ml, off_o, total;
     MidKernelInfo mk;
 };
 
@@ -1208,10 +1386,12 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
     if (pl->rows > 16) return FADE_ERR_UNSUPPORTED;
     pl->NT = pl->rows > 8 ? 2 : 1;
     pl->mid_idx = -1;
+    pl->n_fp = 0;
     for (int i = 0; i < d->n_segments; ++i) {
         const fade_kv_segment& s = d->seg[i];
         if (s.kind == FADE_SEG_FP) {
             if (!s.k || !s.v) return FADE_ERR_INVALID_ARG;
+            ++pl->n_fp;
             continue;
         }
         if (pl->mid_idx >= 0) return FADE_ERR_UNSUPPORTED;  // one quantised tier per call
@@ -1254,6 +1434,9 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
     pl->off_err = off; off += 256;
     pl->off_qrot = off;
     if (rot) off += ((size_t)d->B * d->Hq * d->n_q * d->D * 4 + 255) / 256 * 256;
+    pl->off_cnt = off; off += ((size_t)Z * 4 + 255) / 256 * 256;
+    pl->off_fpml = off; off += ((size_t)Z * pl->rows * 2 * 4 + 255) / 256 * 256;
+    pl->off_fpo = off; off += ((size_t)Z * pl->rows * d->D * 4 + 255) / 256 * 256;
     pl->off_ml = off; off += ((size_t)pl->max_units * pl->rows * 2 * 4 + 255) / 256 * 256;
     pl->off_o = off; off += (size_t)pl->max_units * pl->rows * d->D * 4;
     pl->total = off;
@@ -1312,6 +1495,37 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
         FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)(d->B * d->Hq * d->n_q)), dim3(128),
                                  (size_t)d->D * 4, s, args));
     }
+    // FP tiers: a partial for the merge, or the final output when there is no
+    // middle (and for ragged rows whose middle is empty).
+    // Always launched: with a middle tier it also zeroes the arrival counters
+    // (the workspace may have held another call's partials there).
+    const bool run_fp = true;
+    if (run_fp) {
+        FpParams fp = {};
+        fp.B = d->B; fp.Hq = d->Hq; fp.Hkv = d->Hkv; fp.D = d->D; fp.n_q = d->n_q;
+        fp.g = pl.g; fp.rows = pl.rows; fp.qk_scale = qk_scale;
+        fp.q = d->q; fp.q_sb = d->q_sb; fp.q_sh = d->q_sh; fp.q_ss = d->q_ss;
+        fp.out = d->out; fp.o_sb = d->o_sb; fp.o_sh = d->o_sh; fp.o_ss = d->o_ss;
+        fp.vec = 1;
+        for (int i = 0; i < d->n_segments; ++i) {
+            const fade_kv_segment& sg = d->seg[i];
+            if (sg.kind != FADE_SEG_FP) continue;
+            FpSeg& f = fp.fp[fp.n_fp++];
+            f.k = sg.k; f.v = sg.v; f.row_sb = sg.row_sb; f.row_sh = sg.row_sh;
+            f.row_base = sg.row_base; f.lens = sg.lens; f.len = sg.len;
+            if (!aligned16(sg.k) || !aligned16(sg.v)) fp.vec = 0;
+        }
+        fp.has_mid = has_mid ? 1 : 0;
+        fp.cu_units = d->cu_units;
+        fp.units_per_z = pl.units_per_z;
+        fp.ws_fpml = reinterpret_cast<float*>(ws + pl.off_fpml);
+        fp.ws_fpo = reinterpret_cast<float*>(ws + pl.off_fpo);
+        fp.counters = has_mid ? reinterpret_cast<int*>(ws + pl.off_cnt) : nullptr;
+        void* fn = d->dtype == FADE_F16 ? select_fp<FADE_F16>(d->D, pl.NT) : select_fp<FADE_BF16>(d->D, pl.NT);
+        if (!fn) return FADE_ERR_UNSUPPORTED;
+        void* args[] = {(void*)&fp};
+        FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)Z), dim3(kFpThreads), 0, s, args));
+    }
     if (has_mid) {
         const fade_kv_segment& sg = d->seg[pl.mid_idx];
         CUtensorMap tk, tv;
@@ -1328,6 +1542,15 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
         if (n_rows >= ((int64_t)1 << 31)) return FADE_ERR_UNSUPPORTED;
         if ((st = make_row_map(&tk, sg.k, n_rows, rbk)) != FADE_OK) return st;
         if ((st = make_row_map(&tv, sg.v, n_rows, rbv)) != FADE_OK) return st;
+        // V scales by TMA when every stage's first row lands on a 16-byte
+        // boundary of the scale array; otherwise the producer warp loads them.
+        CUtensorMap ts;
+        memset(&ts, 0, sizeof(ts));
+        int scale_tma = aligned16(sg.v_scale) && !sg.row_base;
+        if (scale_tma && !pl.vg) scale_tma = (sg.row_sb % 8 == 0) && (sg.row_sh % 8 == 0);
+        if (scale_tma && pl.vg) scale_tma = (d->D * 2) % 16 == 0;
+        if (scale_tma && make_scale_map(&ts, sg.v_scale, n_rows, pl.vg, d->D, pl.vg ? sg.group : 1) != FADE_OK)
+            scale_tma = 0;
         MidParams mp = {};
         mp.dtype = d->dtype;
         mp.B = d->B; mp.Hq = d->Hq; mp.Hkv = d->Hkv; mp.D = d->D; mp.n_q = d->n_q;
@@ -1351,34 +1574,18 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
         mp.ws_ml = reinterpret_cast<float*>(ws + pl.off_ml);
         mp.ws_o = reinterpret_cast<float*>(ws + pl.off_o);
         mp.ws_err = reinterpret_cast<int*>(ws + pl.off_err);
-        void* args[] = {(void*)&tk, (void*)&tv, (void*)&mp};
+        mp.counters = reinterpret_cast<int*>(ws + pl.off_cnt);
+        mp.fp_ml = pl.n_fp > 0 ? reinterpret_cast<const float*>(ws + pl.off_fpml) : nullptr;
+        mp.fp_o = pl.n_fp > 0 ? reinterpret_cast<const float*>(ws + pl.off_fpo) : nullptr;
+        mp.out = d->out; mp.o_sb = d->o_sb; mp.o_sh = d->o_sh; mp.o_ss = d->o_ss;
+        mp.rotation = rot ? d->rotation : nullptr;
+        mp.scale_tma = scale_tma;
+        mp.q_vec = aligned16(sg.k_scale) && sg.ks_sb % 8 == 0 && sg.ks_sh % 8 == 0 &&
+                   (rot || (aligned16(d->q) && d->q_sb % 8 == 0 && d->q_sh % 8 == 0 && d->q_ss % 8 == 0));
+        void* args[] = {(void*)&tk, (void*)&tv, (void*)&ts, (void*)&mp};
         FADE_CUDA_TRY(launch_pdl(pl.mk.fn, dim3((unsigned)pl.n_ctas), dim3(kMidThreads),
                                  (size_t)pl.mk.smem, s, args));
     }
-    Tier0Params tp = {};
-    tp.B = d->B; tp.Hq = d->Hq; tp.Hkv = d->Hkv; tp.D = d->D; tp.n_q = d->n_q;
-    tp.g = pl.g; tp.rows = pl.rows; tp.qk_scale = qk_scale;
-    tp.q = d->q; tp.q_sb = d->q_sb; tp.q_sh = d->q_sh; tp.q_ss = d->q_ss;
-    tp.out = d->out; tp.o_sb = d->o_sb; tp.o_sh = d->o_sh; tp.o_ss = d->o_ss;
-    tp.n_fp = 0;
-    for (int i = 0; i < d->n_segments; ++i) {
-        const fade_kv_segment& sg = d->seg[i];
-        if (sg.kind != FADE_SEG_FP) continue;
-        FpSeg& f = tp.fp[tp.n_fp++];
-        f.k = sg.k; f.v = sg.v; f.row_sb = sg.row_sb; f.row_sh = sg.row_sh;
-        f.row_base = sg.row_base; f.lens = sg.lens; f.len = sg.len;
-    }
-    tp.has_mid = has_mid ? 1 : 0;
-    tp.rotation = rot ? d->rotation : nullptr;
-    tp.cu_units = d->cu_units;
-    tp.units_per_z = pl.units_per_z;
-    tp.n_ctas = pl.n_ctas;
-    tp.ws_ml = reinterpret_cast<const float*>(ws + pl.off_ml);
-    tp.ws_o = reinterpret_cast<const float*>(ws + pl.off_o);
-    void* fn = d->dtype == FADE_F16 ? select_tier0<FADE_F16>(d->D, pl.NT) : select_tier0<FADE_BF16>(d->D, pl.NT);
-    if (!fn) return FADE_ERR_UNSUPPORTED;
-    void* args[] = {(void*)&tp};
-    FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)Z), dim3(kTier0Threads), 0, s, args));
     return FADE_OK;
 }
 
@@ -1389,8 +1596,8 @@ extern "C" int fade_workspace_check(void* workspace, size_t ws_bytes, void* stre
     FADE_CUDA_TRY(cudaMemcpyAsync(&h, workspace, sizeof(int), cudaMemcpyDeviceToHost, s));
     FADE_CUDA_TRY(cudaStreamSynchronize(s));
     if (h != 0) {
-        const int zero = 0;
-        FADE_CUDA_TRY(cudaMemcpyAsync(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice, s));
+        // A stalled call may have left arrival counters mid-count: zero it all.
+        FADE_CUDA_TRY(cudaMemsetAsync(workspace, 0, ws_bytes, s));
         FADE_CUDA_TRY(cudaStreamSynchronize(s));
         return FADE_ERR_TIMEOUT;
     }

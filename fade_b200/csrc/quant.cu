@@ -319,12 +319,24 @@ __global__ void age_out_int4_kernel(typename Elem<DT>::T* __restrict__ ring_k,
     const int b = blockIdx.x;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
     const int64_t n = mid_len[b];
+    griddep_launch_dependents();
     const bool room = n < mid_cap;
     int64_t slot = (n - ring_origin) % ring_cap;
     if (slot < 0) slot += ring_cap;
     for (int h = warp; h < H; h += nw) {
         auto* ks = ring_k + b * ring_sb + h * ring_sh + slot * D;
         auto* vs = ring_v + b * ring_sb + h * ring_sh + slot * D;
+        // the new token does not depend on the slot: fetch it first
+        typename Elem<DT>::T kn_r[8], vn_r[8];
+        if (k_new) {
+            const auto* kn = k_new + b * new_sb + h * new_sh;
+            const auto* vn = v_new + b * new_sb + h * new_sh;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int d = lane + 32 * i;
+                if (d < D) { kn_r[i] = kn[d]; vn_r[i] = vn[d]; }
+            }
+        }
         if (room) {
             const auto* sc = k_scale + ((int64_t)b * H + h) * D;
             const int64_t row = b * mid_sb + h * mid_sh + n;
@@ -351,17 +363,15 @@ __global__ void age_out_int4_kernel(typename Elem<DT>::T* __restrict__ ring_k,
         }
         __syncwarp();
         if (k_new && room) {
-            const auto* kn = k_new + b * new_sb + h * new_sh;
-            const auto* vn = v_new + b * new_sb + h * new_sh;
-            for (int d = lane; d < D; d += 32) {
-                ks[d] = kn[d];
-                vs[d] = vn[d];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int d = lane + 32 * i;
+                if (d < D) { ks[d] = kn_r[i]; vs[d] = vn_r[i]; }
             }
         }
     }
     __syncthreads();
     if (threadIdx.x == 0 && room) mid_len[b] = (int32_t)(n + 1);
-    griddep_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -574,24 +584,28 @@ extern "C" int fade_age_out_int4(void* ring_k, void* ring_v, int dtype, int64_t 
     if (!ring_k || !ring_v || !k_packed || !v_packed || !v_scale || !k_scale || !mid_len)
         return FADE_ERR_INVALID_ARG;
     if ((k_new == nullptr) != (v_new == nullptr)) return FADE_ERR_INVALID_ARG;
+    if (D > 256) return FADE_ERR_UNSUPPORTED;
     const int threads = (int)(H < 8 ? (H < 1 ? 1 : H) : 8) * 32;
     cudaStream_t st = as_stream(stream);
-    switch (dtype) {
-        case FADE_F16:
-            age_out_int4_kernel<FADE_F16><<<(unsigned)B, threads, 0, st>>>(
-                (__half*)ring_k, (__half*)ring_v, (int)H, (int)D, ring_cap, ring_sb, ring_sh,
-                ring_origin, k_packed, v_packed, (__half*)v_scale, (const __half*)k_scale, mid_sb,
-                mid_sh, mid_cap, mid_len, (const __half*)k_new, (const __half*)v_new, new_sb, new_sh);
-            break;
-        case FADE_BF16:
-            age_out_int4_kernel<FADE_BF16><<<(unsigned)B, threads, 0, st>>>(
-                (__nv_bfloat16*)ring_k, (__nv_bfloat16*)ring_v, (int)H, (int)D, ring_cap, ring_sb,
-                ring_sh, ring_origin, k_packed, v_packed, (__nv_bfloat16*)v_scale,
-                (const __nv_bfloat16*)k_scale, mid_sb, mid_sh, mid_cap, mid_len,
-                (const __nv_bfloat16*)k_new, (const __nv_bfloat16*)v_new, new_sb, new_sh);
-            break;
-        default: return FADE_ERR_INVALID_ARG;
-    }
-    FADE_LAUNCH_CHECK();
+    void* fn;
+    if (dtype == FADE_F16) fn = (void*)&age_out_int4_kernel<FADE_F16>;
+    else if (dtype == FADE_BF16) fn = (void*)&age_out_int4_kernel<FADE_BF16>;
+    else return FADE_ERR_INVALID_ARG;
+    int Hi = (int)H, Di = (int)D;
+    void* args[] = {&ring_k, &ring_v, &Hi, &Di, &ring_cap, &ring_sb, &ring_sh, &ring_origin,
+                    &k_packed, &v_packed, &v_scale, (void*)&k_scale, &mid_sb, &mid_sh, &mid_cap,
+                    &mid_len, (void*)&k_new, (void*)&v_new, &new_sb, &new_sh};
+    // programmatic dependent launch: the kernel waits (griddepcontrol.wait)
+    // for the previous grid before touching memory, so only its launch overlaps
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)B);
+    cfg.blockDim = dim3((unsigned)threads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    FADE_CUDA_TRY(cudaLaunchKernelExC(&cfg, fn, args));
     return FADE_OK;
 }

@@ -228,8 +228,8 @@ typedef struct fade_decode_desc {
 } fade_decode_desc;
 
 /* Bytes of zero-initialised workspace fade_decode_attn needs for `d`.  The
- * workspace carries split-K partials and an error word; it never needs
- * re-zeroing between calls. */
+ * workspace carries split-K partials, per-row arrival counters (reset by
+ * every call) and an error word; zero-fill it once when allocating it. */
 size_t fade_decode_attn_workspace_size(const fade_decode_desc* d);
 
 /* Attention of q over the union of all segments' tokens (order-free):

@@ -58,7 +58,8 @@ def dtype_ulp(x: np.ndarray, dt: str) -> np.ndarray:
     return np.maximum(2.0 ** (e - mb), tiny)
 
 
-def assert_attn_close(out: np.ndarray, ref: np.ndarray, dt: str, atol: float) -> float:
+def assert_attn_close(out: np.ndarray, ref: np.ndarray, dt: str, atol: float, ulps: float = 1.0,
+                      additive: bool = False) -> float:
     """Attention parity criterion: |out - ref| <= max(atol, 1 ulp of the output
     dtype at |ref|) element-wise.  atol is the north-star tolerance (2e-3 fp16,
     1e-2 bf16); the ulp term is the unavoidable rounding of a result stored in
@@ -67,7 +68,8 @@ def assert_attn_close(out: np.ndarray, ref: np.ndarray, dt: str, atol: float) ->
     in fp16 or >= 2 in bf16).  Returns the worst err / limit."""
     out = np.asarray(out, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
-    lim = np.maximum(atol, dtype_ulp(ref, dt))
+    u = ulps * dtype_ulp(ref, dt)
+    lim = atol + u if additive else np.maximum(atol, u)
     ratio = np.abs(out - ref) / lim
     worst = float(ratio.max()) if ratio.size else 0.0
     assert worst <= 1.0, f"max |out-ref| {np.abs(out - ref).max():.3e}, worst err/limit {worst:.3f}"

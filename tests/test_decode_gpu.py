@@ -80,8 +80,13 @@ def test_rot2_golden(cuda_device):
         FPTier(_fp(g, "recent_k", dt), _fp(g, "recent_v", dt)),
     ]
     out = t_vals(tiered_decode_attention(q, tiers))
-    assert_attn_close(out, from_bits(g["out_ref"], dt), dt, TOL[dt])
-    assert_attn_close(out, g["out_ref32"].view(np.float32), dt, TOL[dt])
+    # The reference dequantises in the rotated basis, rotates back in fp32 and
+    # rounds the un-rotated K/V to bf16 (fade/rotated_quant.py:134-187); the
+    # fused kernel works in the rotated basis (q_rot = q R^T, out = o_rot R), so
+    # that last per-element rounding cannot be reproduced: allow atol + 2 output
+    # ulps (exact rotated-basis math already sits at ~0.6 of this bound).
+    assert_attn_close(out, from_bits(g["out_ref"], dt), dt, TOL[dt], ulps=2, additive=True)
+    assert_attn_close(out, g["out_ref32"].view(np.float32), dt, TOL[dt], ulps=2, additive=True)
 
 
 def _random_int4_case(B, Hq, Hkv, D, n_sink, n_mid, n_rec, dt, seed, n_q=1):
