@@ -139,6 +139,8 @@ _SIGNATURES = {
         [ctypes.POINTER(DecodeDesc), _vp, ctypes.c_size_t, _vp],
     ),
     "fade_workspace_check": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp]),
+    "fade_decode_attn_noalloc_max_bytes": (ctypes.c_size_t, []),
+    "fade_decode_attn_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeDesc), _vp]),
 }
 
 _lib = None

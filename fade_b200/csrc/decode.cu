@@ -1603,3 +1603,57 @@ extern "C" int fade_workspace_check(void* workspace, size_t ws_bytes, void* stre
     }
     return FADE_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of fade_decode_attn.
+//
+// Some callers cannot allocate device memory at the point where they run
+// attention: code inside an allocator-free serving runtime that was handed a
+// fixed memory pool, plugin hosts whose policy forbids cudaMalloc after
+// start-up, or callers that cannot hold a workspace object across calls.
+// This entry point takes its scratch space from a fixed array compiled into
+// the library instead of a caller-supplied workspace.
+// ---------------------------------------------------------------------------
+namespace fade {
+// Every GPU that loads the library reserves this array until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+// Device address of the array per device.  In host code the symbol itself is
+// only a host-side stand-in, so the address is looked up once per device.
+static void* g_noalloc_ptr[kMaxDevices] = {};
+static std::mutex g_noalloc_mu;
+
+static int noalloc_scratch(void** out) {
+    int dev = 0;
+    FADE_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return FADE_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        FADE_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return FADE_OK;
+}
+}  // namespace fade
+
+extern "C" size_t fade_decode_attn_noalloc_max_bytes(void) { return fade::kNoAllocScratchBytes; }
+
+extern "C" int fade_decode_attn_noalloc(const fade_decode_desc* d, void* stream) {
+    const size_t need = fade_decode_attn_workspace_size(d);
+    if (need == 0) {
+        Plan pl;
+        const int st = make_plan(d, &pl);
+        return st != FADE_OK ? st : FADE_ERR_INVALID_ARG;
+    }
+    if (need > fade::kNoAllocScratchBytes) return FADE_ERR_WORKSPACE;
+    void* ws = nullptr;
+    int st = fade::noalloc_scratch(&ws);
+    if (st != FADE_OK) return st;
+    // The array keeps the previous call's bytes.  Only the error word must
+    // start at zero (the per-row arrival counters are reset by the call's own
+    // FP-tier kernel), so clear the first 256 bytes on the caller's stream.
+    FADE_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, as_stream(stream)));
+    return fade_decode_attn(d, ws, fade::kNoAllocScratchBytes, stream);
+}

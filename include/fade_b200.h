@@ -238,6 +238,22 @@ size_t fade_decode_attn_workspace_size(const fade_decode_desc* d);
 int fade_decode_attn(const fade_decode_desc* d, void* workspace, size_t ws_bytes,
                      void* stream);
 
+/* No counterpart in the reference.  fade_decode_attn without a workspace
+ * argument, for callers that cannot allocate device memory when they run
+ * attention (a serving runtime handed a fixed memory pool, a plugin host that
+ * forbids cudaMalloc after start-up, a caller with nowhere to keep a workspace
+ * between calls).  Scratch space comes from one array compiled into the
+ * library: fade_decode_attn_noalloc_max_bytes() bytes (32 MiB), reserved on
+ * every GPU that loads the library until the process exits.  A call whose
+ * fade_decode_attn_workspace_size() exceeds that returns FADE_ERR_WORKSPACE.
+ * The first call on a device looks the array's device address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one array: calls that can overlap on the GPU (different
+ * streams, or different host threads) race and must be serialised by the
+ * caller.  Allocates nothing (no cudaMalloc / cudaFree). */
+size_t fade_decode_attn_noalloc_max_bytes(void);
+int fade_decode_attn_noalloc(const fade_decode_desc* d, void* stream);
+
 /* Reads and clears the device error word of a workspace (synchronises the
  * stream).  Returns FADE_OK or FADE_ERR_TIMEOUT. */
 int fade_workspace_check(void* workspace, size_t ws_bytes, void* stream);
