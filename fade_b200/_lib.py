@@ -10,6 +10,7 @@ CPU tensor raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -155,6 +156,8 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     with _lock:
         if _lib is not None and path is None:
             return _lib
+        if path is None and os.environ.get("FADE_LIB_PATH"):
+            path = os.environ["FADE_LIB_PATH"]   # alternative build (profiling)
         p = Path(path) if path is not None else LIB_PATH
         if not p.exists():
             raise RuntimeError(
@@ -166,8 +169,7 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if path is None:
-            _lib = lib
+        _lib = lib
         return lib
 
 

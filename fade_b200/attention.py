@@ -103,6 +103,25 @@ def _fill_fp(seg: _lib.KVSegment, tier: FPTier, D: int) -> list:
     return [tier.k, tier.v, tier.lens]
 
 
+def _pad_rows(t: Tensor, S_pad: int) -> Tensor:
+    B, H, S = t.shape[:3]
+    out = torch.zeros((B, H, S_pad) + tuple(t.shape[3:]), dtype=t.dtype, device=t.device)
+    out[:, :, :S] = t
+    return out
+
+
+def _row_aligned(tier, rbk: int, rbv: int) -> bool:
+    """The middle kernel streams codes as 128-byte rows: every (b, h) segment must
+    start on one and the arrays must end on one."""
+    tpr = 128 // min(rbk, rbv)
+    for t, rb in ((tier.k_packed, rbk), (tier.v_packed, rbv)):
+        if t.stride(-1) != 1 or t.stride(2) != rb or t.stride(0) % (rb * tpr) or t.stride(1) % (rb * tpr):
+            return False
+        if t.storage_offset() % 128 or (_rows_available(t, rb) * rb) % 128:
+            return False
+    return True
+
+
 def _fill_mid(seg: _lib.KVSegment, tier, D: int, dtype: torch.dtype) -> list:
     if isinstance(tier, Int4Tier):
         seg.kind, kb, vb = _lib.SEG_INT4, 4, 4
@@ -115,6 +134,26 @@ def _fill_mid(seg: _lib.KVSegment, tier, D: int, dtype: torch.dtype) -> list:
     else:
         raise TypeError(f"unknown tier {type(tier)}")
     rbk, rbv = D * kb // 8, D * vb // 8
+    if not _row_aligned(tier, rbk, rbv) and tier.lens is None:
+        # copy into a padded layout the kernel can stream (sequence padded to 128)
+        import dataclasses
+
+        S = tier.k_packed.shape[2]
+        S_pad = -(-S // 128) * 128
+        length = getattr(tier, "length", None)
+        changes = dict(k_packed=_pad_rows(tier.k_packed, S_pad), v_packed=_pad_rows(tier.v_packed, S_pad))
+        if isinstance(tier, Int4K2VTier):
+            G = int(tier.group)
+            changes["v_scale"] = _pad_rows(tier.v_scale, S_pad // G)
+        else:
+            changes["v_scale"] = _pad_rows(tier.v_scale, S_pad)
+        if isinstance(tier, Int4K2VTier):
+            changes["length"] = length if length is not None else S
+        elif isinstance(tier, (Int4Tier, RotTier)):
+            changes["max_len"] = tier.max_len if tier.max_len is not None else S
+        tier = dataclasses.replace(tier, **changes)
+        if isinstance(tier, (Int4Tier, RotTier)) and tier.lens is None:
+            seg.len = S
     sb, sh = _row_strides(tier.k_packed, rbk, "middle k codes")
     if _row_strides(tier.v_packed, rbv, "middle v codes") != (sb, sh):
         raise ValueError("middle K and V codes must share a row layout")
@@ -138,11 +177,14 @@ def _fill_mid(seg: _lib.KVSegment, tier, D: int, dtype: torch.dtype) -> list:
     seg.v_scale = vs.data_ptr()
     S = tier.k_packed.shape[2]
     length = getattr(tier, "length", None)
+    if length is None and isinstance(tier, (Int4Tier, RotTier)) and tier.max_len is not None and tier.lens is None:
+        length = tier.max_len          # padded copy: the valid length is the original S
     seg.len = int(length) if length is not None else S
     seg.max_len = int(tier.max_len) if getattr(tier, "max_len", None) is not None else seg.len
     if tier.lens is not None:
         seg.lens = tier.lens.data_ptr()
-    seg.n_rows = min(_rows_available(tier.k_packed, rbk), _rows_available(tier.v_packed, rbv))
+    tpr = 128 // min(rbk, rbv)
+    seg.n_rows = min(_rows_available(tier.k_packed, rbk), _rows_available(tier.v_packed, rbv)) // tpr * tpr
     keep = [tier.k_packed, tier.v_packed, ks, vs, tier.lens]
     if isinstance(tier, RotTier):
         keep.append(tier.rotation)

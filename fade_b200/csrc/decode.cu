@@ -36,6 +36,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -43,6 +45,29 @@
 
 namespace fade {
 
+// Ablation switch for profiling builds only (default 0 = full kernel):
+// 1 = consumers only cycle the pipeline, 2 = QK^T only, 3 = no scale multiply,
+// 4 = as 1 without the L2 cache hint, 5 = as 1 without the scale copy,
+// 6 = as 1 without per-row setup / flush / merge.
+#ifndef FADE_ABLATE
+#define FADE_ABLATE 0
+#endif
+// Timeline tracing for profiling builds only (FADE_TRACE defined): per CTA
+// event timestamps into a device array read back by fade_trace_read().
+#ifdef FADE_TRACE
+constexpr int kTraceEv = 96;
+__device__ unsigned long long g_trace[1024 * kTraceEv];
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+#define FADE_TR(slot) do { if (threadIdx.x == 0 && blockIdx.x < 1024 && (slot) < kTraceEv) g_trace[blockIdx.x * kTraceEv + (slot)] = gtimer(); } while (0)
+#define FADE_TRP(slot) do { if (threadIdx.x == kConsumerWarps * 32 && blockIdx.x < 1024 && (slot) < kTraceEv) g_trace[blockIdx.x * kTraceEv + (slot)] = gtimer(); } while (0)
+#else
+#define FADE_TR(slot) do {} while (0)
+#define FADE_TRP(slot) do {} while (0)
+#endif
 constexpr int kConsumerWarps = 4;
 constexpr int kMidThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
@@ -159,6 +184,7 @@ template <> struct Pk<FADE_F16> {
         return d;
     }
     __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+        if (FADE_ABLATE == 3) return a ^ (b & 1u);
         uint32_t d;
         asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
         return d;
@@ -189,6 +215,7 @@ template <> struct Pk<FADE_BF16> {
         return d;
     }
     __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+        if (FADE_ABLATE == 3) return a ^ (b & 1u);
         uint32_t d;
         asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
         return d;
@@ -354,16 +381,13 @@ struct MidLayout {
     static_assert(K_BYTES % 1024 == 0 && V_BYTES % 1024 == 0, "stage regions must stay 1 KB aligned");
     static constexpr int SC_BASE = kStages * STAGE_BYTES;
     static constexpr int RING_BYTES = SC_BASE + kStages * SC_BYTES;
-    static constexpr int OBUF_BYTES = NT * 8 * D * 4;
+    static constexpr int OBUF_BYTES = (NT * 8 * D * 4 > 4096) ? NT * 8 * D * 4 : 4096;  // >= merge scratch
     static constexpr int ML_BYTES = kConsumerWarps * 16 * 2 * 4;
     static constexpr int BAR_OFF = RING_BYTES + OBUF_BYTES + ML_BYTES;
     static constexpr int FLAG_OFF = BAR_OFF + 2 * kStages * 8;
     static constexpr int SMEM_BYTES = FLAG_OFF + 16 + 1024;  // +1024 for alignment
 };
 
-__device__ __forceinline__ uint32_t swz(uint32_t off, uint32_t smask) {
-    return off ^ (((off >> 7) & smask) << 4);
-}
 
 template <int DT>
 __device__ __forceinline__ float load_f(const void* p, int64_t i) {
@@ -378,19 +402,30 @@ __device__ __forceinline__ uint32_t dup16(uint16_t v) { return (uint32_t)v | ((u
 
 // Load the 2*NCH ldmatrix tiles (token block tb, 16-byte chunk cb) of one
 // 16-token m-tile: r[tb][cb].  TRANS selects the transposing form (V).
+// Stage tiles hold packed token rows of NCH*16 bytes, 128/(NCH*16) tokens per
+// 128-byte shared-memory row, swizzled by the TMA unit's 128B pattern
+// (16-byte chunk c of row R lands at chunk c ^ (R & 7)): every 8-row ldmatrix
+// read below touches 8 distinct bank groups.
+template <int NCH>
+__device__ __forceinline__ uint32_t tile_off(int tok, int cb) {
+    constexpr int TPR = 8 / NCH;  // tokens per 128-byte row
+    const int row = tok / TPR;
+    const int chunk = (tok % TPR) * NCH + cb;
+    return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
 template <int NCH, bool TRANS>
-__device__ __forceinline__ void load_tiles(uint32_t base, int trow0, int rb, uint32_t smask, int lane,
-                                           uint32_t (&r)[2][NCH]) {
+__device__ __forceinline__ void load_tiles(uint32_t base, int trow0, int lane, uint32_t (&r)[2][NCH]) {
     constexpr int NMAT = 2 * NCH;
     if constexpr (NMAT >= 4) {
 #pragma unroll
         for (int x = 0; x < NMAT / 4; ++x) {
             const int mi = x * 4 + lane / 8;
             const int tb = mi / NCH, cb = mi % NCH;
-            const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * rb + cb * 16);
+            const uint32_t off = tile_off<NCH>(trow0 + tb * 8 + (lane & 7), cb);
             uint32_t r4[4];
-            if constexpr (TRANS) ldsm_x4_t(base + swz(off, smask), r4);
-            else ldsm_x4(base + swz(off, smask), r4);
+            if constexpr (TRANS) ldsm_x4_t(base + off, r4);
+            else ldsm_x4(base + off, r4);
 #pragma unroll
             for (int y = 0; y < 4; ++y) {
                 const int mj = x * 4 + y;
@@ -399,10 +434,10 @@ __device__ __forceinline__ void load_tiles(uint32_t base, int trow0, int rb, uin
         }
     } else {
         const int tb = (lane / 8) & 1;
-        const uint32_t off = (uint32_t)((trow0 + tb * 8 + (lane & 7)) * rb);
+        const uint32_t off = tile_off<NCH>(trow0 + tb * 8 + (lane & 7), 0);
         uint32_t r2[2];
-        if constexpr (TRANS) ldsm_x2_t(base + swz(off, smask), r2);
-        else ldsm_x2(base + swz(off, smask), r2);
+        if constexpr (TRANS) ldsm_x2_t(base + off, r2);
+        else ldsm_x2(base + off, r2);
         r[0][0] = r2[0];
         r[1][0] = r2[1];
     }
@@ -454,11 +489,13 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     __syncthreads();
+    FADE_TR(0);
     // Inputs may be produced by the previous kernel in the stream (age-out,
     // query rotation): wait for it before touching global memory, then let the
     // next kernel in the stream start its prologue.
     griddep_wait();
     griddep_launch_dependents();
+    FADE_TR(1);
     if (ub >= ue) return;
 
     if (warp == kConsumerWarps) {
@@ -483,12 +520,23 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             // Units past this row's length (uniform grid over a capacity bound)
             // carry no tokens: complete the stage without a copy.
             uint8_t* scs = smem + L::SC_BASE + s * L::SC_BYTES;
+            FADE_TRP(40 + i);
             if (lane == 0 && tok0 < len) {
-                const uint32_t sc_bytes = p.scale_tma ? (uint32_t)L::sc_box_bytes(p.group) : 0u;
+                const uint32_t sc_bytes = (p.scale_tma && FADE_ABLATE != 5) ? (uint32_t)L::sc_box_bytes(p.group) : 0u;
                 mbar_expect_tx(full_bar(s), (uint32_t)(L::K_BYTES + L::V_BYTES) + sc_bytes);
-                tma_load_2d(smem_u32(st + L::K_OFF), &tmap_k, 0, (int)row0, full_bar(s), policy);
-                tma_load_2d(smem_u32(st + L::V_OFF), &tmap_v, 0, (int)row0, full_bar(s), policy);
-                if (p.scale_tma) {
+                // maps address 128-byte rows: token row0 starts at row0*RB/128
+#if FADE_ABLATE == 4
+                asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                             ::"r"(smem_u32(st + L::K_OFF)), "l"(reinterpret_cast<uint64_t>(&tmap_k)), "r"(0),
+                             "r"((int)(row0 * L::RBK / 128)), "r"(full_bar(s)) : "memory");
+                asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                             ::"r"(smem_u32(st + L::V_OFF)), "l"(reinterpret_cast<uint64_t>(&tmap_v)), "r"(0),
+                             "r"((int)(row0 * L::RBV / 128)), "r"(full_bar(s)) : "memory");
+#else
+                tma_load_2d(smem_u32(st + L::K_OFF), &tmap_k, 0, (int)(row0 * L::RBK / 128), full_bar(s), policy);
+                tma_load_2d(smem_u32(st + L::V_OFF), &tmap_v, 0, (int)(row0 * L::RBV / 128), full_bar(s), policy);
+#endif
+                if (p.scale_tma && FADE_ABLATE != 5) {
                     // per-token: 1-D map over rows; grouped: 2-D map [groups][D].
                     // Past the map's extent the TMA unit writes zeros.
                     if constexpr (!VGROUP) tma_load_1d(smem_u32(scs), &tmap_s, (int)row0, full_bar(s), policy);
@@ -642,44 +690,79 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // Merge of row z (runs in the CTA whose arrival completed z): obuf and
     // mlbuf are free again here.  Partial of CTA c lives at unit max(zb, ub(c)).
     auto merge = [&](int z, int zb, int c0, int c1) {
+        // Runs in the CTA whose arrival completed row z (usually at the very end
+        // of the kernel, so its latency is the kernel's tail): every partial
+        // statistic is fetched with independent loads into shared memory, then
+        // each output element reads all partials at once.
+        constexpr int KCH = 32;                  // slots handled through smem
         const int rows = p.rows;
+        const int nsl = c1 - c0 + 1;
         float* Mr = mlbuf;            // [16] row max
         float* Lr = mlbuf + 16;       // [16] 1 / row sum
         float* Fw = mlbuf + 32;       // [16] weight of the FP partial
+        float* sw = obuf;             // [KCH][16] slot max -> weight
+        float* sl_ = obuf + KCH * 16; // [KCH][16] slot sum
+        auto slot_of = [&](int j) {
+            const int ucc = (int)((int64_t)(c0 + j) * U / C);
+            return ucc > zb ? ucc : zb;
+        };
+        const bool fast = nsl <= KCH;
+        if (fast) {
+            for (int idx = ctid; idx < nsl * rows; idx += kConsumerWarps * 32) {
+                const int j = idx / rows, r = idx % rows;
+                const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + ((int64_t)slot_of(j) * rows + r) * 2);
+                sw[j * 16 + r] = ml.x;
+                sl_[j * 16 + r] = ml.y;
+            }
+            named_bar_sync(1, kConsumerWarps * 32);
+        }
         if (ctid < rows) {
             const int r = ctid;
-            float M = -INFINITY;
-            const float fm = p.fp_ml ? p.fp_ml[((int64_t)z * rows + r) * 2] : -INFINITY;
-            M = fmaxf(M, fm);
-            for (int cc = c0; cc <= c1; ++cc) {
-                const int ucc = (int)((int64_t)cc * U / C);
-                const int sl = ucc > zb ? ucc : zb;
-                M = fmaxf(M, p.ws_ml[((int64_t)sl * rows + r) * 2]);
-            }
-            float Ls = 0.f;
-            const float fw = (fm == -INFINITY) ? 0.f : ex2(fm - M);
-            if (p.fp_ml) Ls += fw * p.fp_ml[((int64_t)z * rows + r) * 2 + 1];
-            for (int cc = c0; cc <= c1; ++cc) {
-                const int ucc = (int)((int64_t)cc * U / C);
-                const int sl = ucc > zb ? ucc : zb;
-                const float ms = p.ws_ml[((int64_t)sl * rows + r) * 2];
-                if (ms != -INFINITY) Ls += ex2(ms - M) * p.ws_ml[((int64_t)sl * rows + r) * 2 + 1];
+            const float2 fml = p.fp_ml ? *reinterpret_cast<const float2*>(p.fp_ml + ((int64_t)z * rows + r) * 2)
+                                       : make_float2(-INFINITY, 0.f);
+            float M = fml.x;
+            for (int j = 0; j < nsl; ++j)
+                M = fmaxf(M, fast ? sw[j * 16 + r] : p.ws_ml[((int64_t)slot_of(j) * rows + r) * 2]);
+            const float fw = (fml.x == -INFINITY) ? 0.f : ex2(fml.x - M);
+            float Ls = fw * fml.y;
+            for (int j = 0; j < nsl; ++j) {
+                const float ms = fast ? sw[j * 16 + r] : p.ws_ml[((int64_t)slot_of(j) * rows + r) * 2];
+                const float ls = fast ? sl_[j * 16 + r] : p.ws_ml[((int64_t)slot_of(j) * rows + r) * 2 + 1];
+                const float w = (ms == -INFINITY) ? 0.f : ex2(ms - M);
+                Ls += w * ls;
+                if (fast) sw[j * 16 + r] = w;
             }
             Mr[r] = M;
             Lr[r] = Ls > 0.f ? 1.f / Ls : 0.f;
             Fw[r] = fw;
         }
         named_bar_sync(1, kConsumerWarps * 32);
-        for (int i = ctid; i < rows * D; i += kConsumerWarps * 32) {
+        constexpr int PER = NT * 8 * D / (kConsumerWarps * 32);   // outputs per thread (upper bound)
+        float acc[PER];
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            const int i = ctid + k * kConsumerWarps * 32;
+            acc[k] = 0.f;
+            if (i >= rows * D) continue;
             const int r = i / D;
-            float acc = 0.f;
-            for (int cc = c0; cc <= c1; ++cc) {
-                const int ucc = (int)((int64_t)cc * U / C);
-                const int sl = ucc > zb ? ucc : zb;
-                const float ms = p.ws_ml[((int64_t)sl * rows + r) * 2];
-                if (ms != -INFINITY) acc = fmaf(ex2(ms - Mr[r]), p.ws_o[(int64_t)sl * rows * D + i], acc);
+            if (fast) {
+#pragma unroll 8
+                for (int j = 0; j < nsl; ++j) {
+                    const float w = sw[j * 16 + r];
+                    if (w != 0.f) acc[k] = fmaf(w, p.ws_o[(int64_t)slot_of(j) * rows * D + i], acc[k]);
+                }
+            } else {
+                for (int j = 0; j < nsl; ++j) {
+                    const float ms = p.ws_ml[((int64_t)slot_of(j) * rows + r) * 2];
+                    if (ms != -INFINITY) acc[k] = fmaf(ex2(ms - Mr[r]), p.ws_o[(int64_t)slot_of(j) * rows * D + i], acc[k]);
+                }
             }
-            obuf[i] = acc;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            const int i = ctid + k * kConsumerWarps * 32;
+            if (i < rows * D) obuf[i] = acc[k];
         }
         named_bar_sync(1, kConsumerWarps * 32);
         const int b = z / p.Hkv, h = z % p.Hkv;
@@ -781,33 +864,39 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         named_bar_sync(1, kConsumerWarps * 32);
         if (*merge_flag) {
             __threadfence();
+            FADE_TR(38);
             merge(z, zb, c0, c1);
+            FADE_TR(39);
         }
         named_bar_sync(1, kConsumerWarps * 32);
     };
 
     int z = z_of_unit(p, Z, ub);
     int zb = units_begin(p, z), ze = units_begin(p, z + 1);
-    const uint32_t smask_k = (uint32_t)(L::NCHK - 1);
-    const uint32_t smask_v = (uint32_t)(L::NCHV - 1);
 
     for (int u = ub, i = 0; u < ue; ++u, ++i) {
         while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
         if (z != cur_z) {
-            if (cur_z >= 0) flush(cur_z);
-            setup_z(z);
+            if (FADE_ABLATE != 6) {
+                FADE_TR(2 + 3 * (cur_z >= 0 ? 1 : 0));
+                if (cur_z >= 0) flush(cur_z);
+                FADE_TR(3 + 3 * (cur_z >= 0 ? 1 : 0));
+                setup_z(z);
+                FADE_TR(4 + 3 * (cur_z >= 0 ? 1 : 0));
+            }
             cur_z = z;
         }
         const int s = i % kStages;
         const uint32_t ph = (uint32_t)(i / kStages) & 1u;
         const bool ready = mbar_wait(full_bar(s), ph, abort_flag, p.ws_err);
+        FADE_TR(10 + i);
         const int64_t tok_w = (int64_t)(u - zb) * kStageTokens + warp * 32;  // first token of this warp
         const uint8_t* st = smem + s * L::STAGE_BYTES;
         const uint32_t kbase = smem_u32(st + L::K_OFF);
         const uint32_t vbase = smem_u32(st + L::V_OFF);
         const uint8_t* scb = smem + L::SC_BASE + s * L::SC_BYTES;
 
-        if (ready && tok_w < cur_len) {
+        if (ready && tok_w < cur_len && FADE_ABLATE != 1 && FADE_ABLATE < 4) {
             // ---- S^T = K_deq . q^T for the warp's 2 m-tiles ----
             // two accumulators per m-tile (even / odd k-steps) halve the
             // dependent MMA chain; summed before the softmax
@@ -819,7 +908,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 #pragma unroll
                     for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = sacc2[mt][nt][e] = 0.f;
                 uint32_t kr[2][L::NCHK];
-                load_tiles<L::NCHK, false>(kbase, warp * 32 + mt * 16, L::RBK, smask_k, lane, kr);
+                load_tiles<L::NCHK, false>(kbase, warp * 32 + mt * 16, lane, kr);
 #pragma unroll
                 for (int cb = 0; cb < L::NCHK; ++cb) {
                     if constexpr (KB == 4) {
@@ -913,10 +1002,10 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             }
             // ---- O^T += V_deq^T . P^T ----
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
+            for (int mt = 0; mt < (FADE_ABLATE == 2 ? 0 : 2); ++mt) {
                 const int trow0 = warp * 32 + mt * 16;
                 uint32_t vr[2][L::NCHV];
-                load_tiles<L::NCHV, true>(vbase, trow0, L::RBV, smask_v, lane, vr);
+                load_tiles<L::NCHV, true>(vbase, trow0, lane, vr);
                 // tokens of this m-tile past the length: their scales may be
                 // stale bytes (NaN * 0 must not reach the MMA), so zero them;
                 // a tile entirely past the length is skipped.
@@ -1000,7 +1089,9 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(s));
     }
-    if (cur_z >= 0) flush(cur_z);
+    FADE_TR(36);
+    if (cur_z >= 0 && FADE_ABLATE != 6) flush(cur_z);
+    FADE_TR(37);
 }
 
 // ---------------------------------------------------------------------------
@@ -1254,21 +1345,23 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+// Packed code rows (row_bytes = 16..128 per token) are addressed as 128-byte
+// rows holding 128/row_bytes tokens each: one stage (kStageTokens tokens) is a
+// box of row_bytes 128-byte rows, copied with the 128B swizzle.  Narrower
+// boxes (one 64- or 32-byte row per token) made the copy engine issue small
+// requests and capped the stream well below HBM bandwidth.
 static int make_row_map(CUtensorMap* m, const void* base, int64_t n_rows, int row_bytes) {
     auto enc = encode_fn();
     if (!enc) return FADE_ERR_CUDA;
-    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
-    if (row_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
-    else if (row_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
-    else if (row_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
-    else if (row_bytes != 16) return FADE_ERR_UNSUPPORTED;
-    cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)n_rows};
-    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-    cuuint32_t box[2] = {(cuuint32_t)row_bytes, (cuuint32_t)kStageTokens};
+    if (row_bytes != 16 && row_bytes != 32 && row_bytes != 64 && row_bytes != 128) return FADE_ERR_UNSUPPORTED;
+    if ((n_rows * row_bytes) % 128 != 0) return FADE_ERR_ALIGN;
+    cuuint64_t dims[2] = {128, (cuuint64_t)(n_rows * row_bytes / 128)};
+    cuuint64_t strides[1] = {128};
+    cuuint32_t box[2] = {128, (cuuint32_t)(kStageTokens * row_bytes / 128)};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? FADE_OK : FADE_ERR_ALIGN;
 }
 
@@ -1540,6 +1633,11 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
         }
         if (n_rows <= 0) n_rows = 1;
         if (n_rows >= ((int64_t)1 << 31)) return FADE_ERR_UNSUPPORTED;
+        // every (b, h) segment must start on a 128-byte row of both code arrays
+        {
+            const int tpr = 128 / (rbk < rbv ? rbk : rbv);
+            if (sg.row_sb % tpr || sg.row_sh % tpr) return FADE_ERR_ALIGN;
+        }
         if ((st = make_row_map(&tk, sg.k, n_rows, rbk)) != FADE_OK) return st;
         if ((st = make_row_map(&tv, sg.v, n_rows, rbv)) != FADE_OK) return st;
         // V scales by TMA when every stage's first row lands on a 16-byte
@@ -1580,6 +1678,13 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
         mp.out = d->out; mp.o_sb = d->o_sb; mp.o_sh = d->o_sh; mp.o_ss = d->o_ss;
         mp.rotation = rot ? d->rotation : nullptr;
         mp.scale_tma = scale_tma;
+        if (std::getenv("FADE_DEBUG_PLAN")) {
+            std::fprintf(stderr,
+                         "[fade] decode plan: B=%d Hq=%d Hkv=%d D=%d rows=%d kb=%d vb=%d grouped=%d "
+                         "units/z=%d ctas=%d occ=%d smem=%d scale_tma=%d n_rows=%lld\n",
+                         d->B, d->Hq, d->Hkv, d->D, pl.rows, pl.kb, pl.vb, (int)pl.vg, pl.units_per_z,
+                         pl.n_ctas, pl.mk.occ, pl.mk.smem, scale_tma, (long long)n_rows);
+        }
         mp.q_vec = aligned16(sg.k_scale) && sg.ks_sb % 8 == 0 && sg.ks_sh % 8 == 0 &&
                    (rot || (aligned16(d->q) && d->q_sb % 8 == 0 && d->q_sh % 8 == 0 && d->q_ss % 8 == 0));
         void* args[] = {(void*)&tk, (void*)&tv, (void*)&ts, (void*)&mp};
@@ -1657,3 +1762,15 @@ extern "C" int fade_decode_attn_noalloc(const fade_decode_desc* d, void* stream)
     FADE_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, as_stream(stream)));
     return fade_decode_attn(d, ws, fade::kNoAllocScratchBytes, stream);
 }
+
+#ifdef FADE_TRACE
+extern "C" int fade_trace_read(unsigned long long* host, size_t n) {
+    const size_t bytes = n * sizeof(unsigned long long) < sizeof(fade::g_trace) ? n * sizeof(unsigned long long)
+                                                                               : sizeof(fade::g_trace);
+    return cudaMemcpyFromSymbol(host, fade::g_trace, bytes) == cudaSuccess ? 0 : 7;
+}
+extern "C" int fade_trace_clear(void) {
+    static unsigned long long zeros[1024 * fade::kTraceEv];
+    return cudaMemcpyToSymbol(fade::g_trace, zeros, sizeof(zeros)) == cudaSuccess ? 0 : 7;
+}
+#endif
