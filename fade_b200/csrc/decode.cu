@@ -9,13 +9,14 @@
 //
 // Launch sequence (one stream, chained with programmatic dependent launch):
 //   k0  rotate_queries   (only with a rotated tier): q_rot = q @ R^T, fp32.
-//   kf  fp_tier_kernel   one CTA per (b, kv-head): attention over the FP
-//                        sink/recent tiers -> an un-normalised partial (or the
-//                        final output when there is no quantised middle).
 //   k1  middle_kernel    persistent stream-K over the quantised middle; every
-//                        CTA writes one partial per (b, kv-head) it touched and
-//                        counts its arrival; the CTA that completes a row merges
-//                        the FP partial with all middle partials and writes `out`.
+//                        CTA stores one un-normalised partial per (b, kv-head)
+//                        row it touched (plain stores: no fences, counters or
+//                        waits between CTAs).
+//   k2  finish_kernel    one CTA per (b, kv-head): attention over the FP
+//                        sink/recent tiers while k1 drains, then (after k1
+//                        completes) the merge of that partial with the row's
+//                        middle partials -> `out`.
 //
 // k1 data path per CTA (5 warps):
 //   warp 4 (producer): 2-D TMA (cp.async.bulk.tensor, no multicast) of 128
@@ -72,7 +73,6 @@ constexpr int kConsumerWarps = 4;
 constexpr int kMidThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
 constexpr int kStages = 4;
-constexpr int kFpThreads = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polling
 
@@ -317,17 +317,11 @@ struct MidParams {
     const int32_t* cu_units;        // ragged: [Z+1]; null = uniform
     int units_per_z;                // uniform case
     int n_ctas;
-    float* ws_ml;                   // [U][rows][2]
-    float* ws_o;                    // [U][rows][D]
+    float* ws_ml;                   // [U][rows][2] partial (max, sum), log2 domain
+    float* ws_o;                    // [U][rows][D] un-normalised partial output
     int* ws_err;
-    int* counters;                  // [Z] arrivals per row (zeroed by fp_tier_kernel)
     int scale_tma;                  // V scales arrive by TMA (row starts 8-aligned)
     int q_vec;                      // q / k_scale rows allow 16-byte loads
-    const float* fp_ml;             // FP-tier partial [Z][rows][2] or null
-    const float* fp_o;              // [Z][rows][D]
-    void* out;                      // [B,Hq,n_q,D] model dtype
-    int64_t o_sb, o_sh, o_ss;
-    const float* rotation;          // rotated middle: out = fp + mid @ R
 };
 
 __device__ __forceinline__ int64_t seg_len(const MidParams& p, int b) {
@@ -381,8 +375,8 @@ struct MidLayout {
     static_assert(K_BYTES % 1024 == 0 && V_BYTES % 1024 == 0, "stage regions must stay 1 KB aligned");
     static constexpr int SC_BASE = kStages * STAGE_BYTES;
     static constexpr int RING_BYTES = SC_BASE + kStages * SC_BYTES;
-    static constexpr int OBUF_BYTES = (NT * 8 * D * 4 > 4096) ? NT * 8 * D * 4 : 4096;  // >= merge scratch
-    static constexpr int ML_BYTES = kConsumerWarps * 16 * 2 * 4;
+    static constexpr int OBUF_BYTES = 2 * NT * 8 * D * 4;                 // 2 half-sums of the CTA partial
+    static constexpr int ML_BYTES = 2 * kConsumerWarps * NT * 8 * 2 * 4;  // per-warp row stats, 2 buffers
     static constexpr int BAR_OFF = RING_BYTES + OBUF_BYTES + ML_BYTES;
     static constexpr int FLAG_OFF = BAR_OFF + 2 * kStages * 8;
     static constexpr int SMEM_BYTES = FLAG_OFF + 16 + 1024;  // +1024 for alignment
@@ -686,102 +680,14 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         cur_len = seg_len(p, b);
     };
 
-    volatile int* merge_flag = reinterpret_cast<volatile int*>(smem + L::FLAG_OFF + 4);
-    // Merge of row z (runs in the CTA whose arrival completed z): obuf and
-    // mlbuf are free again here.  Partial of CTA c lives at unit max(zb, ub(c)).
-    auto merge = [&](int z, int zb, int c0, int c1) {
-        // Runs in the CTA whose arrival completed row z (usually at the very end
-        // of the kernel, so its latency is the kernel's tail): every partial
-        // statistic is fetched with independent loads into shared memory, then
-        // each output element reads all partials at once.
-        constexpr int KCH = 32;                  // slots handled through smem
-        const int rows = p.rows;
-        const int nsl = c1 - c0 + 1;
-        float* Mr = mlbuf;            // [16] row max
-        float* Lr = mlbuf + 16;       // [16] 1 / row sum
-        float* Fw = mlbuf + 32;       // [16] weight of the FP partial
-        float* sw = obuf;             // [KCH][16] slot max -> weight
-        float* sl_ = obuf + KCH * 16; // [KCH][16] slot sum
-        auto slot_of = [&](int j) {
-            const int ucc = (int)((int64_t)(c0 + j) * U / C);
-            return ucc > zb ? ucc : zb;
-        };
-        const bool fast = nsl <= KCH;
-        if (fast) {
-            for (int idx = ctid; idx < nsl * rows; idx += kConsumerWarps * 32) {
-                const int j = idx / rows, r = idx % rows;
-                const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + ((int64_t)slot_of(j) * rows + r) * 2);
-                sw[j * 16 + r] = ml.x;
-                sl_[j * 16 + r] = ml.y;
-            }
-            named_bar_sync(1, kConsumerWarps * 32);
-        }
-        if (ctid < rows) {
-            const int r = ctid;
-            const float2 fml = p.fp_ml ? *reinterpret_cast<const float2*>(p.fp_ml + ((int64_t)z * rows + r) * 2)
-                                       : make_float2(-INFINITY, 0.f);
-            float M = fml.x;
-            for (int j = 0; j < nsl; ++j)
-                M = fmaxf(M, fast ? sw[j * 16 + r] : p.ws_ml[((int64_t)slot_of(j) * rows + r) * 2]);
-            const float fw = (fml.x == -INFINITY) ? 0.f : ex2(fml.x - M);
-            float Ls = fw * fml.y;
-            for (int j = 0; j < nsl; ++j) {
-                const float ms = fast ? sw[j * 16 + r] : p.ws_ml[((int64_t)slot_of(j) * rows + r) * 2];
-                const float ls = fast ? sl_[j * 16 + r] : p.ws_ml[((int64_t)slot_of(j) * rows + r) * 2 + 1];
-                const float w = (ms == -INFINITY) ? 0.f : ex2(ms - M);
-                Ls += w * ls;
-                if (fast) sw[j * 16 + r] = w;
-            }
-            Mr[r] = M;
-            Lr[r] = Ls > 0.f ? 1.f / Ls : 0.f;
-            Fw[r] = fw;
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
-        constexpr int PER = NT * 8 * D / (kConsumerWarps * 32);   // outputs per thread (upper bound)
-        float acc[PER];
-#pragma unroll
-        for (int k = 0; k < PER; ++k) {
-            const int i = ctid + k * kConsumerWarps * 32;
-            acc[k] = 0.f;
-            if (i >= rows * D) continue;
-            const int r = i / D;
-            if (fast) {
-#pragma unroll 8
-                for (int j = 0; j < nsl; ++j) {
-                    const float w = sw[j * 16 + r];
-                    if (w != 0.f) acc[k] = fmaf(w, p.ws_o[(int64_t)slot_of(j) * rows * D + i], acc[k]);
-                }
-            } else {
-                for (int j = 0; j < nsl; ++j) {
-                    const float ms = p.ws_ml[((int64_t)slot_of(j) * rows + r) * 2];
-                    if (ms != -INFINITY) acc[k] = fmaf(ex2(ms - Mr[r]), p.ws_o[(int64_t)slot_of(j) * rows * D + i], acc[k]);
-                }
-            }
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
-#pragma unroll
-        for (int k = 0; k < PER; ++k) {
-            const int i = ctid + k * kConsumerWarps * 32;
-            if (i < rows * D) obuf[i] = acc[k];
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
-        const int b = z / p.Hkv, h = z % p.Hkv;
-        auto* out = reinterpret_cast<typename Elem<DT>::T*>(p.out);
-        for (int i = ctid; i < rows * D; i += kConsumerWarps * 32) {
-            const int r = i / D, d = i % D;
-            float mid = obuf[i];
-            if (p.rotation) {
-                mid = 0.f;
-                for (int e = 0; e < D; ++e) mid = fmaf(obuf[r * D + e], p.rotation[(int64_t)e * D + d], mid);
-            }
-            float v = mid;
-            if (p.fp_o) v = fmaf(Fw[r], p.fp_o[(int64_t)z * rows * D + i], v);
-            v *= Lr[r];
-            const int j = r / p.n_q, sq = r % p.n_q;
-            out[(int64_t)b * p.o_sb + (int64_t)(h * p.g + j) * p.o_sh + (int64_t)sq * p.o_ss + d] = Elem<DT>::from_f(v);
-        }
-    };
-
+    // Row boundary: combine the 4 consumer warps' online-softmax states into
+    // one CTA partial and store it at the row's slot for this CTA (the first
+    // unit of the row it processed).  Plain stores only: the finisher kernel
+    // reads the partials after this grid has completed, so no fence, counter
+    // or merge sits on the streaming path.  The warps are summed in a fixed
+    // order ((w0 + w2) + (w1 + w3)): repeated calls give identical bits.
+    constexpr int MLW = NT * 8;   // rows per warp in the statistics buffer
+    int n_flush = 0;
     auto flush = [&](int z) {
         // 1) complete the per-thread row sums over the 8 token lanes
 #pragma unroll
@@ -794,19 +700,22 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 l += __shfl_xor_sync(0xffffffffu, l, 16);
                 l_run[nt][e] = l;
             }
+        // statistics alternate between two buffers: a warp can reach the next
+        // flush while threads 0..rows-1 still read this one's
+        float* mlw = mlbuf + (n_flush & 1) * (kConsumerWarps * MLW * 2);
+        ++n_flush;
         if (gid == 0) {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int r = nt * 8 + 2 * t + e;
-                    mlbuf[(warp * 16 + r) * 2 + 0] = m_run[nt][e];
-                    mlbuf[(warp * 16 + r) * 2 + 1] = l_run[nt][e];
+                    mlw[(warp * MLW + r) * 2 + 0] = m_run[nt][e];
+                    mlw[(warp * MLW + r) * 2 + 1] = l_run[nt][e];
                 }
         }
         named_bar_sync(1, kConsumerWarps * 32);
-        // 2) rescale this warp's O to the CTA max and accumulate into obuf
-        float f[NT][2];
+        // 2) rescale this warp's O to the CTA max
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -814,61 +723,60 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 const int r = nt * 8 + 2 * t + e;
                 float M = -INFINITY;
 #pragma unroll
-                for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mlbuf[(w * 16 + r) * 2]);
-                f[nt][e] = (m_run[nt][e] == -INFINITY) ? 0.f : ex2(m_run[nt][e] - M);
+                for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mlw[(w * MLW + r) * 2]);
+                const float f = (m_run[nt][e] == -INFINITY) ? 0.f : ex2(m_run[nt][e] - M);
+#pragma unroll
+                for (int mi = 0; mi < MT; ++mi) {
+                    o[nt][mi][e] *= f;
+                    o[nt][mi][e + 2] *= f;
+                }
             }
-        for (int pass = 0; pass < kConsumerWarps; ++pass) {
-            if (warp == pass) {
+        // 3) half-sums: warps 0/1 store into obuf halves 0/1, warps 2/3 add
+        //    theirs (channel pairs d, d+1 are adjacent: float2 accesses)
+        float* half = obuf + (warp & 1) * (NT * 8 * D);
+        for (int pass = 0; pass < 2; ++pass) {
+            if ((warp >> 1) == pass) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int mi = 0; mi < MT; ++mi)
+                    for (int e = 0; e < 2; ++e) {
+                        const int r = nt * 8 + 2 * t + e;
+                        if (r >= p.rows) continue;
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int r = nt * 8 + 2 * t + (e & 1);
-                            const int d = VMap::vdim(mi, e >> 1, gid);
-                            const float v = o[nt][mi][e] * f[nt][e & 1];
-                            if (pass == 0) obuf[r * D + d] = v; else obuf[r * D + d] += v;
+                        for (int mi = 0; mi < MT; ++mi) {
+                            float2* dst = reinterpret_cast<float2*>(half + r * D + VMap::vdim(mi, 0, gid));
+                            float2 v = make_float2(o[nt][mi][e], o[nt][mi][e + 2]);
+                            if (pass == 1) {
+                                const float2 a = *dst;
+                                v.x += a.x;
+                                v.y += a.y;
+                            }
+                            *dst = v;
                         }
+                    }
             }
             named_bar_sync(1, kConsumerWarps * 32);
         }
-        // 3) write the CTA partial for z to its slot: the first unit of z this
-        //    CTA processed (unique per CTA, inside z's unit range)
+        // 4) store the partial (float4 rows)
         const int zb = units_begin(p, z);
         const int slot = zb > ub ? zb : ub;
-        float* go = p.ws_o + (int64_t)slot * p.rows * D;
-        for (int i = ctid; i < p.rows * D; i += kConsumerWarps * 32) go[i] = obuf[i];
+        float4* go = reinterpret_cast<float4*>(p.ws_o + (int64_t)slot * p.rows * D);
+        const float4* h0 = reinterpret_cast<const float4*>(obuf);
+        const float4* h1 = reinterpret_cast<const float4*>(obuf + NT * 8 * D);
+        for (int i = ctid; i < p.rows * D / 4; i += kConsumerWarps * 32) {
+            const float4 a = h0[i], c = h1[i];
+            go[i] = make_float4(a.x + c.x, a.y + c.y, a.z + c.z, a.w + c.w);
+        }
         if (ctid < p.rows) {
             const int r = ctid;
             float M = -INFINITY, Ls = 0.f;
-            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mlbuf[(w * 16 + r) * 2]);
+            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mlw[(w * MLW + r) * 2]);
             for (int w = 0; w < kConsumerWarps; ++w) {
-                const float mw = mlbuf[(w * 16 + r) * 2];
-                if (mw != -INFINITY) Ls += ex2(mw - M) * mlbuf[(w * 16 + r) * 2 + 1];
+                const float mw = mlw[(w * MLW + r) * 2];
+                if (mw != -INFINITY) Ls += ex2(mw - M) * mlw[(w * MLW + r) * 2 + 1];
             }
-            p.ws_ml[((int64_t)slot * p.rows + r) * 2 + 0] = M;
-            p.ws_ml[((int64_t)slot * p.rows + r) * 2 + 1] = Ls;
+            *reinterpret_cast<float2*>(p.ws_ml + ((int64_t)slot * p.rows + r) * 2) = make_float2(M, Ls);
         }
-        // 4) count the arrival; the last CTA of row z merges every partial of
-        //    z (FP tiers + one per middle CTA) and writes the output.  No CTA
-        //    ever waits for another: the merge runs where the count completes.
-        __threadfence();
-        named_bar_sync(1, kConsumerWarps * 32);
-        const int ze = units_begin(p, z + 1);
-        const int c0 = cta_of_unit(zb, C, U), c1 = cta_of_unit(ze - 1, C, U);
-        if (ctid == 0) {
-            const int old = atomicAdd(p.counters + z, 1);
-            *merge_flag = (old == c1 - c0) ? 1 : 0;
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
-        if (*merge_flag) {
-            __threadfence();
-            FADE_TR(38);
-            merge(z, zb, c0, c1);
-            FADE_TR(39);
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
     };
 
     int z = z_of_unit(p, Z, ub);
@@ -1118,12 +1026,16 @@ __global__ void rotate_queries_kernel(const void* q, int Hq, int n_q, int D, int
 }
 
 // ---------------------------------------------------------------------------
-// k_fp: attention over the FP (model-dtype) tiers -- sinks and the recent
-// window -- one CTA per (b, kv-head).  With a quantised middle it writes an
-// un-normalised partial (m, l, O) that the middle kernel's merge consumes;
-// otherwise (or for a row with no middle units) it writes the final output.
-// Lanes of a warp take 8 tokens x 4 channel quarters for q.k (16-byte loads)
-// and own D/32 channels each for p.v (coalesced rows).
+// k2: finisher, one CTA per (b, kv-head).
+//   Prologue (runs while the middle kernel's last CTAs drain; with no middle
+//   it first waits for the previous kernel): attention over the FP tiers --
+//   sinks and recent window -- from shared-memory chunks of up to kFinChunk
+//   tokens gathered across the FP segments with 16-byte cp.async, giving an
+//   un-normalised partial (m, l, O) in log2 units.
+//   Then griddepcontrol.wait (the middle grid has completed and its partials
+//   are visible), merge with every middle partial of the row (online over
+//   chunks of kFinSlots partials), rotate the middle part back for rotated
+//   tiers (out = fp + mid @ R), normalise and write `out`.
 // ---------------------------------------------------------------------------
 struct FpSeg {
     const void* k;
@@ -1133,7 +1045,11 @@ struct FpSeg {
     const int32_t* lens;
     int64_t len;
 };
-struct FpParams {
+constexpr int kFinThreads = 256;
+constexpr int kFinChunk = 128;   // FP tokens staged per pass
+constexpr int kFinSlots = 64;    // middle partials merged per pass
+
+struct FinParams {
     int B, Hq, Hkv, D, n_q, g, rows;
     float qk_scale;
     const void* q;
@@ -1142,64 +1058,82 @@ struct FpParams {
     int64_t o_sb, o_sh, o_ss;
     int n_fp;
     FpSeg fp[FADE_MAX_SEGMENTS];
-    int has_mid;
+    int vec;                        // FP rows 16-byte aligned: cp.async staging
+    int has_mid;                    // a middle kernel precedes this one
     const int32_t* cu_units;        // middle units per row (ragged) or null
     int units_per_z;
-    float* ws_fpml;                 // [Z][rows][2]
-    float* ws_fpo;                  // [Z][rows][D]
-    int* counters;                  // [Z] middle-kernel arrival counters (zeroed here)
-    int vec;                        // FP rows 16-byte aligned: vector loads
+    int n_ctas;                     // middle grid (before clamping to the units)
+    const float* ws_ml;             // middle partials [U][rows][2]
+    const float* ws_o;              // [U][rows][D]
+    const float* rotation;          // rotated middle: [D,D] fp32, else null
 };
 
-template <int DT, int N>
-__device__ __forceinline__ void load_row_part(const typename Elem<DT>::T* src, bool vec, bool valid,
-                                              float (&dst)[N]) {
-    if (!valid) {
-#pragma unroll
-        for (int e = 0; e < N; ++e) dst[e] = 0.f;
-        return;
-    }
-    if constexpr (N % 8 == 0) {
-        if (vec) {
-#pragma unroll
-            for (int c = 0; c < N / 8; ++c) {
-                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src) + c);
-                const auto* e8 = reinterpret_cast<const typename Elem<DT>::T*>(&raw);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) dst[c * 8 + e] = Elem<DT>::to_f(e8[e]);
-            }
-            return;
-        }
-    }
-#pragma unroll
-    for (int e = 0; e < N; ++e) dst[e] = Elem<DT>::to_f(src[e]);
+template <int D, int NT>
+struct FinLayout {
+    static constexpr int ROWS = NT * 8;
+    static constexpr int KSTR = D + 8;                               // padded K row (elements)
+    static constexpr int K_OFF = 0;                                  // [chunk][KSTR] dtype
+    static constexpr int V_OFF = K_OFF + kFinChunk * KSTR * 2;       // [chunk][D] dtype
+    static constexpr int Q_OFF = V_OFF + kFinChunk * D * 2;          // [ROWS][D] f32 (x qk_scale)
+    static constexpr int P_OFF = Q_OFF + ROWS * D * 4;               // [ROWS][chunk] f32
+    static constexpr int ST_OFF = P_OFF + ROWS * kFinChunk * 4;      // row stats [4][ROWS]
+    static constexpr int SW_OFF = ST_OFF + 4 * ROWS * 4;             // [kFinSlots][ROWS] weights
+    static constexpr int SL_OFF = SW_OFF + kFinSlots * ROWS * 4;     // [kFinSlots][ROWS] sums
+    static constexpr int BYTES = SL_OFF + kFinSlots * ROWS * 4;
+    static_assert(ROWS * D * 4 <= V_OFF, "rotation scratch reuses the K region");
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 template <int DT, int D, int NT>
-__global__ void __launch_bounds__(kFpThreads)
-fp_tier_kernel(FpParams p) {
-    constexpr int ROWS = NT * 8;
-    constexpr int DPL = D / 32;      // channels per lane in p.v
-    constexpr int DQ = D / 4;        // channels per lane in q.k
-    constexpr int QS = DQ + 4;       // padded quarter stride: quarters hit different banks
-    constexpr int RS = 4 * QS;
-    constexpr int NW = kFpThreads / 32;
-    griddep_wait();
-    griddep_launch_dependents();
-    __shared__ __align__(16) float qsm[ROWS * RS];
-    __shared__ float osm[ROWS * D];
-    __shared__ float msm[NW][ROWS], lsm[NW][ROWS];
-    __shared__ float fin_m[ROWS], fin_l[ROWS];
+__global__ void __launch_bounds__(kFinThreads)
+finish_kernel(FinParams p) {
+    using L = FinLayout<D, NT>;
+    using T = typename Elem<DT>::T;
+    constexpr int ROWS = L::ROWS;
+    constexpr int D2 = D / 2;
+    constexpr int OUTS = (ROWS * D2 + kFinThreads - 1) / kFinThreads;   // (row, channel pair) per thread
+    constexpr int NW = kFinThreads / 32;
+    extern __shared__ __align__(16) uint8_t fsm[];
+    T* ksm = reinterpret_cast<T*>(fsm + L::K_OFF);
+    T* vsm = reinterpret_cast<T*>(fsm + L::V_OFF);
+    float* qsm = reinterpret_cast<float*>(fsm + L::Q_OFF);
+    float* psm = reinterpret_cast<float*>(fsm + L::P_OFF);
+    float* m_row = reinterpret_cast<float*>(fsm + L::ST_OFF);
+    float* l_row = m_row + ROWS;
+    float* c_row = m_row + 2 * ROWS;   // per-pass rescale factor
+    float* f_row = m_row + 3 * ROWS;   // final FP weight / 1 / L
+    float* sw = reinterpret_cast<float*>(fsm + L::SW_OFF);
+    float* sl = reinterpret_cast<float*>(fsm + L::SL_OFF);
 
     const int z = blockIdx.x;
     const int b = z / p.Hkv, h = z % p.Hkv;
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int rows = p.rows;
-    // The middle kernel (next in the stream, started only after this grid
-    // completes) counts arrivals per row here; start every call from zero.
-    if (threadIdx.x == 0 && p.counters) p.counters[z] = 0;
+    if (!p.has_mid) griddep_wait();
+    griddep_launch_dependents();
 
-    for (int i = threadIdx.x; i < ROWS * D; i += kFpThreads) {
+    // ---- FP segments of this row: lengths and first rows ----
+    int64_t seg_len_[FADE_MAX_SEGMENTS], seg_row_[FADE_MAX_SEGMENTS];
+    int64_t n_tok = 0;
+#pragma unroll
+    for (int s = 0; s < FADE_MAX_SEGMENTS; ++s) {
+        seg_len_[s] = 0;
+        seg_row_[s] = 0;
+        if (s < p.n_fp) {
+            const FpSeg& sg = p.fp[s];
+            seg_len_[s] = sg.lens ? (int64_t)sg.lens[b] : sg.len;
+            seg_row_[s] = sg.row_base ? sg.row_base[z] : (int64_t)b * sg.row_sb + (int64_t)h * sg.row_sh;
+            n_tok += seg_len_[s];
+        }
+    }
+    // ---- queries, pre-scaled into the log2 domain ----
+    for (int i = tid; i < ROWS * D; i += kFinThreads) {
         const int r = i / D, d = i % D;
         float v = 0.f;
         if (r < rows) {
@@ -1207,125 +1141,219 @@ fp_tier_kernel(FpParams p) {
             v = load_f<DT>(p.q, (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss + d) *
                 p.qk_scale;
         }
-        qsm[r * RS + (d / DQ) * QS + d % DQ] = v;
-        osm[i] = 0.f;
+        qsm[i] = v;
     }
-    __syncthreads();
+    if (tid < ROWS) { m_row[tid] = -INFINITY; l_row[tid] = 0.f; }
+    float acc_f[OUTS][2];
+#pragma unroll
+    for (int k = 0; k < OUTS; ++k) acc_f[k][0] = acc_f[k][1] = 0.f;
 
-    float m[ROWS], l[ROWS], o[ROWS][DPL];
+    for (int64_t t0 = 0; t0 < n_tok; t0 += kFinChunk) {
+        const int n = (int)((n_tok - t0) < kFinChunk ? (n_tok - t0) : kFinChunk);
+        __syncthreads();   // previous pass finished reading ksm / vsm / psm
+        // ---- stage K and V rows of tokens t0 .. t0+n-1 ----
+        constexpr int PCS = D / 8;   // 16-byte pieces per row
+        for (int i = tid; i < n * PCS; i += kFinThreads) {
+            const int tk = i / PCS, c = i % PCS;
+            int64_t ft = t0 + tk;
+            int s = 0;
+            while (s < p.n_fp - 1 && ft >= seg_len_[s]) { ft -= seg_len_[s]; ++s; }
+            const FpSeg& sg = p.fp[s];
+            const int64_t off = (seg_row_[s] + ft) * D + c * 8;
+            T* kd = ksm + tk * L::KSTR + c * 8;
+            T* vd = vsm + tk * D + c * 8;
+            if (p.vec) {
+                cp_async16(smem_u32(kd), reinterpret_cast<const T*>(sg.k) + off);
+                cp_async16(smem_u32(vd), reinterpret_cast<const T*>(sg.v) + off);
+            } else {
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-        m[r] = -INFINITY;
-        l[r] = 0.f;
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) o[r][e] = 0.f;
-    }
-    const int tk = lane >> 2, qd = lane & 3;
-    for (int si = 0; si < p.n_fp; ++si) {
-        const FpSeg& sg = p.fp[si];
-        const int64_t len = sg.lens ? (int64_t)sg.lens[b] : sg.len;
-        const int64_t row0 = sg.row_base ? sg.row_base[z] : (int64_t)b * sg.row_sb + (int64_t)h * sg.row_sh;
-        const auto* K = reinterpret_cast<const typename Elem<DT>::T*>(sg.k);
-        const auto* V = reinterpret_cast<const typename Elem<DT>::T*>(sg.v);
-        for (int64_t t0 = (int64_t)warp * 8; t0 < len; t0 += (int64_t)NW * 8) {
-            const int64_t tok = t0 + tk;
-            const bool tv = tok < len;
-            float kd[DQ];
-            load_row_part<DT, DQ>(K + (row0 + (tv ? tok : 0)) * D + qd * DQ, p.vec != 0, tv, kd);
-            // the group's 8 V rows are requested together with K (one latency)
-            float vv[8][DPL];
-#pragma unroll
-            for (int tt = 0; tt < 8; ++tt) {
-                const int64_t tk2 = t0 + tt;
-                const auto* vr = V + (row0 + (tk2 < len ? tk2 : 0)) * D + lane * DPL;
-#pragma unroll
-                for (int e = 0; e < DPL; ++e) vv[tt][e] = tk2 < len ? Elem<DT>::to_f(vr[e]) : 0.f;
-            }
-            float sc[ROWS];
-#pragma unroll
-            for (int r = 0; r < ROWS; ++r) {
-                const float4* qv = reinterpret_cast<const float4*>(qsm + r * RS + qd * QS);
-                float acc = 0.f;
-#pragma unroll
-                for (int e4 = 0; e4 < DQ / 4; ++e4) {
-                    const float4 q4 = qv[e4];
-                    acc = fmaf(q4.x, kd[4 * e4], acc);
-                    acc = fmaf(q4.y, kd[4 * e4 + 1], acc);
-                    acc = fmaf(q4.z, kd[4 * e4 + 2], acc);
-                    acc = fmaf(q4.w, kd[4 * e4 + 3], acc);
-                }
-                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-                sc[r] = tv ? acc : -INFINITY;
-            }
-            float pr[ROWS];
-#pragma unroll
-            for (int r = 0; r < ROWS; ++r) {
-                float mx = sc[r];
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                const float mnew = fmaxf(m[r], mx);
-                const float corr = (m[r] == -INFINITY) ? 0.f : ex2(m[r] - mnew);
-                m[r] = mnew;
-                pr[r] = (sc[r] == -INFINITY) ? 0.f : ex2(sc[r] - mnew);
-                float ps = (qd == 0) ? pr[r] : 0.f;
-                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-                l[r] = l[r] * corr + ps;
-#pragma unroll
-                for (int e = 0; e < DPL; ++e) o[r][e] *= corr;
-            }
-#pragma unroll
-            for (int tt = 0; tt < 8; ++tt) {
-#pragma unroll
-                for (int r = 0; r < ROWS; ++r) {
-                    const float pt = __shfl_sync(0xffffffffu, pr[r], tt * 4);
-#pragma unroll
-                    for (int e = 0; e < DPL; ++e) o[r][e] = fmaf(pt, vv[tt][e], o[r][e]);
+                for (int e = 0; e < 8; ++e) {
+                    kd[e] = reinterpret_cast<const T*>(sg.k)[off + e];
+                    vd[e] = reinterpret_cast<const T*>(sg.v)[off + e];
                 }
             }
         }
-    }
-    if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) { msm[warp][r] = m[r]; lsm[warp][r] = l[r]; }
-    }
-    __syncthreads();
-    if (threadIdx.x < ROWS) {
-        const int r = threadIdx.x;
-        float M = -INFINITY, Ls = 0.f;
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, msm[w][r]);
-        for (int w = 0; w < NW; ++w)
-            if (msm[w][r] != -INFINITY) Ls += ex2(msm[w][r] - M) * lsm[w][r];
-        fin_m[r] = M;
-        fin_l[r] = Ls;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-        const float f = (m[r] == -INFINITY) ? 0.f : ex2(m[r] - fin_m[r]);
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) atomicAdd(&osm[r * D + lane * DPL + e], o[r][e] * f);
-    }
-    __syncthreads();
-    int units_z = 0;
-    if (p.has_mid) units_z = p.cu_units ? p.cu_units[z + 1] - p.cu_units[z] : p.units_per_z;
-    if (units_z > 0) {
-        for (int i = threadIdx.x; i < rows * D; i += kFpThreads) p.ws_fpo[(int64_t)z * rows * D + i] = osm[i];
-        if (threadIdx.x < rows) {
-            p.ws_fpml[((int64_t)z * rows + threadIdx.x) * 2 + 0] = fin_m[threadIdx.x];
-            p.ws_fpml[((int64_t)z * rows + threadIdx.x) * 2 + 1] = fin_l[threadIdx.x];
+        cp_async_wait_all();
+        __syncthreads();
+        // ---- scores S[r][tok] = q_r . k_tok (log2 domain) ----
+        for (int i = tid; i < rows * n; i += kFinThreads) {
+            const int r = i / n, tk = i % n;
+            const uint4* kr = reinterpret_cast<const uint4*>(ksm + tk * L::KSTR);
+            const float4* qr = reinterpret_cast<const float4*>(qsm + r * D);
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
+            for (int c = 0; c < D / 8; ++c) {
+                const uint4 raw = kr[c];
+                const T* e8 = reinterpret_cast<const T*>(&raw);
+                const float4 q0 = qr[2 * c], q1 = qr[2 * c + 1];
+                a0 = fmaf(q0.x, Elem<DT>::to_f(e8[0]), a0);
+                a1 = fmaf(q0.y, Elem<DT>::to_f(e8[1]), a1);
+                a0 = fmaf(q0.z, Elem<DT>::to_f(e8[2]), a0);
+                a1 = fmaf(q0.w, Elem<DT>::to_f(e8[3]), a1);
+                a0 = fmaf(q1.x, Elem<DT>::to_f(e8[4]), a0);
+                a1 = fmaf(q1.y, Elem<DT>::to_f(e8[5]), a1);
+                a0 = fmaf(q1.z, Elem<DT>::to_f(e8[6]), a0);
+                a1 = fmaf(q1.w, Elem<DT>::to_f(e8[7]), a1);
+            }
+            psm[r * kFinChunk + tk] = a0 + a1;
         }
-    } else {
-        auto* out = reinterpret_cast<typename Elem<DT>::T*>(p.out);
-        for (int i = threadIdx.x; i < rows * D; i += kFpThreads) {
-            const int r = i / D, d = i % D;
-            const int j = r / p.n_q, sq = r % p.n_q;
-            const float v = fin_l[r] > 0.f ? osm[i] / fin_l[r] : 0.f;
-            out[(int64_t)b * p.o_sb + (int64_t)(h * p.g + j) * p.o_sh + (int64_t)sq * p.o_ss + d] = Elem<DT>::from_f(v);
+        __syncthreads();
+        // ---- online softmax per row (one warp per row) ----
+        for (int r = warp; r < rows; r += NW) {
+            float mx = -INFINITY;
+            for (int tk = lane; tk < n; tk += 32) mx = fmaxf(mx, psm[r * kFinChunk + tk]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float mold = m_row[r];
+            const float mnew = fmaxf(mold, mx);
+            float sum = 0.f;
+            for (int tk = lane; tk < n; tk += 32) {
+                const float e = ex2(psm[r * kFinChunk + tk] - mnew);
+                psm[r * kFinChunk + tk] = e;
+                sum += e;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) {
+                const float corr = (mold == -INFINITY) ? 0.f : ex2(mold - mnew);
+                m_row[r] = mnew;
+                l_row[r] = l_row[r] * corr + sum;
+                c_row[r] = corr;
+            }
         }
+        __syncthreads();
+        // ---- O[r][d] = O * corr + sum_tok P[r][tok] V[tok][d] ----
+#pragma unroll
+        for (int k = 0; k < OUTS; ++k) {
+            const int i = tid + k * kFinThreads;
+            if (i >= rows * D2) continue;
+            const int r = i / D2, d2 = i % D2;
+            const float corr = c_row[r];
+            float a0 = acc_f[k][0] * corr, a1 = acc_f[k][1] * corr;
+            const float* pr = psm + r * kFinChunk;
+            const uint32_t* vcol = reinterpret_cast<const uint32_t*>(vsm) + d2;
+#pragma unroll 4
+            for (int tk = 0; tk < n; ++tk) {
+                const uint32_t vv = vcol[tk * D2];
+                const float pt = pr[tk];
+                a0 = fmaf(pt, Elem<DT>::to_f(reinterpret_cast<const T*>(&vv)[0]), a0);
+                a1 = fmaf(pt, Elem<DT>::to_f(reinterpret_cast<const T*>(&vv)[1]), a1);
+            }
+            acc_f[k][0] = a0;
+            acc_f[k][1] = a1;
+        }
+    }
+
+    // ---- middle partials: wait for the middle grid, then merge ----
+    float acc_m[OUTS][2];
+#pragma unroll
+    for (int k = 0; k < OUTS; ++k) acc_m[k][0] = acc_m[k][1] = 0.f;
+    int zb = 0, c0 = 0, nsl = 0, U = 0, C = 1;
+    if (p.has_mid) {
+        griddep_wait();
+        const int Z = p.B * p.Hkv;
+        U = p.cu_units ? p.cu_units[Z] : Z * p.units_per_z;
+        C = p.n_ctas < U ? p.n_ctas : U;
+        zb = p.cu_units ? p.cu_units[z] : z * p.units_per_z;
+        const int ze = p.cu_units ? p.cu_units[z + 1] : (z + 1) * p.units_per_z;
+        if (ze > zb && C > 0) {
+            c0 = cta_of_unit(zb, C, U);
+            nsl = cta_of_unit(ze - 1, C, U) - c0 + 1;
+        }
+    }
+    __syncthreads();   // FP statistics complete
+    for (int j0 = 0; j0 < nsl; j0 += kFinSlots) {
+        const int nj = (nsl - j0) < kFinSlots ? (nsl - j0) : kFinSlots;
+        __syncthreads();
+        for (int i = tid; i < nj * rows; i += kFinThreads) {
+            const int j = i / rows, r = i % rows;
+            const int uc = (int)((int64_t)(c0 + j0 + j) * U / C);
+            const int slot = uc > zb ? uc : zb;
+            const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + ((int64_t)slot * rows + r) * 2);
+            sw[j * ROWS + r] = ml.x;
+            sl[j * ROWS + r] = ml.y;
+        }
+        __syncthreads();
+        if (tid < rows) {
+            const int r = tid;
+            const float mold = m_row[r];
+            float mx = mold;
+            for (int j = 0; j < nj; ++j) mx = fmaxf(mx, sw[j * ROWS + r]);
+            const float corr = (mold == -INFINITY) ? 0.f : ex2(mold - mx);
+            float Ls = l_row[r] * corr;
+            for (int j = 0; j < nj; ++j) {
+                const float ms = sw[j * ROWS + r];
+                const float w = (ms == -INFINITY) ? 0.f : ex2(ms - mx);
+                Ls += w * sl[j * ROWS + r];
+                sw[j * ROWS + r] = w;
+            }
+            m_row[r] = mx;
+            l_row[r] = Ls;
+            c_row[r] = corr;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < OUTS; ++k) {
+            const int i = tid + k * kFinThreads;
+            if (i >= rows * D2) continue;
+            const int r = i / D2, d2 = i % D2;
+            const float corr = c_row[r];
+            float a0 = acc_m[k][0] * corr, a1 = acc_m[k][1] * corr;
+            acc_f[k][0] *= corr;
+            acc_f[k][1] *= corr;
+#pragma unroll 4
+            for (int j = 0; j < nj; ++j) {
+                const float w = sw[j * ROWS + r];
+                if (w == 0.f) continue;
+                const int uc = (int)((int64_t)(c0 + j0 + j) * U / C);
+                const int slot = uc > zb ? uc : zb;
+                const float2 ov = *reinterpret_cast<const float2*>(p.ws_o + ((int64_t)slot * rows + r) * D + 2 * d2);
+                a0 = fmaf(w, ov.x, a0);
+                a1 = fmaf(w, ov.y, a1);
+            }
+            acc_m[k][0] = a0;
+            acc_m[k][1] = a1;
+        }
+    }
+    __syncthreads();
+    if (tid < rows) f_row[tid] = l_row[tid] > 0.f ? 1.f / l_row[tid] : 0.f;
+    if (p.rotation && nsl > 0) {
+        // middle part is in the rotated basis: mid @ R (rows via shared memory)
+        float* msm = reinterpret_cast<float*>(fsm + L::K_OFF);
+#pragma unroll
+        for (int k = 0; k < OUTS; ++k) {
+            const int i = tid + k * kFinThreads;
+            if (i < rows * D2) { msm[2 * i] = acc_m[k][0]; msm[2 * i + 1] = acc_m[k][1]; }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < OUTS; ++k) {
+            const int i = tid + k * kFinThreads;
+            if (i >= rows * D2) continue;
+            const int r = i / D2, d2 = i % D2;
+            float a0 = 0.f, a1 = 0.f;
+            for (int e = 0; e < D; ++e) {
+                const float mv = msm[r * D + e];
+                const float2 rr = *reinterpret_cast<const float2*>(p.rotation + (int64_t)e * D + 2 * d2);
+                a0 = fmaf(mv, rr.x, a0);
+                a1 = fmaf(mv, rr.y, a1);
+            }
+            acc_m[k][0] = a0;
+            acc_m[k][1] = a1;
+        }
+    }
+    __syncthreads();
+    auto* out = reinterpret_cast<T*>(p.out);
+#pragma unroll
+    for (int k = 0; k < OUTS; ++k) {
+        const int i = tid + k * kFinThreads;
+        if (i >= rows * D2) continue;
+        const int r = i / D2, d2 = i % D2;
+        const float inv = f_row[r];
+        const int j = r / p.n_q, sq = r % p.n_q;
+        T* o = out + (int64_t)b * p.o_sb + (int64_t)(h * p.g + j) * p.o_sh + (int64_t)sq * p.o_ss + 2 * d2;
+        o[0] = Elem<DT>::from_f((acc_f[k][0] + acc_m[k][0]) * inv);
+        o[1] = Elem<DT>::from_f((acc_f[k][1] + acc_m[k][1]) * inv);
     }
 }
 
@@ -1447,11 +1475,33 @@ static MidKernelInfo select_mid_d(int D, int NT, int kb, int vb, bool vg, bool r
     return MidKernelInfo{nullptr, 0, 0};
 }
 
+struct FinKernelInfo {
+    void* fn;
+    int smem;
+};
+
+template <int DT, int D, int NT>
+static FinKernelInfo fin_info() {
+    static FinKernelInfo info[kMaxDevices] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) dev = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    FinKernelInfo& i = info[dev];
+    if (!i.fn) {
+        i.smem = FinLayout<D, NT>::BYTES;
+        cudaFuncSetAttribute(&finish_kernel<DT, D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, i.smem);
+        i.fn = reinterpret_cast<void*>(&finish_kernel<DT, D, NT>);
+    }
+    return i;
+}
+
 template <int DT>
-static void* select_fp(int D, int NT) {
-    if (D == 128) return NT == 1 ? (void*)&fp_tier_kernel<DT, 128, 1> : (void*)&fp_tier_kernel<DT, 128, 2>;
-    if (D == 64) return NT == 1 ? (void*)&fp_tier_kernel<DT, 64, 1> : (void*)&fp_tier_kernel<DT, 64, 2>;
-    return nullptr;
+static FinKernelInfo select_fin(int D, int NT) {
+    if (D == 128) return NT == 1 ? fin_info<DT, 128, 1>() : fin_info<DT, 128, 2>();
+    if (D == 64) return NT == 1 ? fin_info<DT, 64, 1>() : fin_info<DT, 64, 2>();
+    return FinKernelInfo{nullptr, 0};
 }
 
 struct Plan {
@@ -1463,7 +1513,7 @@ struct Plan {
     int64_t max_units;   // sizing bound
     int n_ctas;
     int n_fp;
-    size_t off_err, off_qrot, off_cnt, off_fpml, off_fpo, off_ml, off_o, total;
+    size_t off_err, off_qrot, off_ml, off_o, total;
     MidKernelInfo mk;
 };
 
@@ -1527,9 +1577,6 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
     pl->off_err = off; off += 256;
     pl->off_qrot = off;
     if (rot) off += ((size_t)d->B * d->Hq * d->n_q * d->D * 4 + 255) / 256 * 256;
-    pl->off_cnt = off; off += ((size_t)Z * 4 + 255) / 256 * 256;
-    pl->off_fpml = off; off += ((size_t)Z * pl->rows * 2 * 4 + 255) / 256 * 256;
-    pl->off_fpo = off; off += ((size_t)Z * pl->rows * d->D * 4 + 255) / 256 * 256;
     pl->off_ml = off; off += ((size_t)pl->max_units * pl->rows * 2 * 4 + 255) / 256 * 256;
     pl->off_o = off; off += (size_t)pl->max_units * pl->rows * d->D * 4;
     pl->total = off;
@@ -1588,37 +1635,6 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
         FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)(d->B * d->Hq * d->n_q)), dim3(128),
                                  (size_t)d->D * 4, s, args));
     }
-    // FP tiers: a partial for the merge, or the final output when there is no
-    // middle (and for ragged rows whose middle is empty).
-    // Always launched: with a middle tier it also zeroes the arrival counters
-    // (the workspace may have held another call's partials there).
-    const bool run_fp = true;
-    if (run_fp) {
-        FpParams fp = {};
-        fp.B = d->B; fp.Hq = d->Hq; fp.Hkv = d->Hkv; fp.D = d->D; fp.n_q = d->n_q;
-        fp.g = pl.g; fp.rows = pl.rows; fp.qk_scale = qk_scale;
-        fp.q = d->q; fp.q_sb = d->q_sb; fp.q_sh = d->q_sh; fp.q_ss = d->q_ss;
-        fp.out = d->out; fp.o_sb = d->o_sb; fp.o_sh = d->o_sh; fp.o_ss = d->o_ss;
-        fp.vec = 1;
-        for (int i = 0; i < d->n_segments; ++i) {
-            const fade_kv_segment& sg = d->seg[i];
-            if (sg.kind != FADE_SEG_FP) continue;
-            FpSeg& f = fp.fp[fp.n_fp++];
-            f.k = sg.k; f.v = sg.v; f.row_sb = sg.row_sb; f.row_sh = sg.row_sh;
-            f.row_base = sg.row_base; f.lens = sg.lens; f.len = sg.len;
-            if (!aligned16(sg.k) || !aligned16(sg.v)) fp.vec = 0;
-        }
-        fp.has_mid = has_mid ? 1 : 0;
-        fp.cu_units = d->cu_units;
-        fp.units_per_z = pl.units_per_z;
-        fp.ws_fpml = reinterpret_cast<float*>(ws + pl.off_fpml);
-        fp.ws_fpo = reinterpret_cast<float*>(ws + pl.off_fpo);
-        fp.counters = has_mid ? reinterpret_cast<int*>(ws + pl.off_cnt) : nullptr;
-        void* fn = d->dtype == FADE_F16 ? select_fp<FADE_F16>(d->D, pl.NT) : select_fp<FADE_BF16>(d->D, pl.NT);
-        if (!fn) return FADE_ERR_UNSUPPORTED;
-        void* args[] = {(void*)&fp};
-        FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)Z), dim3(kFpThreads), 0, s, args));
-    }
     if (has_mid) {
         const fade_kv_segment& sg = d->seg[pl.mid_idx];
         CUtensorMap tk, tv;
@@ -1672,11 +1688,6 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
         mp.ws_ml = reinterpret_cast<float*>(ws + pl.off_ml);
         mp.ws_o = reinterpret_cast<float*>(ws + pl.off_o);
         mp.ws_err = reinterpret_cast<int*>(ws + pl.off_err);
-        mp.counters = reinterpret_cast<int*>(ws + pl.off_cnt);
-        mp.fp_ml = pl.n_fp > 0 ? reinterpret_cast<const float*>(ws + pl.off_fpml) : nullptr;
-        mp.fp_o = pl.n_fp > 0 ? reinterpret_cast<const float*>(ws + pl.off_fpo) : nullptr;
-        mp.out = d->out; mp.o_sb = d->o_sb; mp.o_sh = d->o_sh; mp.o_ss = d->o_ss;
-        mp.rotation = rot ? d->rotation : nullptr;
         mp.scale_tma = scale_tma;
         if (std::getenv("FADE_DEBUG_PLAN")) {
             std::fprintf(stderr,
@@ -1691,6 +1702,35 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
         FADE_CUDA_TRY(launch_pdl(pl.mk.fn, dim3((unsigned)pl.n_ctas), dim3(kMidThreads),
                                  (size_t)pl.mk.smem, s, args));
     }
+    // Finisher: FP tiers + merge of the middle partials -> out.  Always
+    // launched (it also writes rows whose middle is empty).
+    FinParams fp = {};
+    fp.B = d->B; fp.Hq = d->Hq; fp.Hkv = d->Hkv; fp.D = d->D; fp.n_q = d->n_q;
+    fp.g = pl.g; fp.rows = pl.rows; fp.qk_scale = qk_scale;
+    fp.q = d->q; fp.q_sb = d->q_sb; fp.q_sh = d->q_sh; fp.q_ss = d->q_ss;
+    fp.out = d->out; fp.o_sb = d->o_sb; fp.o_sh = d->o_sh; fp.o_ss = d->o_ss;
+    fp.vec = 1;
+    for (int i = 0; i < d->n_segments; ++i) {
+        const fade_kv_segment& sg = d->seg[i];
+        if (sg.kind != FADE_SEG_FP) continue;
+        FpSeg& f = fp.fp[fp.n_fp++];
+        f.k = sg.k; f.v = sg.v; f.row_sb = sg.row_sb; f.row_sh = sg.row_sh;
+        f.row_base = sg.row_base; f.lens = sg.lens; f.len = sg.len;
+        if (!aligned16(sg.k) || !aligned16(sg.v)) fp.vec = 0;
+    }
+    if ((d->D * 2) % 16 != 0) fp.vec = 0;
+    fp.has_mid = has_mid ? 1 : 0;
+    fp.cu_units = d->cu_units;
+    fp.units_per_z = pl.units_per_z;
+    fp.n_ctas = pl.n_ctas;
+    fp.ws_ml = reinterpret_cast<const float*>(ws + pl.off_ml);
+    fp.ws_o = reinterpret_cast<const float*>(ws + pl.off_o);
+    fp.rotation = rot ? d->rotation : nullptr;
+    const FinKernelInfo fk = d->dtype == FADE_F16 ? select_fin<FADE_F16>(d->D, pl.NT)
+                                                  : select_fin<FADE_BF16>(d->D, pl.NT);
+    if (!fk.fn) return FADE_ERR_UNSUPPORTED;
+    void* fargs[] = {(void*)&fp};
+    FADE_CUDA_TRY(launch_pdl(fk.fn, dim3((unsigned)Z), dim3(kFinThreads), (size_t)fk.smem, s, fargs));
     return FADE_OK;
 }
 
@@ -1701,8 +1741,7 @@ extern "C" int fade_workspace_check(void* workspace, size_t ws_bytes, void* stre
     FADE_CUDA_TRY(cudaMemcpyAsync(&h, workspace, sizeof(int), cudaMemcpyDeviceToHost, s));
     FADE_CUDA_TRY(cudaStreamSynchronize(s));
     if (h != 0) {
-        // A stalled call may have left arrival counters mid-count: zero it all.
-        FADE_CUDA_TRY(cudaMemsetAsync(workspace, 0, ws_bytes, s));
+        FADE_CUDA_TRY(cudaMemsetAsync(workspace, 0, 256, s));
         FADE_CUDA_TRY(cudaStreamSynchronize(s));
         return FADE_ERR_TIMEOUT;
     }
@@ -1757,8 +1796,8 @@ extern "C" int fade_decode_attn_noalloc(const fade_decode_desc* d, void* stream)
     int st = fade::noalloc_scratch(&ws);
     if (st != FADE_OK) return st;
     // The array keeps the previous call's bytes.  Only the error word must
-    // start at zero (the per-row arrival counters are reset by the call's own
-    // FP-tier kernel), so clear the first 256 bytes on the caller's stream.
+    // start at zero (every partial the finisher reads is written by the same
+    // call first), so clear the first 256 bytes on the caller's stream.
     FADE_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, as_stream(stream)));
     return fade_decode_attn(d, ws, fade::kNoAllocScratchBytes, stream);
 }
