@@ -65,7 +65,10 @@ __device__ __forceinline__ unsigned long long gtimer() {
 }
 #define FADE_TR(slot) do { if (threadIdx.x == 0 && blockIdx.x < 1024 && (slot) < kTraceEv) g_trace[blockIdx.x * kTraceEv + (slot)] = gtimer(); } while (0)
 #define FADE_TRP(slot) do { if (threadIdx.x == kConsumerWarps * 32 && blockIdx.x < 1024 && (slot) < kTraceEv) g_trace[blockIdx.x * kTraceEv + (slot)] = gtimer(); } while (0)
+// finisher CTAs record into rows 768.. of the same array
+#define FADE_TRF(slot) do { if (threadIdx.x == 0 && blockIdx.x < 256) g_trace[(768 + blockIdx.x) * kTraceEv + (slot)] = gtimer(); } while (0)
 #else
+#define FADE_TRF(slot) do {} while (0)
 #define FADE_TR(slot) do {} while (0)
 #define FADE_TRP(slot) do {} while (0)
 #endif
@@ -74,6 +77,9 @@ constexpr int kMidThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
 constexpr int kStages = 4;
 constexpr float kLog2e = 1.4426950408889634f;
+// Initial running maximum of the middle kernel's online softmax: finite and
+// below any real score, so exp2(score - max) never sees inf - inf.
+constexpr float kMaskedMax = -1e30f;
 constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polling
 
 // ---------------------------------------------------------------------------
@@ -111,6 +117,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // exits; the device error word tells the host.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* err) {
+    if (mbar_try_wait(bar, parity)) return true;   // common case: one poll
     if (*abort_flag) return false;
     for (uint32_t i = 0; i < kWaitLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -670,7 +677,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            m_run[nt][0] = m_run[nt][1] = -INFINITY;
+            m_run[nt][0] = m_run[nt][1] = kMaskedMax;
             l_run[nt][0] = l_run[nt][1] = 0.f;
 #pragma unroll
             for (int mi = 0; mi < MT; ++mi)
@@ -798,13 +805,14 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         const uint32_t ph = (uint32_t)(i / kStages) & 1u;
         const bool ready = mbar_wait(full_bar(s), ph, abort_flag, p.ws_err);
         FADE_TR(10 + i);
-        const int64_t tok_w = (int64_t)(u - zb) * kStageTokens + warp * 32;  // first token of this warp
+        const int tw = (u - zb) * kStageTokens + warp * 32;  // first token of this warp (row-relative)
+        const int clen = (int)cur_len;
         const uint8_t* st = smem + s * L::STAGE_BYTES;
         const uint32_t kbase = smem_u32(st + L::K_OFF);
         const uint32_t vbase = smem_u32(st + L::V_OFF);
         const uint8_t* scb = smem + L::SC_BASE + s * L::SC_BYTES;
 
-        if (ready && tok_w < cur_len && FADE_ABLATE != 1 && FADE_ABLATE < 4) {
+        if (ready && tw < clen && FADE_ABLATE != 1 && FADE_ABLATE < 4) {
             // ---- S^T = K_deq . q^T for the warp's 2 m-tiles ----
             // two accumulators per m-tile (even / odd k-steps) halve the
             // dependent MMA chain; summed before the softmax
@@ -865,42 +873,64 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 #pragma unroll
                     for (int e = 0; e < 4; ++e) sacc[mt][nt][e] += sacc2[mt][nt][e];
             // ---- online softmax over the 32 tokens (log2 domain) ----
-            uint32_t pb[2][NT][2];
+            // Running maxima start at kMaskedMax (finite), so masked scores
+            // (-inf) give exp2 = 0 and no difference of infinities arises.
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                float mx[2] = {-INFINITY, -INFINITY};
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] *= p.qk_scale;
+            if (tw + 32 > clen) {   // warp-uniform: only the row's last tile is partial
 #pragma unroll
                 for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int tok = (int)tok_w + mt * 16 + gid + ((e >> 1) << 3);
-                        float v = sacc[mt][nt][e] * p.qk_scale;
-                        if (tok >= cur_len) v = -INFINITY;
-                        sacc[mt][nt][e] = v;
-                        mx[e & 1] = fmaxf(mx[e & 1], v);
-                    }
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            if (tw + mt * 16 + gid + ((e >> 1) << 3) >= clen) sacc[mt][nt][e] = -INFINITY;
+            }
+            uint32_t pb[2][NT][2];
+            bool grow = false;
+            float corr[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 4));
-                    mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 8));
-                    mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
-                    const float mnew = fmaxf(m_run[nt][e], mx[e]);
-                    const float corr = (m_run[nt][e] == -INFINITY) ? 0.f : ex2(m_run[nt][e] - mnew);
+                    float mx = fmaxf(fmaxf(sacc[0][nt][e], sacc[0][nt][e + 2]),
+                                     fmaxf(sacc[1][nt][e], sacc[1][nt][e + 2]));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    const float mnew = fmaxf(m_run[nt][e], mx);
+                    grow |= mnew > m_run[nt][e];
+                    corr[nt][e] = ex2(m_run[nt][e] - mnew);
                     m_run[nt][e] = mnew;
-                    l_run[nt][e] *= corr;
-#pragma unroll
-                    for (int mi = 0; mi < MT; ++mi) {
-                        o[nt][mi][e] *= corr;
-                        o[nt][mi][e + 2] *= corr;
-                    }
                 }
+            }
+            // Rescale only when some row maximum of the warp grew (corr is
+            // exactly 1 otherwise, so skipping is bit-identical).
+            if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        l_run[nt][e] *= corr[nt][e];
+#pragma unroll
+                        for (int mi = 0; mi < MT; ++mi) {
+                            o[nt][mi][e] *= corr[nt][e];
+                            o[nt][mi][e + 2] *= corr[nt][e];
+                        }
+                    }
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
                 for (int mt = 0; mt < 2; ++mt) {
                     float pv[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float mref = m_run[nt][e & 1];
-                        const float pe = (sacc[mt][nt][e] == -INFINITY) ? 0.f : ex2(sacc[mt][nt][e] - mref);
+                        const float pe = ex2(sacc[mt][nt][e] - m_run[nt][e & 1]);
                         l_run[nt][e & 1] += pe;
                         pv[e] = pe;
                     }
@@ -917,15 +947,15 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 // tokens of this m-tile past the length: their scales may be
                 // stale bytes (NaN * 0 must not reach the MMA), so zero them;
                 // a tile entirely past the length is skipped.
-                const int64_t tile_tok = tok_w - warp * 32 + trow0;
-                if (tile_tok >= cur_len) continue;
+                const int tile_tok = tw - warp * 32 + trow0;
+                if (tile_tok >= clen) continue;
                 uint32_t vs0 = 0, vs1 = 0;
                 const uint16_t* gsc = nullptr;
                 if constexpr (!VGROUP) {
                     const uint32_t* sc32 = reinterpret_cast<const uint32_t*>(scb);
                     vs0 = sc32[(trow0 + 2 * t) >> 1];       // tokens 2t, 2t+1
                     vs1 = sc32[(trow0 + 8 + 2 * t) >> 1];   // tokens 8+2t, 9+2t
-                    const int64_t rem = cur_len - tile_tok;  // valid tokens in this tile (> 0)
+                    const int rem = clen - tile_tok;  // valid tokens in this tile (> 0)
                     if (rem < 16) {
                         const int t0 = 2 * t, t1 = 8 + 2 * t;
                         vs0 &= (t0 < rem ? 0x0000FFFFu : 0u) | (t0 + 1 < rem ? 0xFFFF0000u : 0u);
@@ -1115,6 +1145,7 @@ finish_kernel(FinParams p) {
     const int b = z / p.Hkv, h = z % p.Hkv;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int rows = p.rows;
+    FADE_TRF(0);
     if (!p.has_mid) griddep_wait();
     griddep_launch_dependents();
 
@@ -1249,8 +1280,10 @@ finish_kernel(FinParams p) {
 #pragma unroll
     for (int k = 0; k < OUTS; ++k) acc_m[k][0] = acc_m[k][1] = 0.f;
     int zb = 0, c0 = 0, nsl = 0, U = 0, C = 1;
+    FADE_TRF(1);
     if (p.has_mid) {
         griddep_wait();
+        FADE_TRF(2);
         const int Z = p.B * p.Hkv;
         U = p.cu_units ? p.cu_units[Z] : Z * p.units_per_z;
         C = p.n_ctas < U ? p.n_ctas : U;
@@ -1355,6 +1388,7 @@ finish_kernel(FinParams p) {
         o[0] = Elem<DT>::from_f((acc_f[k][0] + acc_m[k][0]) * inv);
         o[1] = Elem<DT>::from_f((acc_f[k][1] + acc_m[k][1]) * inv);
     }
+    FADE_TRF(3);
 }
 
 // ---------------------------------------------------------------------------
