@@ -94,6 +94,21 @@ class DecodeDesc(ctypes.Structure):
     ]
 
 
+class AgeOutDesc(ctypes.Structure):
+    _fields_ = [
+        ("ring_seg", ctypes.c_int32),
+        ("mid_seg", ctypes.c_int32),
+        ("ring_cap", _c_i64),
+        ("ring_origin", _c_i64),
+        ("k_new", _vp),
+        ("v_new", _vp),
+        ("new_sb", _c_i64),
+        ("new_sh", _c_i64),
+        ("prefetch_tiers", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
 # (name, restype, argtypes) for every symbol of include/fade_b200.h
 _SIGNATURES = {
     "fade_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -138,6 +153,10 @@ _SIGNATURES = {
     "fade_decode_attn": (
         ctypes.c_int,
         [ctypes.POINTER(DecodeDesc), _vp, ctypes.c_size_t, _vp],
+    ),
+    "fade_decode_attn_age_out": (
+        ctypes.c_int,
+        [ctypes.POINTER(DecodeDesc), ctypes.POINTER(AgeOutDesc), _vp, ctypes.c_size_t, _vp],
     ),
     "fade_workspace_check": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp]),
     "fade_decode_attn_noalloc_max_bytes": (ctypes.c_size_t, []),

@@ -329,6 +329,7 @@ struct MidParams {
     int* ws_err;
     int scale_tma;                  // V scales arrive by TMA (row starts 8-aligned)
     int q_vec;                      // q / k_scale rows allow 16-byte loads
+    int early;                      // producer may stream before the previous kernel ends
 };
 
 __device__ __forceinline__ int64_t seg_len(const MidParams& p, int b) {
@@ -491,11 +492,20 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     }
     __syncthreads();
     FADE_TR(0);
+#ifdef FADE_TRACE
+    if (threadIdx.x == 0 && blockIdx.x < 1024) {
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        g_trace[blockIdx.x * kTraceEv + 95] = smid + 1;
+    }
+#endif
     // Inputs may be produced by the previous kernel in the stream (age-out,
     // query rotation): wait for it before touching global memory, then let the
-    // next kernel in the stream start its prologue.
-    griddep_wait();
-    griddep_launch_dependents();
+    // next kernel in the stream start its prologue.  With `early` the tiers
+    // are known not to be written by that kernel: the producer starts
+    // streaming at once and only the consumers (queries, partial slots) wait.
+    if (!(p.early && warp == kConsumerWarps)) griddep_wait();
+    if (warp < kConsumerWarps) griddep_launch_dependents();
     FADE_TR(1);
     if (ub >= ue) return;
 
@@ -1096,6 +1106,23 @@ struct FinParams {
     const float* ws_ml;             // middle partials [U][rows][2]
     const float* ws_o;              // [U][rows][D]
     const float* rotation;          // rotated middle: [D,D] fp32, else null
+    // fused age-out (fade_decode_attn_age_out); age == 0 otherwise
+    int age;
+    int ring_fp;                    // index into fp[] of the recent-window ring
+    int64_t ring_cap, ring_origin;
+    const void* k_new;              // [B,Hkv,D]
+    const void* v_new;
+    int64_t new_sb, new_sh;
+    uint8_t* mid_k;                 // middle code rows (D/2 bytes), row-indexed
+    uint8_t* mid_v;
+    void* mid_vs;                   // per-row V scale
+    const void* mid_ks;             // per-channel K scale
+    int64_t ks_sb, ks_sh;
+    int64_t mid_sb, mid_sh;
+    const int64_t* mid_row_base;
+    int64_t mid_cap;
+    int32_t* mid_len;               // [B], advanced by the call
+    int* age_cnt;                   // [B] workspace counters (zero between calls)
 };
 
 template <int D, int NT>
@@ -1149,6 +1176,28 @@ finish_kernel(FinParams p) {
     if (!p.has_mid) griddep_wait();
     griddep_launch_dependents();
 
+    // ---- fused age-out: this row's middle length, ring slot, arrival ----
+    __shared__ int s_age[2];   // [0] = n (middle length before the step), [1] = last CTA of b
+    int64_t age_n = 0, age_slot = -1;
+    bool room = false;
+    if (p.age) {
+        if (tid == 0) {
+            const int n = p.mid_len[b];
+            // acq_rel: this CTA's read of mid_len[b] happens before the write
+            // of n + 1 by the last CTA of b (which observes this increment)
+            int old;
+            asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.age_cnt + b) : "memory");
+            s_age[0] = n;
+            s_age[1] = (old == p.Hkv - 1) ? 1 : 0;
+        }
+        __syncthreads();
+        age_n = s_age[0];
+        room = age_n < p.mid_cap;
+        if (room) {
+            age_slot = (age_n - p.ring_origin) % p.ring_cap;
+            if (age_slot < 0) age_slot += p.ring_cap;
+        }
+    }
     // ---- FP segments of this row: lengths and first rows ----
     int64_t seg_len_[FADE_MAX_SEGMENTS], seg_row_[FADE_MAX_SEGMENTS];
     int64_t n_tok = 0;
@@ -1162,6 +1211,17 @@ finish_kernel(FinParams p) {
             seg_row_[s] = sg.row_base ? sg.row_base[z] : (int64_t)b * sg.row_sb + (int64_t)h * sg.row_sh;
             n_tok += seg_len_[s];
         }
+    }
+    // Token order: the FP segments' tokens, then (age-out with room) the new
+    // token.  The ring token at age_slot stays in the list: after staging it
+    // is replaced in shared memory by its INT4 round trip (it moves to the
+    // middle in this step), and the new token takes its ring slot.
+    int64_t ft_aged = -1;
+    const int64_t n_seg_tok = n_tok;
+    if (room) {
+        ft_aged = age_slot;
+        for (int s = 0; s < p.ring_fp; ++s) ft_aged += seg_len_[s];
+        n_tok += 1;
     }
     // ---- queries, pre-scaled into the log2 domain ----
     for (int i = tid; i < ROWS * D; i += kFinThreads) {
@@ -1187,25 +1247,79 @@ finish_kernel(FinParams p) {
         for (int i = tid; i < n * PCS; i += kFinThreads) {
             const int tk = i / PCS, c = i % PCS;
             int64_t ft = t0 + tk;
-            int s = 0;
-            while (s < p.n_fp - 1 && ft >= seg_len_[s]) { ft -= seg_len_[s]; ++s; }
-            const FpSeg& sg = p.fp[s];
-            const int64_t off = (seg_row_[s] + ft) * D + c * 8;
+            const T* ks;
+            const T* vs;
+            if (ft >= n_seg_tok) {   // the step's new token (fused age-out)
+                const int64_t off = (int64_t)b * p.new_sb + (int64_t)h * p.new_sh + c * 8;
+                ks = reinterpret_cast<const T*>(p.k_new) + off;
+                vs = reinterpret_cast<const T*>(p.v_new) + off;
+            } else {
+                int s = 0;
+                while (s < p.n_fp - 1 && ft >= seg_len_[s]) { ft -= seg_len_[s]; ++s; }
+                const FpSeg& sg = p.fp[s];
+                const int64_t off = (seg_row_[s] + ft) * D + c * 8;
+                ks = reinterpret_cast<const T*>(sg.k) + off;
+                vs = reinterpret_cast<const T*>(sg.v) + off;
+            }
             T* kd = ksm + tk * L::KSTR + c * 8;
             T* vd = vsm + tk * D + c * 8;
             if (p.vec) {
-                cp_async16(smem_u32(kd), reinterpret_cast<const T*>(sg.k) + off);
-                cp_async16(smem_u32(vd), reinterpret_cast<const T*>(sg.v) + off);
+                cp_async16(smem_u32(kd), ks);
+                cp_async16(smem_u32(vd), vs);
             } else {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    kd[e] = reinterpret_cast<const T*>(sg.k)[off + e];
-                    vd[e] = reinterpret_cast<const T*>(sg.v)[off + e];
+                    kd[e] = ks[e];
+                    vd[e] = vs[e];
                 }
             }
         }
         cp_async_wait_all();
         __syncthreads();
+        if (ft_aged >= t0 && ft_aged < t0 + n) {
+            // ---- age-out of the oldest ring token (warp 0) ----
+            // INT4 codes exactly as fade_age_out_int4; its shared-memory row
+            // becomes the dequantised value rnd(code * scale) that the middle
+            // tier will hold, and the new token is written into its ring slot.
+            if (warp == 0) {
+                T* kr = ksm + (ft_aged - t0) * L::KSTR;
+                T* vr = vsm + (ft_aged - t0) * D;
+                const int64_t mrow = (p.mid_row_base ? p.mid_row_base[z]
+                                                     : (int64_t)b * p.mid_sb + (int64_t)h * p.mid_sh) + age_n;
+                const T* ksc = reinterpret_cast<const T*>(p.mid_ks) + (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
+                float m = 0.f;
+                for (int d = lane; d < D; d += 32) m = fmaxf(m, fabsf(Elem<DT>::to_f(vr[d])));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                m = fmaxf(m, Elem<DT>::eps());
+                const float inv = inv_scale<DT>(m, 7.f);
+                const float vsc = Elem<DT>::rnd(__fdiv_rn(m, 7.f));
+                if (lane == 0) reinterpret_cast<T*>(p.mid_vs)[mrow] = Elem<DT>::from_f(vsc);
+                for (int pp = lane; pp < D / 2; pp += 32) {
+                    int kq[2], vq[2];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int d = 2 * pp + j;
+                        const float sc = Elem<DT>::to_f(ksc[d]);
+                        const float kx = Elem<DT>::to_f(kr[d]);
+                        kq[j] = (sc > 0.f) ? quant_code(__fdiv_rn(kx, sc), -8.f, 7.f) : 0;
+                        vq[j] = quant_code(Elem<DT>::rnd(__fmul_rn(Elem<DT>::to_f(vr[d]), inv)), -8.f, 7.f);
+                        kr[d] = Elem<DT>::from_f((float)kq[j] * sc);
+                        vr[d] = Elem<DT>::from_f((float)vq[j] * vsc);
+                    }
+                    p.mid_k[mrow * (D / 2) + pp] = (uint8_t)(((kq[0] & 15) << 4) | (kq[1] & 15));
+                    p.mid_v[mrow * (D / 2) + pp] = (uint8_t)(((vq[0] & 15) << 4) | (vq[1] & 15));
+                }
+                // the new token takes the freed ring slot (read above, in this chunk)
+                const FpSeg& rg = p.fp[p.ring_fp];
+                T* rk = const_cast<T*>(reinterpret_cast<const T*>(rg.k)) + (seg_row_[p.ring_fp] + age_slot) * D;
+                T* rv = const_cast<T*>(reinterpret_cast<const T*>(rg.v)) + (seg_row_[p.ring_fp] + age_slot) * D;
+                const T* kn = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
+                const T* vn = reinterpret_cast<const T*>(p.v_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
+                for (int d = lane; d < D; d += 32) { rk[d] = kn[d]; rv[d] = vn[d]; }
+            }
+            __syncthreads();
+        }
         // ---- scores S[r][tok] = q_r . k_tok (log2 domain) ----
         for (int i = tid; i < rows * n; i += kFinThreads) {
             const int r = i / n, tk = i % n;
@@ -1388,6 +1502,13 @@ finish_kernel(FinParams p) {
         o[0] = Elem<DT>::from_f((acc_f[k][0] + acc_m[k][0]) * inv);
         o[1] = Elem<DT>::from_f((acc_f[k][1] + acc_m[k][1]) * inv);
     }
+    // The last CTA of b (every CTA of b has read mid_len[b]; the middle grid,
+    // which reads it too, has completed) advances the length and re-arms the
+    // counter for the next call.
+    if (p.age && tid == 0 && s_age[1]) {
+        if (room) p.mid_len[b] = (int32_t)(age_n + 1);
+        p.age_cnt[b] = 0;
+    }
     FADE_TRF(3);
 }
 
@@ -1547,7 +1668,7 @@ struct Plan {
     int64_t max_units;   // sizing bound
     int n_ctas;
     int n_fp;
-    size_t off_err, off_qrot, off_ml, off_o, total;
+    size_t off_err, off_qrot, off_age, off_ml, off_o, total;
     MidKernelInfo mk;
 };
 
@@ -1611,6 +1732,7 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
     pl->off_err = off; off += 256;
     pl->off_qrot = off;
     if (rot) off += ((size_t)d->B * d->Hq * d->n_q * d->D * 4 + 255) / 256 * 256;
+    pl->off_age = off; off += ((size_t)d->B * 4 + 255) / 256 * 256;
     pl->off_ml = off; off += ((size_t)pl->max_units * pl->rows * 2 * 4 + 255) / 256 * 256;
     pl->off_o = off; off += (size_t)pl->max_units * pl->rows * d->D * 4;
     pl->total = off;
@@ -1642,11 +1764,20 @@ extern "C" size_t fade_decode_attn_workspace_size(const fade_decode_desc* d) {
     return pl.total;
 }
 
-extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size_t ws_bytes,
-                                void* stream) {
+static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* a, void* workspace,
+                            size_t ws_bytes, void* stream) {
     Plan pl;
     int st = make_plan(d, &pl);
     if (st != FADE_OK) return st;
+    if (a) {
+        if (a->ring_seg < 0 || a->ring_seg >= d->n_segments || a->mid_seg < 0 || a->mid_seg >= d->n_segments)
+            return FADE_ERR_INVALID_ARG;
+        const fade_kv_segment& rg = d->seg[a->ring_seg];
+        const fade_kv_segment& md = d->seg[a->mid_seg];
+        if (rg.kind != FADE_SEG_FP || md.kind != FADE_SEG_INT4) return FADE_ERR_UNSUPPORTED;
+        if (d->n_q != 1 || !a->k_new || !a->v_new || !md.lens || md.max_len <= 0) return FADE_ERR_INVALID_ARG;
+        if (rg.lens || rg.len != a->ring_cap || a->ring_cap <= 0) return FADE_ERR_INVALID_ARG;
+    }
     if (d->B == 0) return FADE_OK;
     if (!d->q || !d->out) return FADE_ERR_INVALID_ARG;
     if (!workspace || ws_bytes < pl.total) return FADE_ERR_WORKSPACE;
@@ -1730,6 +1861,7 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
                          d->B, d->Hq, d->Hkv, d->D, pl.rows, pl.kb, pl.vb, (int)pl.vg, pl.units_per_z,
                          pl.n_ctas, pl.mk.occ, pl.mk.smem, scale_tma, (long long)n_rows);
         }
+        mp.early = (a && a->prefetch_tiers) ? 1 : 0;
         mp.q_vec = aligned16(sg.k_scale) && sg.ks_sb % 8 == 0 && sg.ks_sh % 8 == 0 &&
                    (rot || (aligned16(d->q) && d->q_sb % 8 == 0 && d->q_sh % 8 == 0 && d->q_ss % 8 == 0));
         void* args[] = {(void*)&tk, (void*)&tv, (void*)&ts, (void*)&mp};
@@ -1760,12 +1892,41 @@ extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size
     fp.ws_ml = reinterpret_cast<const float*>(ws + pl.off_ml);
     fp.ws_o = reinterpret_cast<const float*>(ws + pl.off_o);
     fp.rotation = rot ? d->rotation : nullptr;
+    if (a) {
+        const fade_kv_segment& md = d->seg[a->mid_seg];
+        fp.age = 1;
+        fp.ring_fp = 0;
+        for (int i = 0; i < a->ring_seg; ++i) fp.ring_fp += d->seg[i].kind == FADE_SEG_FP ? 1 : 0;
+        fp.ring_cap = a->ring_cap;
+        fp.ring_origin = a->ring_origin;
+        fp.k_new = a->k_new; fp.v_new = a->v_new; fp.new_sb = a->new_sb; fp.new_sh = a->new_sh;
+        fp.mid_k = reinterpret_cast<uint8_t*>(const_cast<void*>(md.k));
+        fp.mid_v = reinterpret_cast<uint8_t*>(const_cast<void*>(md.v));
+        fp.mid_vs = const_cast<void*>(md.v_scale);
+        fp.mid_ks = md.k_scale; fp.ks_sb = md.ks_sb; fp.ks_sh = md.ks_sh;
+        fp.mid_sb = md.row_sb; fp.mid_sh = md.row_sh; fp.mid_row_base = md.row_base;
+        fp.mid_cap = md.max_len;
+        fp.mid_len = const_cast<int32_t*>(md.lens);
+        fp.age_cnt = reinterpret_cast<int*>(ws + pl.off_age);
+        if (!aligned16(a->k_new) || !aligned16(a->v_new) || (a->new_sb * 2) % 16 || (a->new_sh * 2) % 16) fp.vec = 0;
+    }
     const FinKernelInfo fk = d->dtype == FADE_F16 ? select_fin<FADE_F16>(d->D, pl.NT)
                                                   : select_fin<FADE_BF16>(d->D, pl.NT);
     if (!fk.fn) return FADE_ERR_UNSUPPORTED;
     void* fargs[] = {(void*)&fp};
     FADE_CUDA_TRY(launch_pdl(fk.fn, dim3((unsigned)Z), dim3(kFinThreads), (size_t)fk.smem, s, fargs));
     return FADE_OK;
+}
+
+extern "C" int fade_decode_attn(const fade_decode_desc* d, void* workspace, size_t ws_bytes,
+                                void* stream) {
+    return decode_attn_impl(d, nullptr, workspace, ws_bytes, stream);
+}
+
+extern "C" int fade_decode_attn_age_out(const fade_decode_desc* d, const fade_age_out_desc* a,
+                                        void* workspace, size_t ws_bytes, void* stream) {
+    if (!a) return FADE_ERR_INVALID_ARG;
+    return decode_attn_impl(d, a, workspace, ws_bytes, stream);
 }
 
 extern "C" int fade_workspace_check(void* workspace, size_t ws_bytes, void* stream) {

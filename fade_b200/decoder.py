@@ -9,12 +9,12 @@ lockstep (the reference's shared-tier batching, fade/cache.py:136-161):
   K per-channel scale [B, Hkv, 1, D], V per-token scale [B, Hkv, cap, 1],
   valid length mid_len [B] (int32, on the device).
 
-One decode step of one layer = two C-ABI calls:
-  1. ``fade_age_out_int4``: the oldest ring token is quantised into the
-     middle (K against its frozen per-channel scale, V with its own per-token
-     scale) and the new token takes its ring slot;
-  2. ``fade_decode_attn``: attention of the layer's query over sink + middle +
-     ring, straight from the compressed tiers.
+One decode step of one layer is one C-ABI call, ``fade_decode_attn_age_out``:
+the oldest ring token is quantised into the middle (K against its frozen
+per-channel scale, V with its own per-token scale), the new token takes its
+ring slot, and the layer's query attends over sink + middle + ring straight
+from the compressed tiers.  ``fused=False`` issues the same step as the two
+separate calls ``fade_age_out_int4`` + ``fade_decode_attn``.
 All positions live in device memory, so ``capture()`` records the whole
 multi-layer step in one CUDA graph and ``replay()`` re-runs it.
 
@@ -76,7 +76,7 @@ def age_out_int4(ring_k: Tensor, ring_v: Tensor, mid_kq: Tensor, mid_vq: Tensor,
 
 class _Layer:
     __slots__ = ("sink_k", "sink_v", "ring_k", "ring_v", "mid_kq", "mid_ks", "mid_vq", "mid_vs",
-                 "mid_len", "ring_origin", "plan", "age_args")
+                 "mid_len", "ring_origin", "plan", "age_args", "age_desc")
 
 
 class TieredDecoder:
@@ -91,12 +91,14 @@ class TieredDecoder:
 
     def __init__(self, n_layers: int, batch: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
                  dtype: torch.dtype = torch.bfloat16, n_sink: int = 4, recent_window: int = 64,
-                 mid_capacity: int = 8192, device: torch.device | str = "cuda", sm_scale: float | None = None):
+                 mid_capacity: int = 8192, device: torch.device | str = "cuda", sm_scale: float | None = None,
+                 fused: bool = True):
         self.L, self.B, self.Hq, self.Hkv, self.D = n_layers, batch, n_q_heads, n_kv_heads, head_dim
         self.dtype, self.n_sink, self.R = dtype, n_sink, recent_window
         self.cap = int(-(-mid_capacity // 128) * 128)
         self.device = torch.device(device)
         self.sm_scale = sm_scale
+        self.fused = fused
         B, H, D = batch, n_kv_heads, head_dim
         dev = self.device
         self.q = torch.zeros(n_layers, B, n_q_heads, 1, D, dtype=dtype, device=dev)
@@ -190,6 +192,15 @@ class TieredDecoder:
                 ly.mid_kq.stride(1) // rbk, self.cap, ly.mid_len.data_ptr(), kn.data_ptr(), vn.data_ptr(),
                 kn.stride(0), kn.stride(1),
             )
+            a = _lib.AgeOutDesc()
+            a.ring_seg, a.mid_seg = 2, 1
+            a.ring_cap, a.ring_origin = R, int(ly.ring_origin)
+            a.k_new, a.v_new = kn.data_ptr(), vn.data_ptr()
+            a.new_sb, a.new_sh = kn.stride(0), kn.stride(1)
+            # the kernel preceding each layer's call never writes this layer's
+            # tiers (only this call does), so the middle may stream early
+            a.prefetch_tiers = 1
+            ly.age_desc = a
         return ly.plan
 
     # ------------------------------------------------------------------- step
@@ -198,11 +209,18 @@ class TieredDecoder:
         st = _lib.bind(self.device)
         for i, ly in enumerate(self.layers):
             p = self._plan(i)
-            _lib.check(lib.fade_age_out_int4(*ly.age_args, st), "age_out_int4")
-            if layer_events is not None:
-                layer_events[i][0].record()
-            _lib.check(lib.fade_decode_attn(ctypes.byref(p.desc), p.workspace.data_ptr(), p.ws_bytes, st),
-                       "fade_decode_attn")
+            if self.fused:
+                if layer_events is not None:
+                    layer_events[i][0].record()
+                _lib.check(lib.fade_decode_attn_age_out(ctypes.byref(p.desc), ctypes.byref(ly.age_desc),
+                                                        p.workspace.data_ptr(), p.ws_bytes, st),
+                           "fade_decode_attn_age_out")
+            else:
+                _lib.check(lib.fade_age_out_int4(*ly.age_args, st), "age_out_int4")
+                if layer_events is not None:
+                    layer_events[i][0].record()
+                _lib.check(lib.fade_decode_attn(ctypes.byref(p.desc), p.workspace.data_ptr(), p.ws_bytes, st),
+                           "fade_decode_attn")
             if layer_events is not None:
                 layer_events[i][1].record()
 

@@ -228,8 +228,9 @@ typedef struct fade_decode_desc {
 } fade_decode_desc;
 
 /* Bytes of zero-initialised workspace fade_decode_attn needs for `d`.  The
- * workspace carries split-K partials, per-row arrival counters (reset by
- * every call) and an error word; zero-fill it once when allocating it. */
+ * workspace carries split-K partials, an error word and the age-out
+ * counters of fade_decode_attn_age_out (each returns to zero by the end of
+ * every call); zero-fill it once when allocating it. */
 size_t fade_decode_attn_workspace_size(const fade_decode_desc* d);
 
 /* Attention of q over the union of all segments' tokens (order-free):
@@ -237,6 +238,35 @@ size_t fade_decode_attn_workspace_size(const fade_decode_desc* d);
  * Quantised tiers are dequantised in registers; K/V never round-trip HBM. */
 int fade_decode_attn(const fade_decode_desc* d, void* workspace, size_t ws_bytes,
                      void* stream);
+
+/* One decode step of one layer: fade_age_out_int4 followed by
+ * fade_decode_attn, fused (no counterpart in the reference, which keeps new
+ * tokens in FP16 until its next reassignment, fade/cache.py:881-1057).
+ * seg[ring_seg] is the FP recent-window ring (rows of D, row_sb / row_sh
+ * strides, ring_cap rows per (b,h)); seg[mid_seg] the FADE_SEG_INT4 middle
+ * with device lengths `lens` (= mid_len [B]) and capacity max_len.  For each b,
+ * with n = lens[b] and slot = (n - ring_origin) mod ring_cap, when n < max_len
+ * the result equals: quantise ring token `slot` into middle row n (K against
+ * its frozen per-channel scale, V with its own per-token scale, exactly as
+ * fade_age_out_int4), put k_new/v_new ([B,Hkv,D], strides new_sb / new_sh)
+ * into the freed slot, lens[b] = n + 1, then attention over all tiers
+ * (n_q must be 1).  Rows with n >= max_len are attended unchanged and the new
+ * token is dropped, as fade_age_out_int4 does.
+ * With prefetch_tiers = 1 the call may read the cache tiers (not q, k_new,
+ * v_new) before the preceding kernel on the stream has finished: set it only
+ * when that kernel does not write them. */
+typedef struct fade_age_out_desc {
+    int32_t ring_seg, mid_seg;
+    int64_t ring_cap, ring_origin;
+    const void* k_new;
+    const void* v_new;
+    int64_t new_sb, new_sh;          /* elements */
+    int32_t prefetch_tiers;
+    int32_t reserved;
+} fade_age_out_desc;
+
+int fade_decode_attn_age_out(const fade_decode_desc* d, const fade_age_out_desc* a,
+                             void* workspace, size_t ws_bytes, void* stream);
 
 /* No counterpart in the reference.  fade_decode_attn without a workspace
  * argument, for callers that cannot allocate device memory when they run

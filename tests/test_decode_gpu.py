@@ -8,10 +8,10 @@ import pytest
 import torch
 
 from conftest import golden
-from gpu_util import assert_attn_close, np_to_dt_tensor, seeded_outliers, t_from_bits, t_vals
+from gpu_util import assert_attn_close, np_to_dt_tensor, seeded_outliers, t_bits, t_from_bits, t_vals
 from oracle import attention as oa
 from oracle import quant as oq
-from oracle.numerics import from_bits
+from oracle.numerics import from_bits, to_bits
 
 pytestmark = pytest.mark.gpu
 TOL = {"f16": 2e-3, "bf16": 1e-2}   # north-star max-abs tolerances (see assert_attn_close)
@@ -215,13 +215,20 @@ def test_repeat_calls_are_stable(cuda_device):
         assert torch.equal(a, b)
 
 
-def test_decoder_step_matches_oracle(cuda_device):
-    """Multi-layer TieredDecoder: age-out + attention per layer, eager and graph-captured."""
+@pytest.mark.parametrize("fused,S,cap", [(True, 600, 600), (False, 600, 600), (True, 194, 128), (False, 194, 128)])
+def test_decoder_step_matches_oracle(cuda_device, fused, S, cap):
+    """Multi-layer TieredDecoder: age-out + attention per layer, eager and
+    graph-captured, as one fused call per layer or as age-out + attention.
+    cap=128 with a 126-token middle runs into the capacity: later steps attend
+    the unchanged tiers and drop the new token.  The stored tiers (codes,
+    scales, ring) must match the oracle bit for bit."""
     from fade_b200.decoder import TieredDecoder
 
     dt = "bf16"
-    L, B, Hq, Hkv, D, S = 2, 2, 8, 2, 128, 600
-    dec = TieredDecoder(L, B, Hq, Hkv, D, dtype=torch.bfloat16, n_sink=4, recent_window=64, mid_capacity=600)
+    L, B, Hq, Hkv, D = 2, 2, 8, 2, 128
+    dec = TieredDecoder(L, B, Hq, Hkv, D, dtype=torch.bfloat16, n_sink=4, recent_window=64, mid_capacity=cap,
+                        fused=fused)
+    cap_r = -(-cap // 128) * 128
     ks_np, vs_np = [], []
     for l in range(L):
         k = seeded_outliers((B, Hkv, S, D), 100 + l, dt)
@@ -247,16 +254,26 @@ def test_decoder_step_matches_oracle(cuda_device):
         out = t_vals(dec.step(np_to_dt_tensor(q, dt), np_to_dt_tensor(kn, dt), np_to_dt_tensor(vn, dt)))
         for l in range(L):
             s = state[l]
-            slot = (s["n"] - s["origin"]) % 64
-            akp, avp, avs = oq.age_out_int4(s["ring_k"][:, :, slot], s["ring_v"][:, :, slot], s["mid_ks"][:, :, 0], dt)
-            s["mid_kq"] = np.concatenate([s["mid_kq"], akp[:, :, None]], axis=2)
-            s["mid_vq"] = np.concatenate([s["mid_vq"], avp[:, :, None]], axis=2)
-            s["mid_vs"] = np.concatenate([s["mid_vs"], avs[:, :, None, None]], axis=2)
-            s["ring_k"][:, :, slot] = kn[l]
-            s["ring_v"][:, :, slot] = vn[l]
-            s["n"] += 1
+            if s["n"] < cap_r:
+                slot = (s["n"] - s["origin"]) % 64
+                akp, avp, avs = oq.age_out_int4(s["ring_k"][:, :, slot], s["ring_v"][:, :, slot], s["mid_ks"][:, :, 0],
+                                                dt)
+                s["mid_kq"] = np.concatenate([s["mid_kq"], akp[:, :, None]], axis=2)
+                s["mid_vq"] = np.concatenate([s["mid_vq"], avp[:, :, None]], axis=2)
+                s["mid_vs"] = np.concatenate([s["mid_vs"], avs[:, :, None, None]], axis=2)
+                s["ring_k"][:, :, slot] = kn[l]
+                s["ring_v"][:, :, slot] = vn[l]
+                s["n"] += 1
             tiers = {"sink_k": s["sink_k"], "sink_v": s["sink_v"], "int4_kq": s["mid_kq"], "int4_ks": s["mid_ks"],
                      "int4_vq": s["mid_vq"], "int4_vs": s["mid_vs"], "recent_k": s["ring_k"], "recent_v": s["ring_v"]}
             ref = oa.tiered_attention(q[l], tiers, dt)
             assert_attn_close(out[l], ref, dt, TOL[dt])
-    assert dec.mid_lengths() == [S - 68 + 4] * L
+    assert dec.mid_lengths() == [min(S - 68 + 4, cap_r)] * L
+    for l in range(L):
+        s, ly = state[l], dec.layers[l]
+        n = s["n"]
+        np.testing.assert_array_equal(ly.mid_kq[:, :, :n].cpu().numpy(), s["mid_kq"])
+        np.testing.assert_array_equal(ly.mid_vq[:, :, :n].cpu().numpy(), s["mid_vq"])
+        np.testing.assert_array_equal(t_bits(ly.mid_vs[:, :, :n]), to_bits(s["mid_vs"], dt))
+        np.testing.assert_array_equal(t_bits(ly.ring_k), to_bits(s["ring_k"], dt))
+        np.testing.assert_array_equal(t_bits(ly.ring_v), to_bits(s["ring_v"], dt))
