@@ -1156,6 +1156,7 @@ finish_kernel(FinParams p) {
     constexpr int D2 = D / 2;
     constexpr int OUTS = (ROWS * D2 + kFinThreads - 1) / kFinThreads;   // (row, channel pair) per thread
     constexpr int NW = kFinThreads / 32;
+    constexpr int PRE = 8;           // middle partials whose outputs are fetched with their statistics
     extern __shared__ __align__(16) uint8_t fsm[];
     T* ksm = reinterpret_cast<T*>(fsm + L::K_OFF);
     T* vsm = reinterpret_cast<T*>(fsm + L::V_OFF);
@@ -1164,9 +1165,10 @@ finish_kernel(FinParams p) {
     float* m_row = reinterpret_cast<float*>(fsm + L::ST_OFF);
     float* l_row = m_row + ROWS;
     float* c_row = m_row + 2 * ROWS;   // per-pass rescale factor
-    float* f_row = m_row + 3 * ROWS;   // final FP weight / 1 / L
+    float* f_row = m_row + 3 * ROWS;   // 1 / L
     float* sw = reinterpret_cast<float*>(fsm + L::SW_OFF);
     float* sl = reinterpret_cast<float*>(fsm + L::SL_OFF);
+    __shared__ int s_age[2];   // [0] = n (middle length before the step), [1] = last CTA of b
 
     const int z = blockIdx.x;
     const int b = z / p.Hkv, h = z % p.Hkv;
@@ -1176,31 +1178,18 @@ finish_kernel(FinParams p) {
     if (!p.has_mid) griddep_wait();
     griddep_launch_dependents();
 
-    // ---- fused age-out: this row's middle length, ring slot, arrival ----
-    __shared__ int s_age[2];   // [0] = n (middle length before the step), [1] = last CTA of b
-    int64_t age_n = 0, age_slot = -1;
-    bool room = false;
-    if (p.age) {
-        if (tid == 0) {
-            const int n = p.mid_len[b];
-            // acq_rel: this CTA's read of mid_len[b] happens before the write
-            // of n + 1 by the last CTA of b (which observes this increment)
-            int old;
-            asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.age_cnt + b) : "memory");
-            s_age[0] = n;
-            s_age[1] = (old == p.Hkv - 1) ? 1 : 0;
-        }
-        __syncthreads();
-        age_n = s_age[0];
-        room = age_n < p.mid_cap;
-        if (room) {
-            age_slot = (age_n - p.ring_origin) % p.ring_cap;
-            if (age_slot < 0) age_slot += p.ring_cap;
-        }
+    // ---- fused age-out: fetch this row's middle length and count this CTA
+    //      (acq_rel: the read of mid_len[b] happens before the write of n + 1
+    //      by the last CTA of b, which observes this increment).  The values
+    //      are consumed after the FP tokens have been requested. ----
+    int age_n_ld = 0, age_old = 0;
+    if (p.age && tid == 0) {
+        age_n_ld = p.mid_len[b];
+        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(age_old) : "l"(p.age_cnt + b) : "memory");
     }
     // ---- FP segments of this row: lengths and first rows ----
     int64_t seg_len_[FADE_MAX_SEGMENTS], seg_row_[FADE_MAX_SEGMENTS];
-    int64_t n_tok = 0;
+    int64_t n_seg_tok = 0;
 #pragma unroll
     for (int s = 0; s < FADE_MAX_SEGMENTS; ++s) {
         seg_len_[s] = 0;
@@ -1209,47 +1198,25 @@ finish_kernel(FinParams p) {
             const FpSeg& sg = p.fp[s];
             seg_len_[s] = sg.lens ? (int64_t)sg.lens[b] : sg.len;
             seg_row_[s] = sg.row_base ? sg.row_base[z] : (int64_t)b * sg.row_sb + (int64_t)h * sg.row_sh;
-            n_tok += seg_len_[s];
+            n_seg_tok += seg_len_[s];
         }
     }
-    // Token order: the FP segments' tokens, then (age-out with room) the new
-    // token.  The ring token at age_slot stays in the list: after staging it
-    // is replaced in shared memory by its INT4 round trip (it moves to the
-    // middle in this step), and the new token takes its ring slot.
-    int64_t ft_aged = -1;
-    const int64_t n_seg_tok = n_tok;
-    if (room) {
-        ft_aged = age_slot;
-        for (int s = 0; s < p.ring_fp; ++s) ft_aged += seg_len_[s];
-        n_tok += 1;
-    }
-    // ---- queries, pre-scaled into the log2 domain ----
-    for (int i = tid; i < ROWS * D; i += kFinThreads) {
-        const int r = i / D, d = i % D;
-        float v = 0.f;
-        if (r < rows) {
-            const int j = r / p.n_q, sq = r % p.n_q;
-            v = load_f<DT>(p.q, (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss + d) *
-                p.qk_scale;
-        }
-        qsm[i] = v;
-    }
-    if (tid < ROWS) { m_row[tid] = -INFINITY; l_row[tid] = 0.f; }
-    float acc_f[OUTS][2];
-#pragma unroll
-    for (int k = 0; k < OUTS; ++k) acc_f[k][0] = acc_f[k][1] = 0.f;
+    // Token order: the FP segments' tokens, then (age-out) the step's new
+    // token, staged before it is known whether the middle has room (without
+    // room it is left out of the softmax).  The ring token at the aged slot
+    // stays in the list: after staging it is replaced in shared memory by its
+    // INT4 round trip (it moves to the middle in this step), and the new token
+    // takes its ring slot.
+    const int64_t n_tok = n_seg_tok + (p.age ? 1 : 0);
 
-    for (int64_t t0 = 0; t0 < n_tok; t0 += kFinChunk) {
-        const int n = (int)((n_tok - t0) < kFinChunk ? (n_tok - t0) : kFinChunk);
-        __syncthreads();   // previous pass finished reading ksm / vsm / psm
-        // ---- stage K and V rows of tokens t0 .. t0+n-1 ----
+    auto stage = [&](int64_t t0, int n) {
         constexpr int PCS = D / 8;   // 16-byte pieces per row
         for (int i = tid; i < n * PCS; i += kFinThreads) {
             const int tk = i / PCS, c = i % PCS;
             int64_t ft = t0 + tk;
             const T* ks;
             const T* vs;
-            if (ft >= n_seg_tok) {   // the step's new token (fused age-out)
+            if (ft >= n_seg_tok) {   // the step's new token
                 const int64_t off = (int64_t)b * p.new_sb + (int64_t)h * p.new_sh + c * 8;
                 ks = reinterpret_cast<const T*>(p.k_new) + off;
                 vs = reinterpret_cast<const T*>(p.v_new) + off;
@@ -1273,6 +1240,50 @@ finish_kernel(FinParams p) {
                     vd[e] = vs[e];
                 }
             }
+        }
+    };
+    if (n_tok > 0) stage(0, (int)(n_tok < kFinChunk ? n_tok : kFinChunk));
+
+    // ---- queries, pre-scaled into the log2 domain ----
+    for (int i = tid; i < ROWS * D; i += kFinThreads) {
+        const int r = i / D, d = i % D;
+        float v = 0.f;
+        if (r < rows) {
+            const int j = r / p.n_q, sq = r % p.n_q;
+            v = load_f<DT>(p.q, (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss + d) *
+                p.qk_scale;
+        }
+        qsm[i] = v;
+    }
+    if (tid < ROWS) { m_row[tid] = -INFINITY; l_row[tid] = 0.f; }
+    if (p.age && tid == 0) {
+        s_age[0] = age_n_ld;
+        s_age[1] = (age_old == p.Hkv - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    int64_t age_n = 0, age_slot = -1, ft_aged = -1, ft_new = -1;
+    bool room = false;
+    if (p.age) {
+        age_n = s_age[0];
+        room = age_n < p.mid_cap;
+        ft_new = n_seg_tok;
+        if (room) {
+            age_slot = (age_n - p.ring_origin) % p.ring_cap;
+            if (age_slot < 0) age_slot += p.ring_cap;
+            ft_aged = age_slot;
+            for (int s = 0; s < p.ring_fp; ++s) ft_aged += seg_len_[s];
+        }
+    }
+
+    float acc_f[OUTS][2];
+#pragma unroll
+    for (int k = 0; k < OUTS; ++k) acc_f[k][0] = acc_f[k][1] = 0.f;
+
+    for (int64_t t0 = 0; t0 < n_tok; t0 += kFinChunk) {
+        const int n = (int)((n_tok - t0) < kFinChunk ? (n_tok - t0) : kFinChunk);
+        if (t0 > 0) {
+            __syncthreads();   // previous pass finished reading ksm / vsm / psm
+            stage(t0, n);
         }
         cp_async_wait_all();
         __syncthreads();
@@ -1340,7 +1351,8 @@ finish_kernel(FinParams p) {
                 a0 = fmaf(q1.z, Elem<DT>::to_f(e8[6]), a0);
                 a1 = fmaf(q1.w, Elem<DT>::to_f(e8[7]), a1);
             }
-            psm[r * kFinChunk + tk] = a0 + a1;
+            // the new token is attended only when the middle had room
+            psm[r * kFinChunk + tk] = (t0 + tk == ft_new && !room) ? -INFINITY : a0 + a1;
         }
         __syncthreads();
         // ---- online softmax per row (one warp per row) ----
@@ -1353,7 +1365,8 @@ finish_kernel(FinParams p) {
             const float mnew = fmaxf(mold, mx);
             float sum = 0.f;
             for (int tk = lane; tk < n; tk += 32) {
-                const float e = ex2(psm[r * kFinChunk + tk] - mnew);
+                const float sv = psm[r * kFinChunk + tk];
+                const float e = (sv == -INFINITY) ? 0.f : ex2(sv - mnew);
                 psm[r * kFinChunk + tk] = e;
                 sum += e;
             }
@@ -1408,15 +1421,31 @@ finish_kernel(FinParams p) {
             nsl = cta_of_unit(ze - 1, C, U) - c0 + 1;
         }
     }
+    auto slot_of = [&](int j) {
+        const int uc = (int)((int64_t)(c0 + j) * U / C);
+        return uc > zb ? uc : zb;
+    };
     __syncthreads();   // FP statistics complete
     for (int j0 = 0; j0 < nsl; j0 += kFinSlots) {
         const int nj = (nsl - j0) < kFinSlots ? (nsl - j0) : kFinSlots;
-        __syncthreads();
+        if (j0 > 0) __syncthreads();
+        // outputs of the first PRE partials are requested together with the
+        // statistics: one memory round trip for the usual handful of partials
+        float2 pre[PRE][OUTS];
+#pragma unroll
+        for (int j = 0; j < PRE; ++j)
+#pragma unroll
+            for (int k = 0; k < OUTS; ++k) {
+                const int i = tid + k * kFinThreads;
+                pre[j][k] = make_float2(0.f, 0.f);
+                if (j < nj && i < rows * D2) {
+                    const int r = i / D2, d2 = i % D2;
+                    pre[j][k] = *reinterpret_cast<const float2*>(p.ws_o + ((int64_t)slot_of(j0 + j) * rows + r) * D + 2 * d2);
+                }
+            }
         for (int i = tid; i < nj * rows; i += kFinThreads) {
             const int j = i / rows, r = i % rows;
-            const int uc = (int)((int64_t)(c0 + j0 + j) * U / C);
-            const int slot = uc > zb ? uc : zb;
-            const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + ((int64_t)slot * rows + r) * 2);
+            const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + ((int64_t)slot_of(j0 + j) * rows + r) * 2);
             sw[j * ROWS + r] = ml.x;
             sl[j * ROWS + r] = ml.y;
         }
@@ -1448,13 +1477,17 @@ finish_kernel(FinParams p) {
             float a0 = acc_m[k][0] * corr, a1 = acc_m[k][1] * corr;
             acc_f[k][0] *= corr;
             acc_f[k][1] *= corr;
-#pragma unroll 4
-            for (int j = 0; j < nj; ++j) {
+#pragma unroll
+            for (int j = 0; j < PRE; ++j) {
+                if (j >= nj) break;
+                const float w = sw[j * ROWS + r];
+                a0 = fmaf(w, pre[j][k].x, a0);
+                a1 = fmaf(w, pre[j][k].y, a1);
+            }
+            for (int j = PRE; j < nj; ++j) {
                 const float w = sw[j * ROWS + r];
                 if (w == 0.f) continue;
-                const int uc = (int)((int64_t)(c0 + j0 + j) * U / C);
-                const int slot = uc > zb ? uc : zb;
-                const float2 ov = *reinterpret_cast<const float2*>(p.ws_o + ((int64_t)slot * rows + r) * D + 2 * d2);
+                const float2 ov = *reinterpret_cast<const float2*>(p.ws_o + ((int64_t)slot_of(j0 + j) * rows + r) * D + 2 * d2);
                 a0 = fmaf(w, ov.x, a0);
                 a1 = fmaf(w, ov.y, a1);
             }
