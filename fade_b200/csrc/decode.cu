@@ -63,8 +63,10 @@ __device__ __forceinline__ unsigned long long gtimer() {
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
-#define FADE_TR(slot) do { if (threadIdx.x == 0 && blockIdx.x < 1024 && (slot) < kTraceEv) g_trace[blockIdx.x * kTraceEv + (slot)] = gtimer(); } while (0)
-#define FADE_TRP(slot) do { if (threadIdx.x == kConsumerWarps * 32 && blockIdx.x < 1024 && (slot) < kTraceEv) g_trace[blockIdx.x * kTraceEv + (slot)] = gtimer(); } while (0)
+// middle CTA c: row 4c + group for the consumer groups (lane 0 of the
+// group's first warp), row 4c + 3 for the producer
+#define FADE_TR(slot) do { if ((threadIdx.x & 127) == 0 && threadIdx.x < blockDim.x - 32 && blockIdx.x < 192 && (slot) < kTraceEv) g_trace[(blockIdx.x * 4 + threadIdx.x / 128) * kTraceEv + (slot)] = gtimer(); } while (0)
+#define FADE_TRP(slot) do { if (threadIdx.x == blockDim.x - 32 && blockIdx.x < 192 && (slot) < kTraceEv) g_trace[(blockIdx.x * 4 + 3) * kTraceEv + (slot)] = gtimer(); } while (0)
 // finisher CTAs record into rows 768.. of the same array
 #define FADE_TRF(slot) do { if (threadIdx.x == 0 && blockIdx.x < 256) g_trace[(768 + blockIdx.x) * kTraceEv + (slot)] = gtimer(); } while (0)
 #else
@@ -72,10 +74,17 @@ __device__ __forceinline__ unsigned long long gtimer() {
 #define FADE_TR(slot) do {} while (0)
 #define FADE_TRP(slot) do {} while (0)
 #endif
-constexpr int kConsumerWarps = 4;
-constexpr int kMidThreads = (kConsumerWarps + 1) * 32;
+constexpr int kConsumerWarps = 4;  // per consumer group; 32 tokens of a stage each
 constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
-constexpr int kStages = 4;
+// One middle CTA per SM: G consumer groups (3 for up to 8 query rows per kv
+// head; 1 above, where the wider state needs the registers) share one
+// producer warp and one ring of stages; group g
+// consumes stages g, g+G, g+2G, ...
+__host__ __device__ constexpr int mid_groups(int NT) { return NT == 1 ? 3 : 1; }
+// + the producer warp + the FP-tier warp
+__host__ __device__ constexpr int mid_threads(int NT) { return (mid_groups(NT) * kConsumerWarps + 2) * 32; }
+constexpr int kMidMaxStages = 15;
+constexpr int kSmemPerBlock = 232448;  // 227 KB opt-in shared memory per CTA
 constexpr float kLog2e = 1.4426950408889634f;
 // Initial running maximum of the middle kernel's online softmax: finite and
 // below any real score, so exp2(score - max) never sees inf - inf.
@@ -306,6 +315,15 @@ template <> struct ChanMap<2> {
 // ---------------------------------------------------------------------------
 // Kernel parameters
 // ---------------------------------------------------------------------------
+struct FpSeg {
+    const void* k;
+    const void* v;
+    int64_t row_sb, row_sh;
+    const int64_t* row_base;
+    const int32_t* lens;
+    int64_t len;
+};
+
 struct MidParams {
     int dtype;
     int B, Hq, Hkv, D, n_q, g, rows;
@@ -330,6 +348,25 @@ struct MidParams {
     int scale_tma;                  // V scales arrive by TMA (row starts 8-aligned)
     int q_vec;                      // q / k_scale rows allow 16-byte loads
     int early;                      // producer may stream before the previous kernel ends
+    // FP tiers (the FP warp): segments, the model-dtype query, partial outputs
+    int n_fp;
+    FpSeg fp[FADE_MAX_SEGMENTS];
+    const void* qo;                 // dtype [B,Hq,n_q,D]
+    int64_t qo_sb, qo_sh, qo_ss;
+    float* ws_fpml;                 // [Z][rows][2]
+    float* ws_fpo;                  // [Z][rows][D]
+    // fused age-out (fade_decode_attn_age_out), age == 0 otherwise
+    int age;
+    int ring_fp;                    // index into fp[] of the recent-window ring
+    int64_t ring_cap, ring_origin;
+    const void* k_new;              // [B,Hkv,D]
+    const void* v_new;
+    int64_t new_sb, new_sh;
+    int64_t mid_cap;
+    const int32_t* mid_len;         // = lens
+    uint8_t* age_k;                 // = the middle's code rows, written at row n
+    uint8_t* age_v;
+    int* ws_age;                    // [Z] middle length after the step
 };
 
 __device__ __forceinline__ int64_t seg_len(const MidParams& p, int b) {
@@ -381,13 +418,24 @@ struct MidLayout {
     static constexpr int V_OFF = K_BYTES;
     static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
     static_assert(K_BYTES % 1024 == 0 && V_BYTES % 1024 == 0, "stage regions must stay 1 KB aligned");
-    static constexpr int SC_BASE = kStages * STAGE_BYTES;
-    static constexpr int RING_BYTES = SC_BASE + kStages * SC_BYTES;
-    static constexpr int OBUF_BYTES = 2 * NT * 8 * D * 4;                 // 2 half-sums of the CTA partial
-    static constexpr int ML_BYTES = 2 * kConsumerWarps * NT * 8 * 2 * 4;  // per-warp row stats, 2 buffers
-    static constexpr int BAR_OFF = RING_BYTES + OBUF_BYTES + ML_BYTES;
-    static constexpr int FLAG_OFF = BAR_OFF + 2 * kStages * 8;
-    static constexpr int SMEM_BYTES = FLAG_OFF + 16 + 1024;  // +1024 for alignment
+    static constexpr int G = mid_groups(NT);
+    static constexpr int OBUF_BYTES = 2 * NT * 8 * D * 4;                 // per group: 2 half-sums of a partial
+    static constexpr int ML_BYTES = 2 * kConsumerWarps * NT * 8 * 2 * 4;  // per group: per-warp row stats, 2 buffers
+    // as many stages as shared memory holds (a multiple of G, so each ring
+    // slot always serves the same group)
+    static constexpr int AB_BYTES = 8 * D;   // FP warp: aged + new token, K and V
+    static constexpr int NS_FIT = (kSmemPerBlock - 1024 - 16 - AB_BYTES - 2 * kMidMaxStages * 8 -
+                                   G * (OBUF_BYTES + ML_BYTES)) /
+                                  (STAGE_BYTES + SC_BYTES);
+    static constexpr int NS = ((NS_FIT < kMidMaxStages ? NS_FIT : kMidMaxStages) / G) * G;
+    static_assert(NS >= 2 * G, "shared memory too small for the stage ring");
+    static constexpr int SC_BASE = NS * STAGE_BYTES;
+    static constexpr int RING_BYTES = SC_BASE + NS * SC_BYTES;
+    static constexpr int BAR_OFF = RING_BYTES + G * (OBUF_BYTES + ML_BYTES);
+    static constexpr int FLAG_OFF = BAR_OFF + 2 * NS * 8;
+    static constexpr int AB_OFF = FLAG_OFF + 16;
+    static constexpr int SMEM_BYTES = AB_OFF + AB_BYTES + 1024;  // +1024 for alignment
+    static_assert(SMEM_BYTES <= kSmemPerBlock, "middle kernel shared memory over the per-CTA limit");
 };
 
 
@@ -446,14 +494,310 @@ __device__ __forceinline__ void load_tiles(uint32_t base, int trow0, int lane, u
 }
 
 // ---------------------------------------------------------------------------
+// FP-tier warp of the middle kernel (one per CTA): attention over the FP
+// tiers (sinks, recent window) of the rows z in [c*Z/n, (c+1)*Z/n), written as
+// one un-normalised partial per row for the finisher, while the consumer
+// groups stream the middle.  With the fused age-out it also moves the oldest
+// ring token into the middle (INT4 codes exactly as fade_age_out_int4) and
+// attends the step's tokens: the aged token as its INT4 round trip and the
+// new token, both staged in shared memory; the aged ring slot is masked.
+// Fragments come straight from global memory (16-byte K loads, 8-byte V
+// loads) in the layouts of the consumer path: K channels in ChanMap<4> order
+// (the query fragments use the same order), O^T rows by ChanMap<4>::vdim.
+// ---------------------------------------------------------------------------
+template <int DT, int D, int NT>
+__device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, uint8_t* abuf) {
+    using T = typename Elem<DT>::T;
+    using P = Pk<DT>;
+    using KMap = ChanMap<4>;
+    using VMap = ChanMap<4>;
+    constexpr int KSTEPS = D / 16, MT = D / 16, NCB = D / 32;
+    constexpr int DPL = D / 32;   // channels per lane in the age-out
+    const int lane = threadIdx.x % 32, gid = lane >> 2, t = lane & 3;
+    const int Z = p.B * p.Hkv;
+    const int z0 = (int)((int64_t)c * Z / n_cta), z1 = (int)((int64_t)(c + 1) * Z / n_cta);
+    T* ab = reinterpret_cast<T*>(abuf);   // [2 tokens][K, V][D]: aged, new
+    for (int z = z0; z < z1; ++z) {
+        const int b = z / p.Hkv, h = z % p.Hkv;
+        // ---- FP segments of the row ----
+        int64_t sl[FADE_MAX_SEGMENTS], sr[FADE_MAX_SEGMENTS], T_seg = 0;
+#pragma unroll
+        for (int s = 0; s < FADE_MAX_SEGMENTS; ++s) {
+            sl[s] = 0;
+            sr[s] = 0;
+            if (s < p.n_fp) {
+                sl[s] = p.fp[s].lens ? (int64_t)p.fp[s].lens[b] : p.fp[s].len;
+                sr[s] = p.fp[s].row_base ? p.fp[s].row_base[z] : (int64_t)b * p.fp[s].row_sb + (int64_t)h * p.fp[s].row_sh;
+                T_seg += sl[s];
+            }
+        }
+        // ---- fused age-out ----
+        int64_t n = 0, ft_aged = -1;
+        bool room = false;
+        if (p.age) {
+            n = p.mid_len[b];
+            room = n < p.mid_cap;
+        }
+        if (room) {
+            int64_t slot = (n - p.ring_origin) % p.ring_cap;
+            if (slot < 0) slot += p.ring_cap;
+            ft_aged = slot;
+            for (int s = 0; s < p.ring_fp; ++s) ft_aged += sl[s];
+            T* rk = reinterpret_cast<T*>(const_cast<void*>(p.fp[p.ring_fp].k)) + (sr[p.ring_fp] + slot) * D;
+            T* rv = reinterpret_cast<T*>(const_cast<void*>(p.fp[p.ring_fp].v)) + (sr[p.ring_fp] + slot) * D;
+            const T* kn = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
+            const T* vn = reinterpret_cast<const T*>(p.v_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
+            const T* ksc = reinterpret_cast<const T*>(p.k_scale) + (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
+            float kx[DPL], vx[DPL], sc[DPL];
+            T knv[DPL], vnv[DPL];
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) {
+                const int d = lane * DPL + i;
+                kx[i] = Elem<DT>::to_f(rk[d]);
+                vx[i] = Elem<DT>::to_f(rv[d]);
+                sc[i] = Elem<DT>::to_f(ksc[d]);
+                knv[i] = kn[d];
+                vnv[i] = vn[d];
+            }
+            float m = 0.f;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) m = fmaxf(m, fabsf(vx[i]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            m = fmaxf(m, Elem<DT>::eps());
+            const float inv = inv_scale<DT>(m, 7.f);
+            const float vsc = Elem<DT>::rnd(__fdiv_rn(m, 7.f));
+            const int64_t mrow = (p.row_base ? p.row_base[z] : (int64_t)b * p.row_sb + (int64_t)h * p.row_sh) + n;
+            if (lane == 0) reinterpret_cast<T*>(const_cast<void*>(p.v_scale))[mrow] = Elem<DT>::from_f(vsc);
+#pragma unroll
+            for (int i = 0; i < DPL; i += 2) {
+                int kq[2], vq[2];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int d = lane * DPL + i + j;
+                    kq[j] = (sc[i + j] > 0.f) ? quant_code(__fdiv_rn(kx[i + j], sc[i + j]), -8.f, 7.f) : 0;
+                    vq[j] = quant_code(Elem<DT>::rnd(__fmul_rn(vx[i + j], inv)), -8.f, 7.f);
+                    ab[0 * 2 * D + d] = Elem<DT>::from_f((float)kq[j] * sc[i + j]);   // aged K
+                    ab[0 * 2 * D + D + d] = Elem<DT>::from_f((float)vq[j] * vsc);     // aged V
+                    ab[1 * 2 * D + d] = knv[i + j];                                   // new K
+                    ab[1 * 2 * D + D + d] = vnv[i + j];                               // new V
+                }
+                const int pp = (lane * DPL + i) / 2;
+                p.age_k[mrow * (D / 2) + pp] = (uint8_t)(((kq[0] & 15) << 4) | (kq[1] & 15));
+                p.age_v[mrow * (D / 2) + pp] = (uint8_t)(((vq[0] & 15) << 4) | (vq[1] & 15));
+            }
+            // the new token takes the freed ring slot (each lane wrote back
+            // only channels it read itself)
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) {
+                const int d = lane * DPL + i;
+                rk[d] = knv[i];
+                rv[d] = vnv[i];
+            }
+        }
+        if (p.age && lane == 0) p.ws_age[z] = (int)(room ? n + 1 : n);
+        __syncwarp();
+        const int64_t T_all = T_seg + (room ? 2 : 0);
+        auto row_ptr = [&](int64_t ft, bool vrow) -> const T* {
+            if (ft >= T_all) ft = 0;   // padding rows: any finite row (masked)
+            if (ft >= T_seg) return ab + (ft - T_seg) * 2 * D + (vrow ? D : 0);
+            int s = 0;
+            while (s < p.n_fp - 1 && ft >= sl[s]) { ft -= sl[s]; ++s; }
+            return reinterpret_cast<const T*>(vrow ? p.fp[s].v : p.fp[s].k) + (sr[s] + ft) * D;
+        };
+        // ---- query fragments (exact model-dtype q), ChanMap<4> order ----
+        uint32_t qf[NT][KSTEPS][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int r = nt * 8 + gid;
+            const bool rv = r < p.rows;
+            const int j = rv ? r / p.n_q : 0, sq = rv ? r % p.n_q : 0;
+            const uint16_t* qp = reinterpret_cast<const uint16_t*>(p.qo) + (int64_t)b * p.qo_sb +
+                                 (int64_t)(h * p.g + j) * p.qo_sh + (int64_t)sq * p.qo_ss;
+#pragma unroll
+            for (int cb = 0; cb < NCB; ++cb) {
+                uint16_t e[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) e[i] = rv ? qp[32 * cb + 8 * t + i] : (uint16_t)0;
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+#pragma unroll
+                    for (int hs = 0; hs < 2; ++hs) {
+                        const int ks = cb * 2 + u;
+                        const int i0 = KMap::kdim(ks, 2 * hs, t) - 32 * cb - 8 * t;
+                        const int i1 = KMap::kdim(ks, 2 * hs + 1, t) - 32 * cb - 8 * t;
+                        qf[nt][ks][hs] = (uint32_t)e[i0] | ((uint32_t)e[i1] << 16);
+                    }
+            }
+        }
+        float m_run[NT][2], l_run[NT][2], o[NT][MT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            m_run[nt][0] = m_run[nt][1] = kMaskedMax;
+            l_run[nt][0] = l_run[nt][1] = 0.f;
+#pragma unroll
+            for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[nt][mi][e] = 0.f;
+        }
+        for (int64_t t0 = 0; t0 < T_all; t0 += 16) {
+            // ---- S^T = K . q^T (16 tokens) ----
+            float sacc[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) sacc[nt][e] = 0.f;
+            {
+                const T* k0 = row_ptr(t0 + gid, false);
+                const T* k1 = row_ptr(t0 + gid + 8, false);
+                uint4 kr0[NCB], kr1[NCB];
+#pragma unroll
+                for (int cb = 0; cb < NCB; ++cb) {
+                    kr0[cb] = *reinterpret_cast<const uint4*>(k0 + 32 * cb + 8 * t);
+                    kr1[cb] = *reinterpret_cast<const uint4*>(k1 + 32 * cb + 8 * t);
+                }
+#pragma unroll
+                for (int cb = 0; cb < NCB; ++cb) {
+                    // channels 8t+0..7 of the chunk as words w0=(0,1) w1=(2,3) w2=(4,5) w3=(6,7)
+                    const uint32_t a_w[2][4] = {{kr0[cb].x, kr0[cb].y, kr0[cb].z, kr0[cb].w},
+                                                {kr1[cb].x, kr1[cb].y, kr1[cb].z, kr1[cb].w}};
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        // u=0: slots (1,5),(0,4); u=1: (3,7),(2,6)  (see ChanMap<4>::kdim)
+                        const uint32_t hi_sel = 0x7632u, lo_sel = 0x5410u;
+                        uint32_t a[4];
+#pragma unroll
+                        for (int rr = 0; rr < 2; ++rr) {
+                            const uint32_t wl = a_w[rr][u], wh = a_w[rr][2 + u];
+                            a[rr] = __byte_perm(wl, wh, hi_sel);       // (ch 2u+1, ch 2u+5)
+                            a[2 + rr] = __byte_perm(wl, wh, lo_sel);   // (ch 2u,   ch 2u+4)
+                        }
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt)
+                            P::mma(sacc[nt], a[0], a[1], a[2], a[3], qf[nt][cb * 2 + u][0], qf[nt][cb * 2 + u][1]);
+                    }
+                }
+            }
+            // ---- online softmax (log2 domain); masked: padding, aged slot ----
+            bool grow = false;
+            float corr[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int64_t ft = t0 + gid + ((e >> 1) << 3);
+                    sacc[nt][e] = (ft >= T_all || ft == ft_aged) ? -INFINITY : sacc[nt][e] * p.qk_scale;
+                }
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    float mx = fmaxf(sacc[nt][e], sacc[nt][e + 2]);
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    const float mnew = fmaxf(m_run[nt][e], mx);
+                    grow |= mnew > m_run[nt][e];
+                    corr[nt][e] = ex2(m_run[nt][e] - mnew);
+                    m_run[nt][e] = mnew;
+                }
+            }
+            if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        l_run[nt][e] *= corr[nt][e];
+#pragma unroll
+                        for (int mi = 0; mi < MT; ++mi) {
+                            o[nt][mi][e] *= corr[nt][e];
+                            o[nt][mi][e + 2] *= corr[nt][e];
+                        }
+                    }
+            }
+            // P as hi + lo model-dtype parts (two MMAs): the FP tiers carry
+            // the sharpest scores, so P keeps ~16 significant bits here
+            uint32_t pb[NT][2], pl[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                float pv[4], lo[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    pv[e] = ex2(sacc[nt][e] - m_run[nt][e & 1]);
+                    l_run[nt][e & 1] += pv[e];
+                }
+                const uint32_t h01 = P::pack(pv[0], pv[1]), h23 = P::pack(pv[2], pv[3]);
+                lo[0] = pv[0] - P::unpack_lo(h01);
+                lo[1] = pv[1] - P::unpack_lo(h01 >> 16);
+                lo[2] = pv[2] - P::unpack_lo(h23);
+                lo[3] = pv[3] - P::unpack_lo(h23 >> 16);
+                pb[nt][0] = movmatrix_t(h01);
+                pb[nt][1] = movmatrix_t(h23);
+                pl[nt][0] = movmatrix_t(P::pack(lo[0], lo[1]));
+                pl[nt][1] = movmatrix_t(P::pack(lo[2], lo[3]));
+            }
+            // ---- O^T += V^T . P^T: tokens 2t, 2t+1, 2t+8, 2t+9 x channels
+            //      32cb + 4gid .. +3 (8-byte loads) ----
+            {
+                const T* v0 = row_ptr(t0 + 2 * t, true);
+                const T* v1 = row_ptr(t0 + 2 * t + 1, true);
+                const T* v2 = row_ptr(t0 + 2 * t + 8, true);
+                const T* v3 = row_ptr(t0 + 2 * t + 9, true);
+#pragma unroll
+                for (int cb = 0; cb < NCB; ++cb) {
+                    const uint2 r0 = *reinterpret_cast<const uint2*>(v0 + 32 * cb + 4 * gid);
+                    const uint2 r1 = *reinterpret_cast<const uint2*>(v1 + 32 * cb + 4 * gid);
+                    const uint2 r2 = *reinterpret_cast<const uint2*>(v2 + 32 * cb + 4 * gid);
+                    const uint2 r3 = *reinterpret_cast<const uint2*>(v3 + 32 * cb + 4 * gid);
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        // channel pair (c, c+1) = 32cb + 4gid + 2j: words .x (j=0) / .y (j=1)
+                        const uint32_t w0 = j ? r0.y : r0.x, w1 = j ? r1.y : r1.x;
+                        const uint32_t w2 = j ? r2.y : r2.x, w3 = j ? r3.y : r3.x;
+                        const uint32_t a0 = __byte_perm(w0, w1, 0x5410u);   // (tok 2t, 2t+1) @ c
+                        const uint32_t a1 = __byte_perm(w0, w1, 0x7632u);   // @ c+1
+                        const uint32_t a2 = __byte_perm(w2, w3, 0x5410u);   // (tok 2t+8, 2t+9) @ c
+                        const uint32_t a3 = __byte_perm(w2, w3, 0x7632u);
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) {
+                            P::mma(o[nt][cb * 2 + j], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+                            P::mma(o[nt][cb * 2 + j], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+                        }
+                    }
+                }
+            }
+        }
+        // ---- partial of row z ----
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float l = l_run[nt][e];
+                l += __shfl_xor_sync(0xffffffffu, l, 4);
+                l += __shfl_xor_sync(0xffffffffu, l, 8);
+                l += __shfl_xor_sync(0xffffffffu, l, 16);
+                const int r = nt * 8 + 2 * t + e;
+                if (r < p.rows) {
+                    if (gid == 0)
+                        *reinterpret_cast<float2*>(p.ws_fpml + ((int64_t)z * p.rows + r) * 2) =
+                            make_float2(m_run[nt][e], l);
+#pragma unroll
+                    for (int mi = 0; mi < MT; ++mi)
+                        *reinterpret_cast<float2*>(p.ws_fpo + ((int64_t)z * p.rows + r) * D + VMap::vdim(mi, 0, gid)) =
+                            make_float2(o[nt][mi][e], o[nt][mi][e + 2]);
+                }
+            }
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
 // k1: middle tier, persistent stream-K
 // QSPLIT: the query is fp32 (rotated tiers) and is fed to the MMA as a
 // hi + lo pair of model-dtype values (two MMAs per k-step).
 // ---------------------------------------------------------------------------
 template <int DT, int D, int KB, int VB, bool VGROUP, int NT, bool QSPLIT>
-__global__ void __launch_bounds__(kMidThreads, (NT == 1 ? 3 : 1))
+__global__ void __launch_bounds__(mid_threads(NT), 1)
 middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-              const __grid_constant__ CUtensorMap tmap_s, MidParams p) {
+              const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ MidParams p) {
     using L = MidLayout<D, KB, VB, VGROUP, NT>;
     using KMap = ChanMap<KB>;
     using VMap = ChanMap<VB>;
@@ -464,26 +808,29 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float* obuf = reinterpret_cast<float*>(smem + L::RING_BYTES);
-    float* mlbuf = reinterpret_cast<float*>(smem + L::RING_BYTES + L::OBUF_BYTES);
+    constexpr int G = L::G, NS = L::NS;
+    constexpr int PRODUCER = G * kConsumerWarps;   // warp index of the producer
     const uint32_t bar_base = smem_u32(smem + L::BAR_OFF);
     auto full_bar = [&](int s) { return bar_base + 8u * s; };
-    auto empty_bar = [&](int s) { return bar_base + 8u * (kStages + s); };
+    auto empty_bar = [&](int s) { return bar_base + 8u * (NS + s); };
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int Z = p.B * p.Hkv;
     const int U = total_units(p, Z);
     // Never more CTAs than units, so every working CTA owns at least one unit
     // (the merge counts arrivals per row by CTA range).
+    // Streaming CTAs: never more than units, so each owns at least one unit.
+    // Every launched CTA runs the FP warp (rows split over the whole grid).
     const int C = p.n_ctas < U ? p.n_ctas : U;
     const int c = blockIdx.x;
-    if (c >= C) return;
-    const int ub = (int)((int64_t)c * U / C), ue = (int)((int64_t)(c + 1) * U / C);
+    const bool streams = c < C;
+    const int ub = streams ? (int)((int64_t)c * U / C) : 0;
+    const int ue = streams ? (int)((int64_t)(c + 1) * U / C) : 0;
 
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::FLAG_OFF);
     if (threadIdx.x == 0) {
         *abort_flag = 0;
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(full_bar(s), 32);
             mbar_init(empty_bar(s), kConsumerWarps);
         }
@@ -493,10 +840,10 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     __syncthreads();
     FADE_TR(0);
 #ifdef FADE_TRACE
-    if (threadIdx.x == 0 && blockIdx.x < 1024) {
+    if (threadIdx.x == 0 && blockIdx.x < 192) {
         unsigned smid;
         asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-        g_trace[blockIdx.x * kTraceEv + 95] = smid + 1;
+        g_trace[(blockIdx.x * 4) * kTraceEv + 95] = smid + 1;
     }
 #endif
     // Inputs may be produced by the previous kernel in the stream (age-out,
@@ -504,12 +851,16 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // next kernel in the stream start its prologue.  With `early` the tiers
     // are known not to be written by that kernel: the producer starts
     // streaming at once and only the consumers (queries, partial slots) wait.
-    if (!(p.early && warp == kConsumerWarps)) griddep_wait();
-    if (warp < kConsumerWarps) griddep_launch_dependents();
+    if (!(p.early && warp == PRODUCER)) griddep_wait();
+    if (warp < PRODUCER) griddep_launch_dependents();
     FADE_TR(1);
+    if (warp == PRODUCER + 1) {
+        fp_rows_warp<DT, D, NT>(p, c, (int)gridDim.x, smem + L::AB_OFF);
+        return;
+    }
     if (ub >= ue) return;
 
-    if (warp == kConsumerWarps) {
+    if (warp == PRODUCER) {
         // ------------------------------ producer ------------------------------
         const uint64_t policy = evict_first_policy();
         if (lane == 0) {
@@ -521,8 +872,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         int zb = units_begin(p, z), ze = units_begin(p, z + 1);
         for (int u = ub, i = 0; u < ue; ++u, ++i) {
             while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
-            const int s = i % kStages;
-            const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+            const int s = i % NS;
+            const uint32_t ph = (uint32_t)(i / NS) & 1u;
             if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.ws_err)) continue;
             const int64_t tok0 = (int64_t)(u - zb) * kStageTokens;
             const int64_t row0 = seg_row0(p, z) + tok0;
@@ -531,7 +882,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             // Units past this row's length (uniform grid over a capacity bound)
             // carry no tokens: complete the stage without a copy.
             uint8_t* scs = smem + L::SC_BASE + s * L::SC_BYTES;
-            FADE_TRP(40 + i);
+            if (i < 40) FADE_TRP(40 + i);
             if (lane == 0 && tok0 < len) {
                 const uint32_t sc_bytes = (p.scale_tma && FADE_ABLATE != 5) ? (uint32_t)L::sc_box_bytes(p.group) : 0u;
                 mbar_expect_tx(full_bar(s), (uint32_t)(L::K_BYTES + L::V_BYTES) + sc_bytes);
@@ -578,22 +929,27 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         // Drain: wait until the consumers released every stage still in flight,
         // so no TMA write targets this CTA's shared memory after it exits.
         const int n = ue - ub;
-        for (int i = (n > kStages ? n : kStages); i < n + kStages; ++i) {
-            const int s = i % kStages;
-            const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+        for (int i = (n > NS ? n : NS); i < n + NS; ++i) {
+            const int s = i % NS;
+            const uint32_t ph = (uint32_t)(i / NS) & 1u;
             mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.ws_err);
         }
         return;
     }
 
     // ------------------------------ consumers ------------------------------
+    const int grp = warp / kConsumerWarps;   // consumer group
+    const int gw = warp % kConsumerWarps;    // warp within the group
     const int gid = lane >> 2, t = lane & 3;
-    const int ctid = threadIdx.x;  // 0..127
+    const int ctid = gw * 32 + lane;         // 0..127 within the group
+    const int bar_id = 1 + grp;              // the group's named barrier
+    float* obuf = reinterpret_cast<float*>(smem + L::RING_BYTES + grp * (L::OBUF_BYTES + L::ML_BYTES));
+    float* mlbuf = obuf + L::OBUF_BYTES / 4;
     uint32_t qf[NQ][NT][KSTEPS][2];  // B fragments (exact model-dtype query)
     uint32_t ksc[KSTEPS][2];         // K scale pairs matching the A pairs
     float m_run[NT][2], l_run[NT][2];
     float o[NT][MT][4];
-    int cur_z = -1;
+    int cur_z = -1, z_first = 0;
     int64_t cur_len = 0;
 
     // Each thread's K channels form, per 16-byte chunk cb of a packed row, one
@@ -703,7 +1059,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // reads the partials after this grid has completed, so no fence, counter
     // or merge sits on the streaming path.  The warps are summed in a fixed
     // order ((w0 + w2) + (w1 + w3)): repeated calls give identical bits.
-    constexpr int MLW = NT * 8;   // rows per warp in the statistics buffer
+    constexpr int MLW = NT * 8;   // rows per gw in the statistics buffer
     int n_flush = 0;
     auto flush = [&](int z) {
         // 1) complete the per-thread row sums over the 8 token lanes
@@ -717,7 +1073,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 l += __shfl_xor_sync(0xffffffffu, l, 16);
                 l_run[nt][e] = l;
             }
-        // statistics alternate between two buffers: a warp can reach the next
+        // statistics alternate between two buffers: a gw can reach the next
         // flush while threads 0..rows-1 still read this one's
         float* mlw = mlbuf + (n_flush & 1) * (kConsumerWarps * MLW * 2);
         ++n_flush;
@@ -727,12 +1083,12 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int r = nt * 8 + 2 * t + e;
-                    mlw[(warp * MLW + r) * 2 + 0] = m_run[nt][e];
-                    mlw[(warp * MLW + r) * 2 + 1] = l_run[nt][e];
+                    mlw[(gw * MLW + r) * 2 + 0] = m_run[nt][e];
+                    mlw[(gw * MLW + r) * 2 + 1] = l_run[nt][e];
                 }
         }
-        named_bar_sync(1, kConsumerWarps * 32);
-        // 2) rescale this warp's O to the CTA max
+        named_bar_sync(bar_id, kConsumerWarps * 32);
+        // 2) rescale this gw's O to the CTA max
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -750,9 +1106,9 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             }
         // 3) half-sums: warps 0/1 store into obuf halves 0/1, warps 2/3 add
         //    theirs (channel pairs d, d+1 are adjacent: float2 accesses)
-        float* half = obuf + (warp & 1) * (NT * 8 * D);
+        float* half = obuf + (gw & 1) * (NT * 8 * D);
         for (int pass = 0; pass < 2; ++pass) {
-            if ((warp >> 1) == pass) {
+            if ((gw >> 1) == pass) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -772,11 +1128,11 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         }
                     }
             }
-            named_bar_sync(1, kConsumerWarps * 32);
+            named_bar_sync(bar_id, kConsumerWarps * 32);
         }
-        // 4) store the partial (float4 rows)
-        const int zb = units_begin(p, z);
-        const int slot = zb > ub ? zb : ub;
+        // 4) store the partial (float4 rows) at the first unit of z this
+        //    group processed (unique per group and row)
+        const int slot = z_first;
         float4* go = reinterpret_cast<float4*>(p.ws_o + (int64_t)slot * p.rows * D);
         const float4* h0 = reinterpret_cast<const float4*>(obuf);
         const float4* h1 = reinterpret_cast<const float4*>(obuf + NT * 8 * D);
@@ -799,7 +1155,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     int z = z_of_unit(p, Z, ub);
     int zb = units_begin(p, z), ze = units_begin(p, z + 1);
 
-    for (int u = ub, i = 0; u < ue; ++u, ++i) {
+    for (int i = grp; ub + i < ue; i += G) {
+        const int u = ub + i;
         while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
         if (z != cur_z) {
             if (FADE_ABLATE != 6) {
@@ -810,12 +1167,13 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 FADE_TR(4 + 3 * (cur_z >= 0 ? 1 : 0));
             }
             cur_z = z;
+            z_first = u;
         }
-        const int s = i % kStages;
-        const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+        const int s = i % NS;
+        const uint32_t ph = (uint32_t)(i / NS) & 1u;
         const bool ready = mbar_wait(full_bar(s), ph, abort_flag, p.ws_err);
-        FADE_TR(10 + i);
-        const int tw = (u - zb) * kStageTokens + warp * 32;  // first token of this warp (row-relative)
+        if (i / G < 24) FADE_TR(10 + i / G);
+        const int tw = (u - zb) * kStageTokens + gw * 32;  // first token of this gw (row-relative)
         const int clen = (int)cur_len;
         const uint8_t* st = smem + s * L::STAGE_BYTES;
         const uint32_t kbase = smem_u32(st + L::K_OFF);
@@ -823,7 +1181,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         const uint8_t* scb = smem + L::SC_BASE + s * L::SC_BYTES;
 
         if (ready && tw < clen && FADE_ABLATE != 1 && FADE_ABLATE < 4) {
-            // ---- S^T = K_deq . q^T for the warp's 2 m-tiles ----
+            // ---- S^T = K_deq . q^T for the gw's 2 m-tiles ----
             // two accumulators per m-tile (even / odd k-steps) halve the
             // dependent MMA chain; summed before the softmax
             float sacc[2][NT][4], sacc2[2][NT][4];
@@ -834,7 +1192,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 #pragma unroll
                     for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = sacc2[mt][nt][e] = 0.f;
                 uint32_t kr[2][L::NCHK];
-                load_tiles<L::NCHK, false>(kbase, warp * 32 + mt * 16, lane, kr);
+                load_tiles<L::NCHK, false>(kbase, gw * 32 + mt * 16, lane, kr);
 #pragma unroll
                 for (int cb = 0; cb < L::NCHK; ++cb) {
                     if constexpr (KB == 4) {
@@ -891,7 +1249,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) sacc[mt][nt][e] *= p.qk_scale;
-            if (tw + 32 > clen) {   // warp-uniform: only the row's last tile is partial
+            if (tw + 32 > clen) {   // gw-uniform: only the row's last tile is partial
 #pragma unroll
                 for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -918,7 +1276,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     m_run[nt][e] = mnew;
                 }
             }
-            // Rescale only when some row maximum of the warp grew (corr is
+            // Rescale only when some row maximum of the gw grew (corr is
             // exactly 1 otherwise, so skipping is bit-identical).
             if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
@@ -951,13 +1309,13 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             // ---- O^T += V_deq^T . P^T ----
 #pragma unroll
             for (int mt = 0; mt < (FADE_ABLATE == 2 ? 0 : 2); ++mt) {
-                const int trow0 = warp * 32 + mt * 16;
+                const int trow0 = gw * 32 + mt * 16;
                 uint32_t vr[2][L::NCHV];
                 load_tiles<L::NCHV, true>(vbase, trow0, lane, vr);
                 // tokens of this m-tile past the length: their scales may be
                 // stale bytes (NaN * 0 must not reach the MMA), so zero them;
                 // a tile entirely past the length is skipped.
-                const int tile_tok = tw - warp * 32 + trow0;
+                const int tile_tok = tw - gw * 32 + trow0;
                 if (tile_tok >= clen) continue;
                 uint32_t vs0 = 0, vs1 = 0;
                 const uint16_t* gsc = nullptr;
@@ -1077,14 +1435,6 @@ __global__ void rotate_queries_kernel(const void* q, int Hq, int n_q, int D, int
 //   chunks of kFinSlots partials), rotate the middle part back for rotated
 //   tiers (out = fp + mid @ R), normalise and write `out`.
 // ---------------------------------------------------------------------------
-struct FpSeg {
-    const void* k;
-    const void* v;
-    int64_t row_sb, row_sh;
-    const int64_t* row_base;
-    const int32_t* lens;
-    int64_t len;
-};
 constexpr int kFinThreads = 256;
 constexpr int kFinChunk = 128;   // FP tokens staged per pass
 constexpr int kFinSlots = 64;    // middle partials merged per pass
@@ -1103,26 +1453,16 @@ struct FinParams {
     const int32_t* cu_units;        // middle units per row (ragged) or null
     int units_per_z;
     int n_ctas;                     // middle grid (before clamping to the units)
+    int groups;                     // consumer groups per middle CTA
     const float* ws_ml;             // middle partials [U][rows][2]
     const float* ws_o;              // [U][rows][D]
     const float* rotation;          // rotated middle: [D,D] fp32, else null
-    // fused age-out (fade_decode_attn_age_out); age == 0 otherwise
+    // FP-tier partials and the fused age-out's new lengths (middle kernel)
+    const float* ws_fpml;           // [Z][rows][2]
+    const float* ws_fpo;            // [Z][rows][D]
     int age;
-    int ring_fp;                    // index into fp[] of the recent-window ring
-    int64_t ring_cap, ring_origin;
-    const void* k_new;              // [B,Hkv,D]
-    const void* v_new;
-    int64_t new_sb, new_sh;
-    uint8_t* mid_k;                 // middle code rows (D/2 bytes), row-indexed
-    uint8_t* mid_v;
-    void* mid_vs;                   // per-row V scale
-    const void* mid_ks;             // per-channel K scale
-    int64_t ks_sb, ks_sh;
-    int64_t mid_sb, mid_sh;
-    const int64_t* mid_row_base;
-    int64_t mid_cap;
-    int32_t* mid_len;               // [B], advanced by the call
-    int* age_cnt;                   // [B] workspace counters (zero between calls)
+    int32_t* mid_len;
+    const int* ws_age;              // [Z]
 };
 
 template <int D, int NT>
@@ -1136,7 +1476,8 @@ struct FinLayout {
     static constexpr int ST_OFF = P_OFF + ROWS * kFinChunk * 4;      // row stats [4][ROWS]
     static constexpr int SW_OFF = ST_OFF + 4 * ROWS * 4;             // [kFinSlots][ROWS] weights
     static constexpr int SL_OFF = SW_OFF + kFinSlots * ROWS * 4;     // [kFinSlots][ROWS] sums
-    static constexpr int BYTES = SL_OFF + kFinSlots * ROWS * 4;
+    static constexpr int SLOT_OFF = SL_OFF + kFinSlots * ROWS * 4;   // [kFinSlots] partial slots
+    static constexpr int BYTES = SLOT_OFF + kFinSlots * 4;
     static_assert(ROWS * D * 4 <= V_OFF, "rotation scratch reuses the K region");
 };
 
@@ -1149,7 +1490,7 @@ __device__ __forceinline__ void cp_async_wait_all() {
 
 template <int DT, int D, int NT>
 __global__ void __launch_bounds__(kFinThreads)
-finish_kernel(FinParams p) {
+finish_kernel(const __grid_constant__ FinParams p) {
     using L = FinLayout<D, NT>;
     using T = typename Elem<DT>::T;
     constexpr int ROWS = L::ROWS;
@@ -1168,267 +1509,209 @@ finish_kernel(FinParams p) {
     float* f_row = m_row + 3 * ROWS;   // 1 / L
     float* sw = reinterpret_cast<float*>(fsm + L::SW_OFF);
     float* sl = reinterpret_cast<float*>(fsm + L::SL_OFF);
-    __shared__ int s_age[2];   // [0] = n (middle length before the step), [1] = last CTA of b
+    int* sslot = reinterpret_cast<int*>(fsm + L::SLOT_OFF);
 
     const int z = blockIdx.x;
     const int b = z / p.Hkv, h = z % p.Hkv;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int rows = p.rows;
     FADE_TRF(0);
-    if (!p.has_mid) griddep_wait();
-    griddep_launch_dependents();
-
-    // ---- fused age-out: fetch this row's middle length and count this CTA
-    //      (acq_rel: the read of mid_len[b] happens before the write of n + 1
-    //      by the last CTA of b, which observes this increment).  The values
-    //      are consumed after the FP tokens have been requested. ----
-    int age_n_ld = 0, age_old = 0;
-    if (p.age && tid == 0) {
-        age_n_ld = p.mid_len[b];
-        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(age_old) : "l"(p.age_cnt + b) : "memory");
-    }
-    // ---- FP segments of this row: lengths and first rows ----
-    int64_t seg_len_[FADE_MAX_SEGMENTS], seg_row_[FADE_MAX_SEGMENTS];
-    int64_t n_seg_tok = 0;
-#pragma unroll
-    for (int s = 0; s < FADE_MAX_SEGMENTS; ++s) {
-        seg_len_[s] = 0;
-        seg_row_[s] = 0;
-        if (s < p.n_fp) {
-            const FpSeg& sg = p.fp[s];
-            seg_len_[s] = sg.lens ? (int64_t)sg.lens[b] : sg.len;
-            seg_row_[s] = sg.row_base ? sg.row_base[z] : (int64_t)b * sg.row_sb + (int64_t)h * sg.row_sh;
-            n_seg_tok += seg_len_[s];
-        }
-    }
-    // Token order: the FP segments' tokens, then (age-out) the step's new
-    // token, staged before it is known whether the middle has room (without
-    // room it is left out of the softmax).  The ring token at the aged slot
-    // stays in the list: after staging it is replaced in shared memory by its
-    // INT4 round trip (it moves to the middle in this step), and the new token
-    // takes its ring slot.
-    const int64_t n_tok = n_seg_tok + (p.age ? 1 : 0);
-
-    auto stage = [&](int64_t t0, int n) {
-        constexpr int PCS = D / 8;   // 16-byte pieces per row
-        for (int i = tid; i < n * PCS; i += kFinThreads) {
-            const int tk = i / PCS, c = i % PCS;
-            int64_t ft = t0 + tk;
-            const T* ks;
-            const T* vs;
-            if (ft >= n_seg_tok) {   // the step's new token
-                const int64_t off = (int64_t)b * p.new_sb + (int64_t)h * p.new_sh + c * 8;
-                ks = reinterpret_cast<const T*>(p.k_new) + off;
-                vs = reinterpret_cast<const T*>(p.v_new) + off;
-            } else {
-                int s = 0;
-                while (s < p.n_fp - 1 && ft >= seg_len_[s]) { ft -= seg_len_[s]; ++s; }
-                const FpSeg& sg = p.fp[s];
-                const int64_t off = (seg_row_[s] + ft) * D + c * 8;
-                ks = reinterpret_cast<const T*>(sg.k) + off;
-                vs = reinterpret_cast<const T*>(sg.v) + off;
-            }
-            T* kd = ksm + tk * L::KSTR + c * 8;
-            T* vd = vsm + tk * D + c * 8;
-            if (p.vec) {
-                cp_async16(smem_u32(kd), ks);
-                cp_async16(smem_u32(vd), vs);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    kd[e] = ks[e];
-                    vd[e] = vs[e];
-                }
-            }
-        }
-    };
-    if (n_tok > 0) stage(0, (int)(n_tok < kFinChunk ? n_tok : kFinChunk));
-
-    // ---- queries, pre-scaled into the log2 domain ----
-    for (int i = tid; i < ROWS * D; i += kFinThreads) {
-        const int r = i / D, d = i % D;
-        float v = 0.f;
-        if (r < rows) {
-            const int j = r / p.n_q, sq = r % p.n_q;
-            v = load_f<DT>(p.q, (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss + d) *
-                p.qk_scale;
-        }
-        qsm[i] = v;
-    }
-    if (tid < ROWS) { m_row[tid] = -INFINITY; l_row[tid] = 0.f; }
-    if (p.age && tid == 0) {
-        s_age[0] = age_n_ld;
-        s_age[1] = (age_old == p.Hkv - 1) ? 1 : 0;
-    }
-    __syncthreads();
-    int64_t age_n = 0, age_slot = -1, ft_aged = -1, ft_new = -1;
-    bool room = false;
-    if (p.age) {
-        age_n = s_age[0];
-        room = age_n < p.mid_cap;
-        ft_new = n_seg_tok;
-        if (room) {
-            age_slot = (age_n - p.ring_origin) % p.ring_cap;
-            if (age_slot < 0) age_slot += p.ring_cap;
-            ft_aged = age_slot;
-            for (int s = 0; s < p.ring_fp; ++s) ft_aged += seg_len_[s];
-        }
-    }
-
     float acc_f[OUTS][2];
 #pragma unroll
     for (int k = 0; k < OUTS; ++k) acc_f[k][0] = acc_f[k][1] = 0.f;
 
-    for (int64_t t0 = 0; t0 < n_tok; t0 += kFinChunk) {
-        const int n = (int)((n_tok - t0) < kFinChunk ? (n_tok - t0) : kFinChunk);
-        if (t0 > 0) {
-            __syncthreads();   // previous pass finished reading ksm / vsm / psm
-            stage(t0, n);
-        }
-        cp_async_wait_all();
-        __syncthreads();
-        if (ft_aged >= t0 && ft_aged < t0 + n) {
-            // ---- age-out of the oldest ring token (warp 0) ----
-            // INT4 codes exactly as fade_age_out_int4; its shared-memory row
-            // becomes the dequantised value rnd(code * scale) that the middle
-            // tier will hold, and the new token is written into its ring slot.
-            if (warp == 0) {
-                T* kr = ksm + (ft_aged - t0) * L::KSTR;
-                T* vr = vsm + (ft_aged - t0) * D;
-                const int64_t mrow = (p.mid_row_base ? p.mid_row_base[z]
-                                                     : (int64_t)b * p.mid_sb + (int64_t)h * p.mid_sh) + age_n;
-                const T* ksc = reinterpret_cast<const T*>(p.mid_ks) + (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
-                float m = 0.f;
-                for (int d = lane; d < D; d += 32) m = fmaxf(m, fabsf(Elem<DT>::to_f(vr[d])));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                m = fmaxf(m, Elem<DT>::eps());
-                const float inv = inv_scale<DT>(m, 7.f);
-                const float vsc = Elem<DT>::rnd(__fdiv_rn(m, 7.f));
-                if (lane == 0) reinterpret_cast<T*>(p.mid_vs)[mrow] = Elem<DT>::from_f(vsc);
-                for (int pp = lane; pp < D / 2; pp += 32) {
-                    int kq[2], vq[2];
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const int d = 2 * pp + j;
-                        const float sc = Elem<DT>::to_f(ksc[d]);
-                        const float kx = Elem<DT>::to_f(kr[d]);
-                        kq[j] = (sc > 0.f) ? quant_code(__fdiv_rn(kx, sc), -8.f, 7.f) : 0;
-                        vq[j] = quant_code(Elem<DT>::rnd(__fmul_rn(Elem<DT>::to_f(vr[d]), inv)), -8.f, 7.f);
-                        kr[d] = Elem<DT>::from_f((float)kq[j] * sc);
-                        vr[d] = Elem<DT>::from_f((float)vq[j] * vsc);
-                    }
-                    p.mid_k[mrow * (D / 2) + pp] = (uint8_t)(((kq[0] & 15) << 4) | (kq[1] & 15));
-                    p.mid_v[mrow * (D / 2) + pp] = (uint8_t)(((vq[0] & 15) << 4) | (vq[1] & 15));
-                }
-                // the new token takes the freed ring slot (read above, in this chunk)
-                const FpSeg& rg = p.fp[p.ring_fp];
-                T* rk = const_cast<T*>(reinterpret_cast<const T*>(rg.k)) + (seg_row_[p.ring_fp] + age_slot) * D;
-                T* rv = const_cast<T*>(reinterpret_cast<const T*>(rg.v)) + (seg_row_[p.ring_fp] + age_slot) * D;
-                const T* kn = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
-                const T* vn = reinterpret_cast<const T*>(p.v_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
-                for (int d = lane; d < D; d += 32) { rk[d] = kn[d]; rv[d] = vn[d]; }
-            }
-            __syncthreads();
-        }
-        // ---- scores S[r][tok] = q_r . k_tok (log2 domain) ----
-        for (int i = tid; i < rows * n; i += kFinThreads) {
-            const int r = i / n, tk = i % n;
-            const uint4* kr = reinterpret_cast<const uint4*>(ksm + tk * L::KSTR);
-            const float4* qr = reinterpret_cast<const float4*>(qsm + r * D);
-            float a0 = 0.f, a1 = 0.f;
-#pragma unroll 4
-            for (int c = 0; c < D / 8; ++c) {
-                const uint4 raw = kr[c];
-                const T* e8 = reinterpret_cast<const T*>(&raw);
-                const float4 q0 = qr[2 * c], q1 = qr[2 * c + 1];
-                a0 = fmaf(q0.x, Elem<DT>::to_f(e8[0]), a0);
-                a1 = fmaf(q0.y, Elem<DT>::to_f(e8[1]), a1);
-                a0 = fmaf(q0.z, Elem<DT>::to_f(e8[2]), a0);
-                a1 = fmaf(q0.w, Elem<DT>::to_f(e8[3]), a1);
-                a0 = fmaf(q1.x, Elem<DT>::to_f(e8[4]), a0);
-                a1 = fmaf(q1.y, Elem<DT>::to_f(e8[5]), a1);
-                a0 = fmaf(q1.z, Elem<DT>::to_f(e8[6]), a0);
-                a1 = fmaf(q1.w, Elem<DT>::to_f(e8[7]), a1);
-            }
-            // the new token is attended only when the middle had room
-            psm[r * kFinChunk + tk] = (t0 + tk == ft_new && !room) ? -INFINITY : a0 + a1;
-        }
-        __syncthreads();
-        // ---- online softmax per row (one warp per row) ----
-        for (int r = warp; r < rows; r += NW) {
-            float mx = -INFINITY;
-            for (int tk = lane; tk < n; tk += 32) mx = fmaxf(mx, psm[r * kFinChunk + tk]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            const float mold = m_row[r];
-            const float mnew = fmaxf(mold, mx);
-            float sum = 0.f;
-            for (int tk = lane; tk < n; tk += 32) {
-                const float sv = psm[r * kFinChunk + tk];
-                const float e = (sv == -INFINITY) ? 0.f : ex2(sv - mnew);
-                psm[r * kFinChunk + tk] = e;
-                sum += e;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) {
-                const float corr = (mold == -INFINITY) ? 0.f : ex2(mold - mnew);
-                m_row[r] = mnew;
-                l_row[r] = l_row[r] * corr + sum;
-                c_row[r] = corr;
-            }
-        }
-        __syncthreads();
-        // ---- O[r][d] = O * corr + sum_tok P[r][tok] V[tok][d] ----
+    float2 fp_ml = make_float2(-INFINITY, 0.f);   // FP-tier partial statistics of row tid
+    if (p.has_mid) {
+        // The middle kernel's FP warps computed the FP-tier partial of every
+        // row (and the fused age-out): wait for that grid; the merge below
+        // starts from that partial (its loads overlap the slot lookup).
+        griddep_wait();
+        griddep_launch_dependents();
+        FADE_TRF(2);
+        if (tid < rows) fp_ml = *reinterpret_cast<const float2*>(p.ws_fpml + ((int64_t)z * rows + tid) * 2);
 #pragma unroll
         for (int k = 0; k < OUTS; ++k) {
             const int i = tid + k * kFinThreads;
-            if (i >= rows * D2) continue;
-            const int r = i / D2, d2 = i % D2;
-            const float corr = c_row[r];
-            float a0 = acc_f[k][0] * corr, a1 = acc_f[k][1] * corr;
-            const float* pr = psm + r * kFinChunk;
-            const uint32_t* vcol = reinterpret_cast<const uint32_t*>(vsm) + d2;
-#pragma unroll 4
-            for (int tk = 0; tk < n; ++tk) {
-                const uint32_t vv = vcol[tk * D2];
-                const float pt = pr[tk];
-                a0 = fmaf(pt, Elem<DT>::to_f(reinterpret_cast<const T*>(&vv)[0]), a0);
-                a1 = fmaf(pt, Elem<DT>::to_f(reinterpret_cast<const T*>(&vv)[1]), a1);
+            if (i < rows * D2) {
+                const int r = i / D2, d2 = i % D2;
+                const float2 v = *reinterpret_cast<const float2*>(p.ws_fpo + ((int64_t)z * rows + r) * D + 2 * d2);
+                acc_f[k][0] = v.x;
+                acc_f[k][1] = v.y;
             }
-            acc_f[k][0] = a0;
-            acc_f[k][1] = a1;
+        }
+        // the middle grid (every reader of the lengths) has completed: advance
+        if (p.age && h == 0 && tid == 0) p.mid_len[b] = p.ws_age[z];
+    } else {
+        griddep_wait();
+        griddep_launch_dependents();
+        // ---- no quantised tier: attention over the FP segments here ----
+        int64_t seg_len_[FADE_MAX_SEGMENTS], seg_row_[FADE_MAX_SEGMENTS];
+        int64_t n_tok = 0;
+#pragma unroll
+        for (int s = 0; s < FADE_MAX_SEGMENTS; ++s) {
+            seg_len_[s] = 0;
+            seg_row_[s] = 0;
+            if (s < p.n_fp) {
+                const FpSeg& sg = p.fp[s];
+                seg_len_[s] = sg.lens ? (int64_t)sg.lens[b] : sg.len;
+                seg_row_[s] = sg.row_base ? sg.row_base[z] : (int64_t)b * sg.row_sb + (int64_t)h * sg.row_sh;
+                n_tok += seg_len_[s];
+            }
+        }
+        auto stage = [&](int64_t t0, int n) {
+            constexpr int PCS = D / 8;   // 16-byte pieces per row
+            for (int i = tid; i < n * PCS; i += kFinThreads) {
+                const int tk = i / PCS, c = i % PCS;
+                int64_t ft = t0 + tk;
+                int s = 0;
+                while (s < p.n_fp - 1 && ft >= seg_len_[s]) { ft -= seg_len_[s]; ++s; }
+                const FpSeg& sg = p.fp[s];
+                const int64_t off = (seg_row_[s] + ft) * D + c * 8;
+                const T* ks = reinterpret_cast<const T*>(sg.k) + off;
+                const T* vs = reinterpret_cast<const T*>(sg.v) + off;
+                T* kd = ksm + tk * L::KSTR + c * 8;
+                T* vd = vsm + tk * D + c * 8;
+                if (p.vec) {
+                    cp_async16(smem_u32(kd), ks);
+                    cp_async16(smem_u32(vd), vs);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        kd[e] = ks[e];
+                        vd[e] = vs[e];
+                    }
+                }
+            }
+        };
+        if (n_tok > 0) stage(0, (int)(n_tok < kFinChunk ? n_tok : kFinChunk));
+        for (int i = tid; i < ROWS * D; i += kFinThreads) {
+            const int r = i / D, d = i % D;
+            float v = 0.f;
+            if (r < rows) {
+                const int j = r / p.n_q, sq = r % p.n_q;
+                v = load_f<DT>(p.q, (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss + d) *
+                    p.qk_scale;
+            }
+            qsm[i] = v;
+        }
+        if (tid < ROWS) { m_row[tid] = -INFINITY; l_row[tid] = 0.f; }
+        for (int64_t t0 = 0; t0 < n_tok; t0 += kFinChunk) {
+            const int n = (int)((n_tok - t0) < kFinChunk ? (n_tok - t0) : kFinChunk);
+            if (t0 > 0) {
+                __syncthreads();   // previous pass finished reading ksm / vsm / psm
+                stage(t0, n);
+            }
+            cp_async_wait_all();
+            __syncthreads();
+            // ---- scores S[r][tok] = q_r . k_tok (log2 domain) ----
+            for (int i = tid; i < rows * n; i += kFinThreads) {
+                const int r = i / n, tk = i % n;
+                const uint4* kr = reinterpret_cast<const uint4*>(ksm + tk * L::KSTR);
+                const float4* qr = reinterpret_cast<const float4*>(qsm + r * D);
+                float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
+                for (int c = 0; c < D / 8; ++c) {
+                    const uint4 raw = kr[c];
+                    const T* e8 = reinterpret_cast<const T*>(&raw);
+                    const float4 q0 = qr[2 * c], q1 = qr[2 * c + 1];
+                    a0 = fmaf(q0.x, Elem<DT>::to_f(e8[0]), a0);
+                    a1 = fmaf(q0.y, Elem<DT>::to_f(e8[1]), a1);
+                    a0 = fmaf(q0.z, Elem<DT>::to_f(e8[2]), a0);
+                    a1 = fmaf(q0.w, Elem<DT>::to_f(e8[3]), a1);
+                    a0 = fmaf(q1.x, Elem<DT>::to_f(e8[4]), a0);
+                    a1 = fmaf(q1.y, Elem<DT>::to_f(e8[5]), a1);
+                    a0 = fmaf(q1.z, Elem<DT>::to_f(e8[6]), a0);
+                    a1 = fmaf(q1.w, Elem<DT>::to_f(e8[7]), a1);
+                }
+                psm[r * kFinChunk + tk] = a0 + a1;
+            }
+            __syncthreads();
+            // ---- online softmax per row (one warp per row) ----
+            for (int r = warp; r < rows; r += NW) {
+                float mx = -INFINITY;
+                for (int tk = lane; tk < n; tk += 32) mx = fmaxf(mx, psm[r * kFinChunk + tk]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const float mold = m_row[r];
+                const float mnew = fmaxf(mold, mx);
+                float sum = 0.f;
+                for (int tk = lane; tk < n; tk += 32) {
+                    const float e = ex2(psm[r * kFinChunk + tk] - mnew);
+                    psm[r * kFinChunk + tk] = e;
+                    sum += e;
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                if (lane == 0) {
+                    const float corr = (mold == -INFINITY) ? 0.f : ex2(mold - mnew);
+                    m_row[r] = mnew;
+                    l_row[r] = l_row[r] * corr + sum;
+                    c_row[r] = corr;
+                }
+            }
+            __syncthreads();
+            // ---- O[r][d] = O * corr + sum_tok P[r][tok] V[tok][d] ----
+#pragma unroll
+            for (int k = 0; k < OUTS; ++k) {
+                const int i = tid + k * kFinThreads;
+                if (i >= rows * D2) continue;
+                const int r = i / D2, d2 = i % D2;
+                const float corr = c_row[r];
+                float a0 = acc_f[k][0] * corr, a1 = acc_f[k][1] * corr;
+                const float* pr = psm + r * kFinChunk;
+                const uint32_t* vcol = reinterpret_cast<const uint32_t*>(vsm) + d2;
+#pragma unroll 4
+                for (int tk = 0; tk < n; ++tk) {
+                    const uint32_t vv = vcol[tk * D2];
+                    const float pt = pr[tk];
+                    a0 = fmaf(pt, Elem<DT>::to_f(reinterpret_cast<const T*>(&vv)[0]), a0);
+                    a1 = fmaf(pt, Elem<DT>::to_f(reinterpret_cast<const T*>(&vv)[1]), a1);
+                }
+                acc_f[k][0] = a0;
+                acc_f[k][1] = a1;
+            }
         }
     }
+    FADE_TRF(1);
 
-    // ---- middle partials: wait for the middle grid, then merge ----
+    // ---- merge the middle partials ----
     float acc_m[OUTS][2];
 #pragma unroll
     for (int k = 0; k < OUTS; ++k) acc_m[k][0] = acc_m[k][1] = 0.f;
-    int zb = 0, c0 = 0, nsl = 0, U = 0, C = 1;
-    FADE_TRF(1);
+    int zb = 0, ze = 0, c0 = 0, nsl = 0, U = 0, C = 1;
+    const int G = p.groups;
     if (p.has_mid) {
-        griddep_wait();
-        FADE_TRF(2);
         const int Z = p.B * p.Hkv;
         U = p.cu_units ? p.cu_units[Z] : Z * p.units_per_z;
         C = p.n_ctas < U ? p.n_ctas : U;
         zb = p.cu_units ? p.cu_units[z] : z * p.units_per_z;
-        const int ze = p.cu_units ? p.cu_units[z + 1] : (z + 1) * p.units_per_z;
+        ze = p.cu_units ? p.cu_units[z + 1] : (z + 1) * p.units_per_z;
         if (ze > zb && C > 0) {
             c0 = cta_of_unit(zb, C, U);
-            nsl = cta_of_unit(ze - 1, C, U) - c0 + 1;
+            nsl = (cta_of_unit(ze - 1, C, U) - c0 + 1) * G;
         }
     }
+    // Candidate partial j: middle CTA c0 + j / G, consumer group j % G, which
+    // stored its partial of this row at the first unit of the row it
+    // processed (units ub + g, ub + g + G, ... of the CTA's range), if any.
     auto slot_of = [&](int j) {
-        const int uc = (int)((int64_t)(c0 + j) * U / C);
-        return uc > zb ? uc : zb;
+        const int c = c0 + j / G, g = j % G;
+        const int ub = (int)((int64_t)c * U / C), ue = (int)((int64_t)(c + 1) * U / C);
+        const int u0 = zb > ub ? zb : ub;
+        const int u = u0 + ((g - (u0 - ub)) % G + G) % G;
+        return (u < ze && u < ue) ? u : -1;
     };
-    __syncthreads();   // FP statistics complete
+    if (tid < (nsl < kFinSlots ? nsl : kFinSlots)) sslot[tid] = slot_of(tid);
+    __syncthreads();   // FP statistics complete (FP path), first slots known
+    if (p.has_mid && tid < ROWS) { m_row[tid] = fp_ml.x; l_row[tid] = fp_ml.y; }
+    __syncthreads();
     for (int j0 = 0; j0 < nsl; j0 += kFinSlots) {
         const int nj = (nsl - j0) < kFinSlots ? (nsl - j0) : kFinSlots;
-        if (j0 > 0) __syncthreads();
+        if (j0 > 0) {
+            __syncthreads();
+            if (tid < nj) sslot[tid] = slot_of(j0 + tid);
+            __syncthreads();
+        }
         // outputs of the first PRE partials are requested together with the
         // statistics: one memory round trip for the usual handful of partials
         float2 pre[PRE][OUTS];
@@ -1438,14 +1721,17 @@ finish_kernel(FinParams p) {
             for (int k = 0; k < OUTS; ++k) {
                 const int i = tid + k * kFinThreads;
                 pre[j][k] = make_float2(0.f, 0.f);
-                if (j < nj && i < rows * D2) {
+                const int sl_j = j < nj ? sslot[j] : -1;
+                if (sl_j >= 0 && i < rows * D2) {
                     const int r = i / D2, d2 = i % D2;
-                    pre[j][k] = *reinterpret_cast<const float2*>(p.ws_o + ((int64_t)slot_of(j0 + j) * rows + r) * D + 2 * d2);
+                    pre[j][k] = *reinterpret_cast<const float2*>(p.ws_o + ((int64_t)sl_j * rows + r) * D + 2 * d2);
                 }
             }
         for (int i = tid; i < nj * rows; i += kFinThreads) {
             const int j = i / rows, r = i % rows;
-            const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + ((int64_t)slot_of(j0 + j) * rows + r) * 2);
+            const int sl_j = sslot[j];
+            const float2 ml = sl_j >= 0 ? *reinterpret_cast<const float2*>(p.ws_ml + ((int64_t)sl_j * rows + r) * 2)
+                                        : make_float2(-INFINITY, 0.f);
             sw[j * ROWS + r] = ml.x;
             sl[j * ROWS + r] = ml.y;
         }
@@ -1486,8 +1772,8 @@ finish_kernel(FinParams p) {
             }
             for (int j = PRE; j < nj; ++j) {
                 const float w = sw[j * ROWS + r];
-                if (w == 0.f) continue;
-                const float2 ov = *reinterpret_cast<const float2*>(p.ws_o + ((int64_t)slot_of(j0 + j) * rows + r) * D + 2 * d2);
+                if (w == 0.f) continue;   // also every missing slot
+                const float2 ov = *reinterpret_cast<const float2*>(p.ws_o + ((int64_t)sslot[j] * rows + r) * D + 2 * d2);
                 a0 = fmaf(w, ov.x, a0);
                 a1 = fmaf(w, ov.y, a1);
             }
@@ -1496,6 +1782,7 @@ finish_kernel(FinParams p) {
         }
     }
     __syncthreads();
+    FADE_TRF(11);
     if (tid < rows) f_row[tid] = l_row[tid] > 0.f ? 1.f / l_row[tid] : 0.f;
     if (p.rotation && nsl > 0) {
         // middle part is in the rotated basis: mid @ R (rows via shared memory)
@@ -1534,13 +1821,6 @@ finish_kernel(FinParams p) {
         T* o = out + (int64_t)b * p.o_sb + (int64_t)(h * p.g + j) * p.o_sh + (int64_t)sq * p.o_ss + 2 * d2;
         o[0] = Elem<DT>::from_f((acc_f[k][0] + acc_m[k][0]) * inv);
         o[1] = Elem<DT>::from_f((acc_f[k][1] + acc_m[k][1]) * inv);
-    }
-    // The last CTA of b (every CTA of b has read mid_len[b]; the middle grid,
-    // which reads it too, has completed) advances the length and re-arms the
-    // counter for the next call.
-    if (p.age && tid == 0 && s_age[1]) {
-        if (room) p.mid_len[b] = (int32_t)(age_n + 1);
-        p.age_cnt[b] = 0;
     }
     FADE_TRF(3);
 }
@@ -1620,6 +1900,8 @@ struct MidKernelInfo {
     void* fn;
     int smem;
     int occ;
+    int threads;
+    int groups;
 };
 
 // Function attributes are per device: configure each (kernel, device) once.
@@ -1639,8 +1921,10 @@ static MidKernelInfo mid_info() {
         cudaFuncSetAttribute(&middle_kernel<DT, D, KB, VB, VG, NT, QS>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, i.smem);
         int occ = 0;
+        i.threads = mid_threads(NT);
+        i.groups = mid_groups(NT);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, &middle_kernel<DT, D, KB, VB, VG, NT, QS>,
-                                                      kMidThreads, i.smem);
+                                                      i.threads, i.smem);
         i.occ = occ > 0 ? occ : 1;
         i.fn = reinterpret_cast<void*>(&middle_kernel<DT, D, KB, VB, VG, NT, QS>);
     }
@@ -1653,14 +1937,14 @@ static MidKernelInfo select_mid(int kb, int vb, bool vg, bool rot) {
     if (!rot && kb == 4 && vb == 2 && vg) return mid_info<DT, D, 4, 2, true, NT, false>();
     if (rot && kb == 4 && vb == 4 && !vg) return mid_info<DT, D, 4, 4, false, NT, true>();
     if (rot && kb == 2 && vb == 2 && !vg) return mid_info<DT, D, 2, 2, false, NT, true>();
-    return MidKernelInfo{nullptr, 0, 0};
+    return MidKernelInfo{nullptr, 0, 0, 0, 0};
 }
 
 template <int DT>
 static MidKernelInfo select_mid_d(int D, int NT, int kb, int vb, bool vg, bool rot) {
     if (D == 128) return NT == 1 ? select_mid<DT, 128, 1>(kb, vb, vg, rot) : select_mid<DT, 128, 2>(kb, vb, vg, rot);
     if (D == 64) return NT == 1 ? select_mid<DT, 64, 1>(kb, vb, vg, rot) : select_mid<DT, 64, 2>(kb, vb, vg, rot);
-    return MidKernelInfo{nullptr, 0, 0};
+    return MidKernelInfo{nullptr, 0, 0, 0, 0};
 }
 
 struct FinKernelInfo {
@@ -1701,7 +1985,7 @@ struct Plan {
     int64_t max_units;   // sizing bound
     int n_ctas;
     int n_fp;
-    size_t off_err, off_qrot, off_age, off_ml, off_o, total;
+    size_t off_err, off_qrot, off_age, off_fpml, off_fpo, off_ml, off_o, total;
     MidKernelInfo mk;
 };
 
@@ -1765,7 +2049,9 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
     pl->off_err = off; off += 256;
     pl->off_qrot = off;
     if (rot) off += ((size_t)d->B * d->Hq * d->n_q * d->D * 4 + 255) / 256 * 256;
-    pl->off_age = off; off += ((size_t)d->B * 4 + 255) / 256 * 256;
+    pl->off_age = off; off += ((size_t)Z * 4 + 255) / 256 * 256;
+    pl->off_fpml = off; off += ((size_t)Z * pl->rows * 2 * 4 + 255) / 256 * 256;
+    pl->off_fpo = off; off += ((size_t)Z * pl->rows * d->D * 4 + 255) / 256 * 256;
     pl->off_ml = off; off += ((size_t)pl->max_units * pl->rows * 2 * 4 + 255) / 256 * 256;
     pl->off_o = off; off += (size_t)pl->max_units * pl->rows * d->D * 4;
     pl->total = off;
@@ -1895,10 +2181,37 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
                          pl.n_ctas, pl.mk.occ, pl.mk.smem, scale_tma, (long long)n_rows);
         }
         mp.early = (a && a->prefetch_tiers) ? 1 : 0;
+        // FP tiers for the FP warp
+        mp.n_fp = 0;
+        for (int i = 0; i < d->n_segments; ++i) {
+            const fade_kv_segment& f = d->seg[i];
+            if (f.kind != FADE_SEG_FP) continue;
+            FpSeg& o = mp.fp[mp.n_fp++];
+            o.k = f.k; o.v = f.v; o.row_sb = f.row_sb; o.row_sh = f.row_sh;
+            o.row_base = f.row_base; o.lens = f.lens; o.len = f.len;
+            // fragments are read with 16-byte (K) and 8-byte (V) loads
+            if (!aligned16(f.k) || !aligned16(f.v)) return FADE_ERR_ALIGN;
+        }
+        mp.qo = d->q; mp.qo_sb = d->q_sb; mp.qo_sh = d->q_sh; mp.qo_ss = d->q_ss;
+        mp.ws_fpml = reinterpret_cast<float*>(ws + pl.off_fpml);
+        mp.ws_fpo = reinterpret_cast<float*>(ws + pl.off_fpo);
+        mp.ws_age = reinterpret_cast<int*>(ws + pl.off_age);
+        if (a) {
+            mp.age = 1;
+            mp.ring_fp = 0;
+            for (int i = 0; i < a->ring_seg; ++i) mp.ring_fp += d->seg[i].kind == FADE_SEG_FP ? 1 : 0;
+            mp.ring_cap = a->ring_cap;
+            mp.ring_origin = a->ring_origin;
+            mp.k_new = a->k_new; mp.v_new = a->v_new; mp.new_sb = a->new_sb; mp.new_sh = a->new_sh;
+            mp.mid_cap = sg.max_len;
+            mp.mid_len = sg.lens;
+            mp.age_k = reinterpret_cast<uint8_t*>(const_cast<void*>(sg.k));
+            mp.age_v = reinterpret_cast<uint8_t*>(const_cast<void*>(sg.v));
+        }
         mp.q_vec = aligned16(sg.k_scale) && sg.ks_sb % 8 == 0 && sg.ks_sh % 8 == 0 &&
                    (rot || (aligned16(d->q) && d->q_sb % 8 == 0 && d->q_sh % 8 == 0 && d->q_ss % 8 == 0));
         void* args[] = {(void*)&tk, (void*)&tv, (void*)&ts, (void*)&mp};
-        FADE_CUDA_TRY(launch_pdl(pl.mk.fn, dim3((unsigned)pl.n_ctas), dim3(kMidThreads),
+        FADE_CUDA_TRY(launch_pdl(pl.mk.fn, dim3((unsigned)pl.n_ctas), dim3((unsigned)pl.mk.threads),
                                  (size_t)pl.mk.smem, s, args));
     }
     // Finisher: FP tiers + merge of the middle partials -> out.  Always
@@ -1922,26 +2235,16 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
     fp.cu_units = d->cu_units;
     fp.units_per_z = pl.units_per_z;
     fp.n_ctas = pl.n_ctas;
+    fp.groups = has_mid ? pl.mk.groups : 1;
     fp.ws_ml = reinterpret_cast<const float*>(ws + pl.off_ml);
     fp.ws_o = reinterpret_cast<const float*>(ws + pl.off_o);
     fp.rotation = rot ? d->rotation : nullptr;
+    fp.ws_fpml = reinterpret_cast<const float*>(ws + pl.off_fpml);
+    fp.ws_fpo = reinterpret_cast<const float*>(ws + pl.off_fpo);
+    fp.ws_age = reinterpret_cast<const int*>(ws + pl.off_age);
     if (a) {
-        const fade_kv_segment& md = d->seg[a->mid_seg];
         fp.age = 1;
-        fp.ring_fp = 0;
-        for (int i = 0; i < a->ring_seg; ++i) fp.ring_fp += d->seg[i].kind == FADE_SEG_FP ? 1 : 0;
-        fp.ring_cap = a->ring_cap;
-        fp.ring_origin = a->ring_origin;
-        fp.k_new = a->k_new; fp.v_new = a->v_new; fp.new_sb = a->new_sb; fp.new_sh = a->new_sh;
-        fp.mid_k = reinterpret_cast<uint8_t*>(const_cast<void*>(md.k));
-        fp.mid_v = reinterpret_cast<uint8_t*>(const_cast<void*>(md.v));
-        fp.mid_vs = const_cast<void*>(md.v_scale);
-        fp.mid_ks = md.k_scale; fp.ks_sb = md.ks_sb; fp.ks_sh = md.ks_sh;
-        fp.mid_sb = md.row_sb; fp.mid_sh = md.row_sh; fp.mid_row_base = md.row_base;
-        fp.mid_cap = md.max_len;
-        fp.mid_len = const_cast<int32_t*>(md.lens);
-        fp.age_cnt = reinterpret_cast<int*>(ws + pl.off_age);
-        if (!aligned16(a->k_new) || !aligned16(a->v_new) || (a->new_sb * 2) % 16 || (a->new_sh * 2) % 16) fp.vec = 0;
+        fp.mid_len = const_cast<int32_t*>(d->seg[a->mid_seg].lens);
     }
     const FinKernelInfo fk = d->dtype == FADE_F16 ? select_fin<FADE_F16>(d->D, pl.NT)
                                                   : select_fin<FADE_BF16>(d->D, pl.NT);
