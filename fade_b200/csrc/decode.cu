@@ -66,7 +66,7 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // middle CTA c: row 4c + group for the consumer groups (lane 0 of the
 // group's first warp), row 4c + 3 for the producer
 #define FADE_TR(slot) do { if ((threadIdx.x & 127) == 0 && threadIdx.x < blockDim.x - 32 && blockIdx.x < 192 && (slot) < kTraceEv) g_trace[(blockIdx.x * 4 + threadIdx.x / 128) * kTraceEv + (slot)] = gtimer(); } while (0)
-#define FADE_TRP(slot) do { if (threadIdx.x == blockDim.x - 32 && blockIdx.x < 192 && (slot) < kTraceEv) g_trace[(blockIdx.x * 4 + 3) * kTraceEv + (slot)] = gtimer(); } while (0)
+#define FADE_TRP(slot) do { if (threadIdx.x == (blockDim.x / 32 - 1) / 5 * 4 * 32 && blockIdx.x < 192 && (slot) < kTraceEv) g_trace[(blockIdx.x * 4 + 3) * kTraceEv + (slot)] = gtimer(); } while (0)
 // finisher CTAs record into rows 768.. of the same array
 #define FADE_TRF(slot) do { if (threadIdx.x == 0 && blockIdx.x < 256) g_trace[(768 + blockIdx.x) * kTraceEv + (slot)] = gtimer(); } while (0)
 #else
@@ -81,8 +81,10 @@ constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
 // producer warp and one ring of stages; group g
 // consumes stages g, g+G, g+2G, ...
 __host__ __device__ constexpr int mid_groups(int NT) { return NT == 1 ? 3 : 1; }
-// + the producer warp + the FP-tier warp
-__host__ __device__ constexpr int mid_threads(int NT) { return (mid_groups(NT) * kConsumerWarps + 2) * 32; }
+// + one producer warp per group + the FP-tier warp
+__host__ __device__ constexpr int mid_threads(int NT) {
+    return (mid_groups(NT) * (kConsumerWarps + 1) + 1) * 32;
+}
 constexpr int kMidMaxStages = 15;
 constexpr int kSmemPerBlock = 232448;  // 227 KB opt-in shared memory per CTA
 constexpr float kLog2e = 1.4426950408889634f;
@@ -263,14 +265,15 @@ template <> struct Pk<FADE_BF16> {
 // multiplies by the scale with one packed multiply, which rounds exactly like
 // the reference's `q.to(dtype) * scale.to(dtype)` (fade/quant.py:124-127).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t shr_k(uint32_t x, int i) { return x >> (4 * (i + 1)); }
 template <int DT> struct Conv {
     // INT4: bytes b0..b3 of x hold elements (2j: high nibble, 2j+1: low).
     // h[0]=(e1,e5) h[1]=(e0,e4) h[2]=(e3,e7) h[3]=(e2,e6)
     __device__ __forceinline__ static void int4(uint32_t x, uint32_t (&h)[4]) {
         h[0] = Pk<DT>::sub(lop3_and_xor(x, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
-        h[1] = Pk<DT>::sub(lop3_and_xor(x >> 4, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
-        h[2] = Pk<DT>::sub(lop3_and_xor(x >> 8, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
-        h[3] = Pk<DT>::sub(lop3_and_xor(x >> 12, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+        h[1] = Pk<DT>::sub(lop3_and_xor(shr_k(x, 0), 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+        h[2] = Pk<DT>::sub(lop3_and_xor(shr_k(x, 1), 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+        h[3] = Pk<DT>::sub(lop3_and_xor(shr_k(x, 2), 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
     }
     // 2-bit: field f of a byte sits at bit 6-2f.  h[0..3] = fields 3,2,1,0 of
     // bytes (0,2); h[4..7] = fields 3,2,1,0 of bytes (1,3).
@@ -809,12 +812,14 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int G = L::G, NS = L::NS;
-    constexpr int PRODUCER = G * kConsumerWarps;   // warp index of the producer
+    constexpr int PRODUCER = G * kConsumerWarps;   // first producer warp (one per group)
+    constexpr int FPWARP = PRODUCER + G;            // the FP-tier warp
     const uint32_t bar_base = smem_u32(smem + L::BAR_OFF);
     auto full_bar = [&](int s) { return bar_base + 8u * s; };
     auto empty_bar = [&](int s) { return bar_base + 8u * (NS + s); };
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const bool is_producer = warp >= PRODUCER && warp < FPWARP;
     const int Z = p.B * p.Hkv;
     const int U = total_units(p, Z);
     // Never more CTAs than units, so every working CTA owns at least one unit
@@ -851,17 +856,21 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // next kernel in the stream start its prologue.  With `early` the tiers
     // are known not to be written by that kernel: the producer starts
     // streaming at once and only the consumers (queries, partial slots) wait.
-    if (!(p.early && warp == PRODUCER)) griddep_wait();
+    if (!(p.early && is_producer)) griddep_wait();
     if (warp < PRODUCER) griddep_launch_dependents();
     FADE_TR(1);
-    if (warp == PRODUCER + 1) {
+    if (warp == FPWARP) {
         fp_rows_warp<DT, D, NT>(p, c, (int)gridDim.x, smem + L::AB_OFF);
         return;
     }
     if (ub >= ue) return;
 
-    if (warp == PRODUCER) {
-        // ------------------------------ producer ------------------------------
+    if (is_producer) {
+        // ------------------------------ producers ------------------------------
+        // One warp per consumer group, each filling only its group's slots
+        // (stages g, g+G, ...), so a group that pauses (row flush) never
+        // holds back the other groups' stages.
+        const int pg = warp - PRODUCER;
         const uint64_t policy = evict_first_policy();
         if (lane == 0) {
             prefetch_tmap(&tmap_k);
@@ -870,7 +879,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         }
         int z = z_of_unit(p, Z, ub);
         int zb = units_begin(p, z), ze = units_begin(p, z + 1);
-        for (int u = ub, i = 0; u < ue; ++u, ++i) {
+        for (int i = pg; ub + i < ue; i += G) {
+            const int u = ub + i;
             while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
             const int s = i % NS;
             const uint32_t ph = (uint32_t)(i / NS) & 1u;
@@ -926,10 +936,15 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             }
             mbar_arrive(full_bar(s));
         }
-        // Drain: wait until the consumers released every stage still in flight,
-        // so no TMA write targets this CTA's shared memory after it exits.
+        // Drain: wait until the group released every stage still in flight,
+        // so no TMA write targets this CTA's shared memory after it exits:
+        // the waits the group's next NS/G stages would make.
         const int n = ue - ub;
-        for (int i = (n > NS ? n : NS); i < n + NS; ++i) {
+        int i_next = pg;
+        while (i_next < n) i_next += G;
+        for (int k = 0; k < NS / G; ++k) {
+            const int i = i_next + k * G;
+            if (i - NS < 0) continue;   // that slot was never used
             const int s = i % NS;
             const uint32_t ph = (uint32_t)(i / NS) & 1u;
             mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.ws_err);
@@ -1171,6 +1186,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         }
         const int s = i % NS;
         const uint32_t ph = (uint32_t)(i / NS) & 1u;
+        if (i / G < 24) FADE_TR(40 + i / G);
         const bool ready = mbar_wait(full_bar(s), ph, abort_flag, p.ws_err);
         if (i / G < 24) FADE_TR(10 + i / G);
         const int tw = (u - zb) * kStageTokens + gw * 32;  // first token of this gw (row-relative)
