@@ -91,7 +91,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 // Initial running maximum of the middle kernel's online softmax: finite and
 // below any real score, so exp2(score - max) never sees inf - inf.
 constexpr float kMaskedMax = -1e30f;
-constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polling
+constexpr uint32_t kWaitPolls = 1u << 15;   // bounded mbarrier polling ...
+constexpr uint32_t kWaitHintNs = 10000;     // ... of up to 10 us each
 
 // ---------------------------------------------------------------------------
 // PTX wrappers (mbarrier, TMA, ldmatrix, movmatrix, mma)
@@ -121,6 +122,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait that lets the hardware suspend the warp up to `ns` nanoseconds
+// until the phase completes (fewer polling instructions while waiting)
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait: gives up after kWaitLimit polls (each poll may suspend the
 // thread for a hardware-defined interval) and never spins forever.  A CTA-wide
 // abort flag makes every later wait of the CTA fail at once, so a CTA whose
@@ -130,9 +143,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           int* err) {
     if (mbar_try_wait(bar, parity)) return true;   // common case: one poll
     if (*abort_flag) return false;
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 1023u) == 1023u && *abort_flag) return false;
+    // each poll suspends up to kWaitHintNs: at most kWaitPolls * kWaitHintNs
+    // (about 0.3 s) in total, then the CTA aborts
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        if (mbar_try_wait_hint(bar, parity, kWaitHintNs)) return true;
+        if ((i & 63u) == 63u && *abort_flag) return false;
     }
     *abort_flag = 1;
     atomicExch(err, 1);
@@ -465,6 +480,62 @@ __device__ __forceinline__ uint32_t tile_off(int tok, int cb) {
     const int row = tok / TPR;
     const int chunk = (tok % TPR) * NCH + cb;
     return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// Per-lane shared-memory offsets of the ldmatrix reads of a warp's two
+// 16-token m-tiles, computed once per kernel.  When an m-tile step moves the
+// swizzle rows by a multiple of 8 the second m-tile is the first plus a
+// constant (the XOR pattern repeats every 8 rows).
+template <int NCH>
+struct TileOffs {
+    static constexpr int TPR = 8 / NCH;
+    static constexpr int NX = (2 * NCH >= 4) ? 2 * NCH / 4 : 1;
+    static constexpr bool SHIFT = ((16 / TPR) % 8) == 0;
+    static constexpr uint32_t MT_STEP = (16 / TPR) * 128;
+    uint32_t o[SHIFT ? 1 : 2][NX];
+    __device__ __forceinline__ TileOffs(int trow_warp, int lane) {
+#pragma unroll
+        for (int mt = 0; mt < (SHIFT ? 1 : 2); ++mt)
+#pragma unroll
+            for (int x = 0; x < NX; ++x) {
+                const int trow0 = trow_warp + mt * 16;
+                if constexpr (2 * NCH >= 4) {
+                    const int mi = x * 4 + lane / 8;
+                    o[mt][x] = tile_off<NCH>(trow0 + (mi / NCH) * 8 + (lane & 7), mi % NCH);
+                } else {
+                    o[mt][x] = tile_off<NCH>(trow0 + ((lane / 8) & 1) * 8 + (lane & 7), 0);
+                }
+            }
+    }
+    __device__ __forceinline__ uint32_t get(int mt, int x) const {
+        if constexpr (SHIFT) return o[0][x] + (uint32_t)mt * MT_STEP;
+        else return o[mt][x];
+    }
+};
+
+template <int NCH, bool TRANS>
+__device__ __forceinline__ void load_tiles_at(uint32_t base, const TileOffs<NCH>& to, int mt,
+                                              uint32_t (&r)[2][NCH]) {
+    constexpr int NMAT = 2 * NCH;
+    if constexpr (NMAT >= 4) {
+#pragma unroll
+        for (int x = 0; x < NMAT / 4; ++x) {
+            uint32_t r4[4];
+            if constexpr (TRANS) ldsm_x4_t(base + to.get(mt, x), r4);
+            else ldsm_x4(base + to.get(mt, x), r4);
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                const int mj = x * 4 + y;
+                r[mj / NCH][mj % NCH] = r4[y];
+            }
+        }
+    } else {
+        uint32_t r2[2];
+        if constexpr (TRANS) ldsm_x2_t(base + to.get(mt, 0), r2);
+        else ldsm_x2(base + to.get(mt, 0), r2);
+        r[0][0] = r2[0];
+        r[1][0] = r2[1];
+    }
 }
 
 template <int NCH, bool TRANS>
@@ -958,6 +1029,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     const int gid = lane >> 2, t = lane & 3;
     const int ctid = gw * 32 + lane;         // 0..127 within the group
     const int bar_id = 1 + grp;              // the group's named barrier
+    const TileOffs<L::NCHK> koffs(gw * 32, lane);
+    const TileOffs<L::NCHV> voffs(gw * 32, lane);
     float* obuf = reinterpret_cast<float*>(smem + L::RING_BYTES + grp * (L::OBUF_BYTES + L::ML_BYTES));
     float* mlbuf = obuf + L::OBUF_BYTES / 4;
     uint32_t qf[NQ][NT][KSTEPS][2];  // B fragments (exact model-dtype query)
@@ -1170,6 +1243,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     int z = z_of_unit(p, Z, ub);
     int zb = units_begin(p, z), ze = units_begin(p, z + 1);
 
+    int s = grp;            // ring slot of stage i = i % NS
+    uint32_t ph = 0;        // its phase parity = (i / NS) & 1
     for (int i = grp; ub + i < ue; i += G) {
         const int u = ub + i;
         while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
@@ -1184,8 +1259,6 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             cur_z = z;
             z_first = u;
         }
-        const int s = i % NS;
-        const uint32_t ph = (uint32_t)(i / NS) & 1u;
         if (i / G < 24) FADE_TR(40 + i / G);
         const bool ready = mbar_wait(full_bar(s), ph, abort_flag, p.ws_err);
         if (i / G < 24) FADE_TR(10 + i / G);
@@ -1208,7 +1281,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 #pragma unroll
                     for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = sacc2[mt][nt][e] = 0.f;
                 uint32_t kr[2][L::NCHK];
-                load_tiles<L::NCHK, false>(kbase, gw * 32 + mt * 16, lane, kr);
+                load_tiles_at<L::NCHK, false>(kbase, koffs, mt, kr);
 #pragma unroll
                 for (int cb = 0; cb < L::NCHK; ++cb) {
                     if constexpr (KB == 4) {
@@ -1327,7 +1400,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             for (int mt = 0; mt < (FADE_ABLATE == 2 ? 0 : 2); ++mt) {
                 const int trow0 = gw * 32 + mt * 16;
                 uint32_t vr[2][L::NCHV];
-                load_tiles<L::NCHV, true>(vbase, trow0, lane, vr);
+                load_tiles_at<L::NCHV, true>(vbase, voffs, mt, vr);
                 // tokens of this m-tile past the length: their scales may be
                 // stale bytes (NaN * 0 must not reach the MMA), so zero them;
                 // a tile entirely past the length is skipped.
@@ -1410,6 +1483,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(s));
+        s += G;
+        if (s >= NS) { s -= NS; ph ^= 1u; }
     }
     FADE_TR(36);
     if (cur_z >= 0 && FADE_ABLATE != 6) flush(cur_z);
