@@ -41,7 +41,11 @@ def parse():
     ap.add_argument("--impl", choices=("fade", "reference"), default="fade")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--layers", type=int, default=CFG["layers"],
+                    help="layers per step (profiling captures use 1; the benchmark is 32)")
+    args = ap.parse_args()
+    CFG["layers"] = args.layers
+    return args
 
 
 def dist_env():
