@@ -122,6 +122,39 @@ def _row_aligned(tier, rbk: int, rbv: int) -> bool:
     return True
 
 
+def _code_bits(tier) -> tuple[int, int]:
+    if isinstance(tier, Int4Tier):
+        return 4, 4
+    if isinstance(tier, Int4K2VTier):
+        return 4, 2
+    if isinstance(tier, RotTier):
+        return tier.bits, tier.bits
+    raise TypeError(f"unknown tier {type(tier)}")
+
+
+def align_tier(tier, D: int):
+    """A copy of a quantised tier that the middle kernel can stream: each
+    (b, h) segment padded to a multiple of 128 tokens so it starts on a
+    128-byte code row (the tier itself when it already does).  Caches that
+    keep a tier across many decode steps align it once."""
+    import dataclasses
+
+    kb, vb = _code_bits(tier)
+    if _row_aligned(tier, D * kb // 8, D * vb // 8) or tier.lens is not None:
+        return tier
+    S = tier.k_packed.shape[2]
+    S_pad = -(-S // 128) * 128
+    changes = dict(k_packed=_pad_rows(tier.k_packed, S_pad), v_packed=_pad_rows(tier.v_packed, S_pad))
+    if isinstance(tier, Int4K2VTier):
+        G = int(tier.group)
+        changes["v_scale"] = _pad_rows(tier.v_scale, S_pad // G)
+        changes["length"] = tier.length if tier.length is not None else S
+    else:
+        changes["v_scale"] = _pad_rows(tier.v_scale, S_pad)
+        changes["max_len"] = tier.max_len if tier.max_len is not None else S
+    return dataclasses.replace(tier, **changes)
+
+
 def _fill_mid(seg: _lib.KVSegment, tier, D: int, dtype: torch.dtype) -> list:
     if isinstance(tier, Int4Tier):
         seg.kind, kb, vb = _lib.SEG_INT4, 4, 4
@@ -135,25 +168,9 @@ def _fill_mid(seg: _lib.KVSegment, tier, D: int, dtype: torch.dtype) -> list:
         raise TypeError(f"unknown tier {type(tier)}")
     rbk, rbv = D * kb // 8, D * vb // 8
     if not _row_aligned(tier, rbk, rbv) and tier.lens is None:
-        # copy into a padded layout the kernel can stream (sequence padded to 128)
-        import dataclasses
-
-        S = tier.k_packed.shape[2]
-        S_pad = -(-S // 128) * 128
-        length = getattr(tier, "length", None)
-        changes = dict(k_packed=_pad_rows(tier.k_packed, S_pad), v_packed=_pad_rows(tier.v_packed, S_pad))
-        if isinstance(tier, Int4K2VTier):
-            G = int(tier.group)
-            changes["v_scale"] = _pad_rows(tier.v_scale, S_pad // G)
-        else:
-            changes["v_scale"] = _pad_rows(tier.v_scale, S_pad)
-        if isinstance(tier, Int4K2VTier):
-            changes["length"] = length if length is not None else S
-        elif isinstance(tier, (Int4Tier, RotTier)):
-            changes["max_len"] = tier.max_len if tier.max_len is not None else S
-        tier = dataclasses.replace(tier, **changes)
-        if isinstance(tier, (Int4Tier, RotTier)) and tier.lens is None:
-            seg.len = S
+        tier = align_tier(tier, D)
+        if isinstance(tier, (Int4Tier, RotTier)):
+            seg.len = tier.max_len
     sb, sh = _row_strides(tier.k_packed, rbk, "middle k codes")
     if _row_strides(tier.v_packed, rbv, "middle v codes") != (sb, sh):
         raise ValueError("middle K and V codes must share a row layout")

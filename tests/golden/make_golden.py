@@ -39,6 +39,63 @@ def outlier_tensor(shape, gen, n_out=4, mult=8.0):
     return x
 
 
+def rope_schemes(ref: str) -> None:
+    """cos/sin tables of every RoPE scheme family (fade/rope.py)."""
+    sys.path.insert(0, ref)
+    from fade import rope as R
+
+    schemes = {
+        "vanilla": R.Vanilla(theta=5e5, head_dim=128),
+        "linear": R.LinearScaled(theta=1e4, head_dim=64, factor=4.0),
+        "llama3": R.Llama3(theta=5e5, head_dim=128, factor=8.0, low_freq_factor=1.0, high_freq_factor=4.0,
+                           original_max_position_embeddings=8192),
+        "ntk": R.NtkAware(theta=1e4, head_dim=64, factor=2.0),
+        "yarn": R.Yarn(theta=1e6, head_dim=128, factor=4.0, original_max_position_embeddings=32768),
+        "proportional": R.Proportional(theta=1e4, head_dim=64, partial_rotary_factor=0.5),
+        "mrope": R.MRope(theta=1e6, head_dim=128, partial_rotary_factor=1.0, mrope_section=[16, 24, 24]),
+        "norope": R.NoRope(theta=1e4, head_dim=64),
+    }
+    pos = torch.tensor([0, 1, 2, 3, 17, 255, 4095, 8191, 32767, 100000])
+    out = {"positions": pos.numpy()}
+    for name, sc in schemes.items():
+        for dn, dt in (("f16", torch.float16), ("bf16", torch.bfloat16)):
+            c, s_ = sc.compute_cos_sin(pos, torch.device("cpu"), model_dtype=dt)
+            out[f"{name}_{dn}_cos"] = c[0, 0].numpy()
+            out[f"{name}_{dn}_sin"] = s_[0, 0].numpy()
+    np.savez_compressed(OUT / "rope_schemes.npz", **out)
+
+
+def cache_perseq(ref: str) -> None:
+    """Per-sequence tier assignment (fade/cache.py:1059-1230): two rows with
+    different evictions, then the stored FP16 / INT4 tiers and positions."""
+    sys.path.insert(0, ref)
+    from fade.cache import TIER_EVICT, TIER_FP16, TIER_INT4, TieredKVCache
+    from fade.rope import Vanilla
+
+    gen = torch.Generator().manual_seed(5)
+    B, H, D, S = 2, 2, 64, 160
+    dt = torch.float16
+    scheme = Vanilla(theta=1e4, head_dim=D)
+    c, s_ = scheme.compute_cos_sin(torch.arange(S), torch.device("cpu"), model_dtype=dt)
+    k = TieredKVCache._apply_rope(outlier_tensor((B, H, S, D), gen).to(dt), c, s_)
+    v = outlier_tensor((B, H, S, D), gen).to(dt)
+    cache = TieredKVCache(n_sink=4, recent_window=16, int4_budget=80, dtype=dt, head_dim=D, rope_scheme=scheme)
+    cache.update(k, v, 0)
+    t = torch.full((B, S), TIER_INT4, dtype=torch.long)
+    t[:, :4] = TIER_FP16
+    t[:, S - 16:] = TIER_FP16
+    t[0, 10:40] = TIER_EVICT          # row 0 loses 30 tokens
+    t[1, 50:60] = TIER_EVICT          # row 1 loses 10
+    cache.apply_tier_assignment_per_sequence(0, t)
+    st = cache._layers[0]
+    out = {"k": bits(k), "v": bits(v), "tiers": t.numpy(),
+           "fp16_k": bits(st.fp16_k), "fp16_v": bits(st.fp16_v), "fp16_pos": st.fp16_pos.numpy(),
+           "int4_kq": st.int4_kq.numpy(), "int4_ks": bits(st.int4_ks), "int4_vq": st.int4_vq.numpy(),
+           "int4_vs": bits(st.int4_vs), "int4_pos": st.int4_pos.numpy(),
+           "next_position": np.int64(st.next_position), "sink_count": np.int64(st.sink_count)}
+    np.savez_compressed(OUT / "cache_perseq.npz", **out)
+
+
 def main(ref: str) -> None:
     sys.path.insert(0, ref)
     import torch.nn.functional as F
@@ -215,7 +272,15 @@ def main(ref: str) -> None:
 if __name__ == "__main__":
     import os
 
-    ref_path = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FADE_REFERENCE_PATH")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    ref_path = args[0] if args else os.environ.get("FADE_REFERENCE_PATH")
     if not ref_path:
-        raise SystemExit("usage: make_golden.py <path to the reference checkout>")
-    main(ref_path)
+        raise SystemExit("usage: make_golden.py <path to the reference checkout> [--only-rope-schemes|--only-cache-perseq]")
+    if "--only-rope-schemes" in sys.argv:
+        rope_schemes(ref_path)
+    elif "--only-cache-perseq" in sys.argv:
+        cache_perseq(ref_path)
+    else:
+        main(ref_path)
+        rope_schemes(ref_path)
+        cache_perseq(ref_path)

@@ -1,0 +1,192 @@
+"""TieredKVCache / create_tiered_cache on the GPU against the reference's own
+cache states (fixtures made by running the reference: tests/golden/) and
+against transformers' SDPA path on the same model."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from gpu_util import assert_attn_close, t_bits, t_from_bits, t_vals
+
+pytestmark = pytest.mark.gpu
+TOL = {"f16": 2e-3, "bf16": 1e-2}
+
+
+def _tiers(S, n_sink=4, recent=64):
+    from fade_b200.cache import TIER_FP16, TIER_INT4
+
+    t = torch.full((S,), TIER_INT4, dtype=torch.long)
+    t[:n_sink] = TIER_FP16
+    t[S - recent:] = TIER_FP16
+    return t
+
+
+def _eq(t, ref_bits, what):
+    np.testing.assert_array_equal(t_bits(t), ref_bits, err_msg=what)
+
+
+def test_cache_cfg1_tiers_and_decode(cuda_device):
+    """Config-1 shape, no eviction: tiers bit-exact, fused decode vs the reference's SDPA."""
+    from fade_b200.cache import TieredKVCache
+
+    g = golden("decode_cfg1")
+    k, v, q = t_from_bits(g["k_roped"], "f16"), t_from_bits(g["v"], "f16"), t_from_bits(g["q"], "f16")
+    S = k.shape[2]
+    cache = TieredKVCache(n_sink=4, recent_window=64, dtype=torch.float16, rope_theta=1e6, head_dim=64)
+    K0, V0 = cache.update(k, v, 0)
+    assert torch.equal(K0, k) and torch.equal(V0, v) and cache.get_seq_length(0) == S
+    cache.apply_tier_assignment(0, _tiers(S))
+    st = cache._layers[0]
+    _eq(st.sink_k, g["sink_k"], "sink_k")
+    _eq(st.sink_v, g["sink_v"], "sink_v")
+    _eq(st.fp16_k, g["recent_k"], "recent_k")
+    _eq(st.fp16_v, g["recent_v"], "recent_v")
+    np.testing.assert_array_equal(st.int4_kq.cpu().numpy(), g["int4_kq"])
+    np.testing.assert_array_equal(st.int4_vq.cpu().numpy(), g["int4_vq"])
+    _eq(st.int4_ks, g["int4_ks"], "int4_ks")
+    _eq(st.int4_vs, g["int4_vs"], "int4_vs")
+    assert cache.get_seq_length(0) == S
+    out = cache.decode_attention(0, q)
+    assert_attn_close(t_vals(out), t_vals(t_from_bits(g["out_ref32"], "f32")), "f16", TOL["f16"])
+    # the materialised path (update with a new token) keeps working after reassignment
+    K, V = cache._materialize(0)
+    assert K.shape[2] == S
+
+
+def test_cache_cfg3_eviction_k4v2(cuda_device):
+    """Config-3 shape: H2O tiers with eviction (re-RoPE), K INT4 + V grouped INT2."""
+    from fade_b200.cache import TieredKVCache
+    from fade_b200.rope import Vanilla
+
+    g = golden("decode_cfg3_small")
+    k, v, q = t_from_bits(g["k_roped"], "f16"), t_from_bits(g["v"], "f16"), t_from_bits(g["q"], "f16")
+    D = k.shape[-1]
+    cache = TieredKVCache(n_sink=4, recent_window=64, int4_budget=100, dtype=torch.float16, rope_theta=1e6,
+                          head_dim=D, middle_v_bits=2, rope_scheme=Vanilla(theta=1e6, head_dim=D))
+    cache.update(k, v, 0)
+    cache.apply_tier_assignment(0, torch.from_numpy(g["tiers"]))
+    st = cache._layers[0]
+    assert st.next_position == int(g["next_position"]) and st.int4_pos.shape[0] == int(g["n_mid"])
+    for name, ref in (("sink_k", "sink_k"), ("sink_v", "sink_v"), ("fp16_k", "recent_k"), ("fp16_v", "recent_v")):
+        a = t_bits(getattr(st, name)).astype(np.int32)
+        b = g[ref].astype(np.int32)
+        # re-RoPE'd keys: exact or one ulp (fp32 rounding order); values exact
+        assert np.abs(a - b).max() <= (1 if name.endswith("_k") else 0), name
+    np.testing.assert_array_equal(st.int4_vq.cpu().numpy(), g["int4_vq2"])
+    _eq(st.int4_vs, g["int4_vs2"], "int4_vs (grouped INT2)")
+    kq_diff = (st.int4_kq.cpu().numpy() != g["int4_kq"]).mean()
+    assert kq_diff < 0.002, kq_diff    # codes of re-RoPE'd K: an ulp can cross a rounding boundary
+    out = cache.decode_attention(0, q)
+    assert_attn_close(t_vals(out), t_vals(t_from_bits(g["out_ref32"], "f32")), "f16", TOL["f16"])
+
+
+def test_cache_rotated_backend(cuda_device):
+    """Config-4 shape: rotated 2-bit backend; the fused kernel reads its codes directly."""
+    from fade_b200.backends import RotatedINT4Backend
+    from fade_b200.cache import TieredKVCache
+
+    g = golden("decode_rot_small")
+    k, v, q = t_from_bits(g["k"], "bf16"), t_from_bits(g["v"], "bf16"), t_from_bits(g["q"], "bf16")
+    D, S = k.shape[-1], k.shape[2]
+    cache = TieredKVCache(n_sink=4, recent_window=64, dtype=torch.bfloat16, head_dim=D,
+                          quant_backend=RotatedINT4Backend(head_dim=D, bits=2, seed=42))
+    cache.update(k, v, 0)
+    cache.apply_tier_assignment(0, _tiers(S))
+    st = cache._layers[0]
+    _eq(st.sink_k, g["sink_k"], "sink_k")
+    _eq(st.fp16_v, g["recent_v"], "recent_v")
+    for ours, ref in ((st.backend_k["packed"], "rot_kq"), (st.backend_v["packed"], "rot_vq")):
+        assert (ours.cpu().numpy() != g[ref]).mean() < 0.004, ref
+    out = cache.decode_attention(0, q)
+    assert_attn_close(t_vals(out), t_vals(t_from_bits(g["out_ref32"], "f32")), "bf16", TOL["bf16"], ulps=2,
+                      additive=True)
+
+
+def test_cache_per_sequence_assignment(cuda_device):
+    """Per-row tiers with different evictions: stored tiers as the reference's."""
+    from fade_b200.cache import TieredKVCache
+    from fade_b200.rope import Vanilla
+
+    g = golden("cache_perseq")
+    k, v = t_from_bits(g["k"], "f16"), t_from_bits(g["v"], "f16")
+    D = k.shape[-1]
+    cache = TieredKVCache(n_sink=4, recent_window=16, int4_budget=80, dtype=torch.float16, head_dim=D,
+                          rope_scheme=Vanilla(theta=1e4, head_dim=D))
+    cache.update(k, v, 0)
+    cache.apply_tier_assignment_per_sequence(0, torch.from_numpy(g["tiers"]))
+    st = cache._layers[0]
+    assert st.next_position == int(g["next_position"]) and st.sink_count == int(g["sink_count"])
+    np.testing.assert_array_equal(st.fp16_pos.cpu().numpy(), g["fp16_pos"])
+    np.testing.assert_array_equal(st.int4_pos.cpu().numpy(), g["int4_pos"])
+    assert np.abs(t_bits(st.fp16_k).astype(np.int32) - g["fp16_k"].astype(np.int32)).max() <= 1
+    _eq(st.fp16_v, g["fp16_v"], "fp16_v")
+    assert (st.int4_kq.cpu().numpy() != g["int4_kq"]).mean() < 0.002
+    np.testing.assert_array_equal(st.int4_vq.cpu().numpy(), g["int4_vq"])
+    _eq(st.int4_vs, g["int4_vs"], "int4_vs")
+    # fused decode over the per-sequence tiers == SDPA over the materialised cache
+    q = torch.randn(k.shape[0], 4, 1, D, device=k.device).to(torch.float16)
+    out = cache.decode_attention(0, q)
+    K, V = cache._materialize(0)
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), K.float(), V.float(), enable_gqa=True)
+    assert_attn_close(t_vals(out), t_vals(ref), "f16", TOL["f16"])
+
+
+def test_checkpoint_roundtrip(cuda_device):
+    from fade_b200.cache import TieredKVCache
+
+    g = golden("decode_cfg1")
+    k, v, q = t_from_bits(g["k_roped"], "f16"), t_from_bits(g["v"], "f16"), t_from_bits(g["q"], "f16")
+    a = TieredKVCache(n_sink=4, recent_window=64, dtype=torch.float16, head_dim=64)
+    a.update(k, v, 0)
+    a.apply_tier_assignment(0, _tiers(k.shape[2]))
+    sd = a.cache_state_dict()
+    assert sd["layer.0.int4_kq"].device.type == "cpu"
+    b = TieredKVCache(n_sink=4, recent_window=64, dtype=torch.float16, head_dim=64)
+    b.load_cache_state_dict(sd, device=k.device)
+    assert b.get_seq_length(0) == a.get_seq_length(0)
+    assert torch.equal(a.decode_attention(0, q), b.decode_attention(0, q))
+    assert b.compressed_storage_bytes() > 0 and a.storage_bytes() >= a.compressed_storage_bytes() - 2 * 4 * 64 * 2
+
+
+def _tiny_llama(dev):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig(vocab_size=256, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, rope_theta=5e5, max_position_embeddings=1024)
+    torch.manual_seed(0)
+    return LlamaForCausalLM(cfg).to(device=dev, dtype=torch.bfloat16).eval()
+
+
+def test_hf_decode_fused_matches_sdpa(cuda_device):
+    """A (random-init) Llama decodes through create_tiered_cache: the fused
+    tiered attention gives the logits of transformers' SDPA over the
+    materialised cache, before and after an INT4 reassignment."""
+    from fade_b200.patch import create_tiered_cache
+
+    dev = torch.device("cuda", 0)
+    m_fused, m_ref = _tiny_llama(dev), _tiny_llama(dev)
+    m_ref.load_state_dict(m_fused.state_dict())
+    c_fused = create_tiered_cache(m_fused, dtype=torch.bfloat16, n_sink=4, recent_window=64)
+    c_ref = create_tiered_cache(m_ref, dtype=torch.bfloat16, n_sink=4, recent_window=64, fused_attention=False)
+    assert c_fused.fused_decode and not c_ref.fused_decode
+    ids = torch.randint(0, 256, (2, 300), generator=torch.Generator().manual_seed(1)).to(dev)
+    with torch.no_grad():
+        lf = m_fused(input_ids=ids, past_key_values=c_fused, use_cache=True).logits[:, -1]
+        lr = m_ref(input_ids=ids, past_key_values=c_ref, use_cache=True).logits[:, -1]
+        assert torch.allclose(lf.float(), lr.float(), atol=1e-3)
+        nxt = lf.argmax(-1, keepdim=True)
+        for step in range(6):
+            if step == 2:   # compress the middle of every layer
+                for layer in range(2):
+                    S = c_fused.get_seq_length(layer)
+                    c_fused.apply_tier_assignment(layer, _tiers(S))
+                    c_ref.apply_tier_assignment(layer, _tiers(S))
+            lf = m_fused(input_ids=nxt, past_key_values=c_fused, use_cache=True).logits[:, -1].float()
+            lr = m_ref(input_ids=nxt, past_key_values=c_ref, use_cache=True).logits[:, -1].float()
+            err = (lf - lr).abs().max().item()
+            assert err < 0.05 * max(1.0, lr.abs().max().item()), (step, err)
+            nxt = lr.argmax(-1, keepdim=True)
+    assert c_fused.get_seq_length(0) == c_ref.get_seq_length(0) == 306
