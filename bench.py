@@ -187,7 +187,7 @@ def config_block(n):
 # --------------------------------------------------------------------------
 # fade arm (GPU)
 # --------------------------------------------------------------------------
-def build_decoder(dev, total_steps):
+def build_decoder(dev, total_steps, shard_start: int = 0):
     import torch
 
     from fade_b200.decoder import TieredDecoder
@@ -199,7 +199,7 @@ def build_decoder(dev, total_steps):
     gen = torch.Generator(device=dev)
     B, H, S, D = CFG["batch"], CFG["n_kv_heads"], CFG["context"], CFG["head_dim"]
     for layer in range(CFG["layers"]):
-        gen.manual_seed(1000 + layer)
+        gen.manual_seed(1000 + layer + 100003 * shard_start)   # this rank's rows of the global batch
         k = torch.randn(B, H, S, D, device=dev, generator=gen)
         v = torch.randn(B, H, S, D, device=dev, generator=gen)
         for h in range(H):
@@ -216,13 +216,17 @@ def run_fade(args, ws, rank, local):
     import torch
     import torch.distributed as dist
 
+    from fade_b200.shard import batch_shard, gather_objects, max_over_ranks
+
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     K, W = args.steps, max(3, args.warmup)
     roof_steps = min(K, 10)
     e2e_steps = 0 if args.no_e2e else min(K, 20)
     total = 2 + W + K + roof_steps + e2e_steps
-    dec, n_mid0 = build_decoder(dev, total)
+    start, rows = batch_shard(CFG["batch"] * ws, ws, rank)   # weak scaling: CFG["batch"] rows per GPU
+    assert rows == CFG["batch"]
+    dec, n_mid0 = build_decoder(dev, total, start)
     L = CFG["layers"]
     gen = torch.Generator(device=dev).manual_seed(7 + rank)
     q = torch.randn(dec.q.shape, device=dev, generator=gen).to(torch.bfloat16)
@@ -239,11 +243,7 @@ def run_fade(args, ws, rank, local):
 
     props = torch.cuda.get_device_properties(dev)
     bus = getattr(props, "pci_bus_id", None)
-    bus_ids = [bus] if bus is not None else []
-    if ws > 1:
-        gathered = [None] * ws
-        dist.all_gather_object(gathered, bus)
-        bus_ids = [b for b in gathered if b is not None]
+    bus_ids = [b for b in gather_objects(bus) if b is not None]
     sampler = ClockSampler(bus_ids) if rank == 0 else None
 
     # ---------------- timed region: K graph replays ----------------
@@ -262,11 +262,7 @@ def run_fade(args, ws, rank, local):
     if ws > 1:
         dist.barrier()
     clocks = sampler.stop() if sampler else None
-    ms = e0.elapsed_time(e1)
-    t_ms = torch.tensor([ms], device=dev)
-    if ws > 1:
-        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
-    ms_max = float(t_ms.item())
+    ms_max = max_over_ranks(e0.elapsed_time(e1), dev)   # the job's step time: slowest rank
     dec.check_device_errors()
 
     # bytes over the timed steps (the middle grows by one token per step)
@@ -326,15 +322,13 @@ def run_fade(args, ws, rank, local):
             dec.step_host(qh, kh, vh, oh)
         s1.record()
         torch.cuda.synchronize(dev)
-        e_ms = torch.tensor([s0.elapsed_time(s1)], device=dev)
-        if ws > 1:
-            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e_ms = max_over_ranks(s0.elapsed_time(s1), dev)
         n_e = n_mid_start + K + roof_steps + 1
         eb = sum((sum(algorithmic_bytes(n_e + i + 1)) * L) for i in range(e2e_steps))
-        e2e = {"value": round(eb * ws / (float(e_ms.item()) / 1e3) / 1e9, 3), "unit": "GB/s",
+        e2e = {"value": round(eb * ws / (e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": int(qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2),
                "d2h_bytes_per_step": int(oh.numel() * 2),
-               "ms_per_step": round(float(e_ms.item()) / e2e_steps, 4)}
+               "ms_per_step": round(e_ms / e2e_steps, 4)}
 
     if rank != 0:
         return
