@@ -140,10 +140,11 @@ def align_tier(tier, D: int):
     import dataclasses
 
     kb, vb = _code_bits(tier)
-    if _row_aligned(tier, D * kb // 8, D * vb // 8) or tier.lens is not None:
+    same_rows = tier.k_packed.shape[2] == tier.v_packed.shape[2]
+    if tier.lens is not None or (same_rows and _row_aligned(tier, D * kb // 8, D * vb // 8)):
         return tier
-    S = tier.k_packed.shape[2]
-    S_pad = -(-S // 128) * 128
+    S = tier.k_packed.shape[2]          # valid tokens (V may carry group padding beyond)
+    S_pad = -(-max(S, tier.v_packed.shape[2]) // 128) * 128
     changes = dict(k_packed=_pad_rows(tier.k_packed, S_pad), v_packed=_pad_rows(tier.v_packed, S_pad))
     if isinstance(tier, Int4K2VTier):
         G = int(tier.group)
@@ -167,7 +168,8 @@ def _fill_mid(seg: _lib.KVSegment, tier, D: int, dtype: torch.dtype) -> list:
     else:
         raise TypeError(f"unknown tier {type(tier)}")
     rbk, rbv = D * kb // 8, D * vb // 8
-    if not _row_aligned(tier, rbk, rbv) and tier.lens is None:
+    if tier.lens is None and (not _row_aligned(tier, rbk, rbv)
+                              or tier.k_packed.shape[2] != tier.v_packed.shape[2]):
         tier = align_tier(tier, D)
         if isinstance(tier, (Int4Tier, RotTier)):
             seg.len = tier.max_len
