@@ -49,7 +49,8 @@ namespace fade {
 // Ablation switch for profiling builds only (default 0 = full kernel):
 // 1 = consumers only cycle the pipeline, 2 = QK^T only, 3 = no scale multiply,
 // 4 = as 1 without the L2 cache hint, 5 = as 1 without the scale copy,
-// 6 = as 1 without per-row setup / flush / merge.
+// 6 = as 1 without per-row setup / flush / merge, 7 = no softmax (P = S),
+// 8 = no K dequantisation (raw code words into the MMA), 9 = no V dequantisation.
 #ifndef FADE_ABLATE
 #define FADE_ABLATE 0
 #endif
@@ -1269,7 +1270,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         const uint32_t vbase = smem_u32(st + L::V_OFF);
         const uint8_t* scb = smem + L::SC_BASE + s * L::SC_BYTES;
 
-        if (ready && tw < clen && FADE_ABLATE != 1 && FADE_ABLATE < 4) {
+        if (ready && tw < clen && FADE_ABLATE != 1 && FADE_ABLATE != 4 && FADE_ABLATE != 5 && FADE_ABLATE != 6) {
             // ---- S^T = K_deq . q^T for the gw's 2 m-tiles ----
             // two accumulators per m-tile (even / odd k-steps) halve the
             // dependent MMA chain; summed before the softmax
@@ -1286,15 +1287,21 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 for (int cb = 0; cb < L::NCHK; ++cb) {
                     if constexpr (KB == 4) {
                         uint32_t h0[4], h1[4];
-                        Conv<DT>::int4(kr[0][cb], h0);
-                        Conv<DT>::int4(kr[1][cb], h1);
+                        if constexpr (FADE_ABLATE == 8) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) { h0[j] = kr[0][cb]; h1[j] = kr[1][cb]; }
+                        } else {
+                            Conv<DT>::int4(kr[0][cb], h0);
+                            Conv<DT>::int4(kr[1][cb], h1);
+                        }
 #pragma unroll
                         for (int u2 = 0; u2 < 2; ++u2) {
                             const int ks = cb * 2 + u2;
-                            const uint32_t a0 = P::mul(h0[2 * u2], ksc[ks][0]);
-                            const uint32_t a1 = P::mul(h1[2 * u2], ksc[ks][0]);
-                            const uint32_t a2 = P::mul(h0[2 * u2 + 1], ksc[ks][1]);
-                            const uint32_t a3 = P::mul(h1[2 * u2 + 1], ksc[ks][1]);
+                            const bool raw = FADE_ABLATE == 8;
+                            const uint32_t a0 = raw ? h0[2 * u2] : P::mul(h0[2 * u2], ksc[ks][0]);
+                            const uint32_t a1 = raw ? h1[2 * u2] : P::mul(h1[2 * u2], ksc[ks][0]);
+                            const uint32_t a2 = raw ? h0[2 * u2 + 1] : P::mul(h0[2 * u2 + 1], ksc[ks][1]);
+                            const uint32_t a3 = raw ? h1[2 * u2 + 1] : P::mul(h1[2 * u2 + 1], ksc[ks][1]);
 #pragma unroll
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
@@ -1348,6 +1355,18 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             if (tw + mt * 16 + gid + ((e >> 1) << 3) >= clen) sacc[mt][nt][e] = -INFINITY;
             }
             uint32_t pb[2][NT][2];
+#if FADE_ABLATE == 7
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    pb[mt][nt][0] = movmatrix_t(P::pack(sacc[mt][nt][0], sacc[mt][nt][1]));
+                    pb[mt][nt][1] = movmatrix_t(P::pack(sacc[mt][nt][2], sacc[mt][nt][3]));
+                }
+            if (false) {
+#else
+            {
+#endif
             bool grow = false;
             float corr[NT][2];
 #pragma unroll
@@ -1395,6 +1414,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     pb[mt][nt][1] = movmatrix_t(P::pack(pv[2], pv[3]));
                 }
             }
+            }   // softmax
             // ---- O^T += V_deq^T . P^T ----
 #pragma unroll
             for (int mt = 0; mt < (FADE_ABLATE == 2 ? 0 : 2); ++mt) {
@@ -1425,14 +1445,21 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 for (int cb = 0; cb < L::NCHV; ++cb) {
                     if constexpr (VB == 4) {
                         uint32_t h0[4], h1[4];
-                        Conv<DT>::int4(vr[0][cb], h0);   // tokens 2t,2t+1
-                        Conv<DT>::int4(vr[1][cb], h1);   // tokens 8+2t, 9+2t
+                        if constexpr (FADE_ABLATE == 9) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) { h0[j] = vr[0][cb]; h1[j] = vr[1][cb]; }
+                        } else {
+                            Conv<DT>::int4(vr[0][cb], h0);   // tokens 2t,2t+1
+                            Conv<DT>::int4(vr[1][cb], h1);   // tokens 8+2t, 9+2t
+                        }
                         // m-tile j: rows (gid: e_{2j} -> h[2j+1]), (gid+8: e_{2j+1} -> h[2j])
 #pragma unroll
                         for (int j = 0; j < 2; ++j) {
                             const int mi = cb * 2 + j;
                             uint32_t a0, a1, a2, a3;
-                            if constexpr (!VGROUP) {
+                            if constexpr (FADE_ABLATE == 9) {
+                                a0 = h0[2 * j + 1]; a1 = h0[2 * j]; a2 = h1[2 * j + 1]; a3 = h1[2 * j];
+                            } else if constexpr (!VGROUP) {
                                 a0 = P::mul(h0[2 * j + 1], vs0);
                                 a1 = P::mul(h0[2 * j], vs0);
                                 a2 = P::mul(h1[2 * j + 1], vs1);
