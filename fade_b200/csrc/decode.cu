@@ -93,7 +93,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 // below any real score, so exp2(score - max) never sees inf - inf.
 constexpr float kMaskedMax = -1e30f;
 constexpr uint32_t kWaitPolls = 1u << 15;   // bounded mbarrier polling ...
-constexpr uint32_t kWaitHintNs = 10000;     // ... of up to 10 us each
+#ifndef FADE_WAIT_HINT_NS
+#define FADE_WAIT_HINT_NS 10000
+#endif
+constexpr uint32_t kWaitHintNs = FADE_WAIT_HINT_NS;   // ... of up to 10 us each
 
 // ---------------------------------------------------------------------------
 // PTX wrappers (mbarrier, TMA, ldmatrix, movmatrix, mma)
@@ -715,7 +718,11 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
 #pragma unroll
                 for (int e = 0; e < 4; ++e) o[nt][mi][e] = 0.f;
         }
+#ifdef FADE_NO_FPATTN
+        for (int64_t t0 = 0; t0 < 0; t0 += 16) {   // profiling: FP tiers skipped
+#else
         for (int64_t t0 = 0; t0 < T_all; t0 += 16) {
+#endif
             // ---- S^T = K . q^T (16 tokens) ----
             float sacc[NT][4];
 #pragma unroll
@@ -951,15 +958,22 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         }
         int z = z_of_unit(p, Z, ub);
         int zb = units_begin(p, z), ze = units_begin(p, z + 1);
-        for (int i = pg; ub + i < ue; i += G) {
+        // per-row values refreshed only when the row changes
+        int64_t zrow0 = seg_row0(p, z), zlen = seg_len(p, z / p.Hkv);
+        int s = pg;            // ring slot of stage i (i % NS), and its phase parity
+        uint32_t ph = 0;
+        for (int i = pg; ub + i < ue; i += G, s += G) {
+            if (s >= NS) { s -= NS; ph ^= 1u; }
             const int u = ub + i;
-            while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
-            const int s = i % NS;
-            const uint32_t ph = (uint32_t)(i / NS) & 1u;
+            if (u >= ze) {
+                while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
+                zrow0 = seg_row0(p, z);
+                zlen = seg_len(p, z / p.Hkv);
+            }
             if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.ws_err)) continue;
             const int64_t tok0 = (int64_t)(u - zb) * kStageTokens;
-            const int64_t row0 = seg_row0(p, z) + tok0;
-            const int64_t len = seg_len(p, z / p.Hkv);
+            const int64_t row0 = zrow0 + tok0;
+            const int64_t len = zlen;
             uint8_t* st = smem + s * L::STAGE_BYTES;
             // Units past this row's length (uniform grid over a capacity bound)
             // carry no tokens: complete the stage without a copy.
