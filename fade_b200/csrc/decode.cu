@@ -87,6 +87,7 @@ __host__ __device__ constexpr int mid_threads(int NT) {
     return (mid_groups(NT) * (kConsumerWarps + 1) + 1) * 32;
 }
 constexpr int kMidMaxStages = 15;
+constexpr int kFpChunk = 80;       // FP-tier tokens the FP warp stages per pass
 constexpr int kSmemPerBlock = 232448;  // 227 KB opt-in shared memory per CTA
 constexpr float kLog2e = 1.4426950408889634f;
 // Initial running maximum of the middle kernel's online softmax: finite and
@@ -205,6 +206,12 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
     uint32_t d;
     asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
     return d;
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -445,7 +452,7 @@ struct MidLayout {
     static constexpr int ML_BYTES = 2 * kConsumerWarps * NT * 8 * 2 * 4;  // per group: per-warp row stats, 2 buffers
     // as many stages as shared memory holds (a multiple of G, so each ring
     // slot always serves the same group)
-    static constexpr int AB_BYTES = 8 * D;   // FP warp: aged + new token, K and V
+    static constexpr int AB_BYTES = 2 * kFpChunk * (D + 8) * 2;   // FP warp: staged K and V rows
     static constexpr int NS_FIT = (kSmemPerBlock - 1024 - 16 - AB_BYTES - 2 * kMidMaxStages * 8 -
                                    G * (OBUF_BYTES + ML_BYTES)) /
                                   (STAGE_BYTES + SC_BYTES);
@@ -575,26 +582,28 @@ __device__ __forceinline__ void load_tiles(uint32_t base, int trow0, int lane, u
 // FP-tier warp of the middle kernel (one per CTA): attention over the FP
 // tiers (sinks, recent window) of the rows z in [c*Z/n, (c+1)*Z/n), written as
 // one un-normalised partial per row for the finisher, while the consumer
-// groups stream the middle.  With the fused age-out it also moves the oldest
-// ring token into the middle (INT4 codes exactly as fade_age_out_int4) and
-// attends the step's tokens: the aged token as its INT4 round trip and the
-// new token, both staged in shared memory; the aged ring slot is masked.
-// Fragments come straight from global memory (16-byte K loads, 8-byte V
-// loads) in the layouts of the consumer path: K channels in ChanMap<4> order
-// (the query fragments use the same order), O^T rows by ChanMap<4>::vdim.
+// groups stream the middle.  The FP tokens of a row are staged into shared
+// memory with 16-byte cp.async in chunks of kFpChunk tokens (one memory round
+// trip per chunk, so the warp's latency stays well below the streaming time),
+// then multiplied with ldmatrix + mma.sync like the consumer path.  With the
+// fused age-out the warp also moves the oldest ring token into the middle
+// (INT4 codes exactly as fade_age_out_int4): its staged row is replaced by
+// the INT4 round trip, the step's new token is staged after the FP tokens,
+// and the new token is written into the freed ring slot.
 // ---------------------------------------------------------------------------
 template <int DT, int D, int NT>
-__device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, uint8_t* abuf) {
+__device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, uint8_t* fsm) {
     using T = typename Elem<DT>::T;
     using P = Pk<DT>;
-    using KMap = ChanMap<4>;
-    using VMap = ChanMap<4>;
-    constexpr int KSTEPS = D / 16, MT = D / 16, NCB = D / 32;
-    constexpr int DPL = D / 32;   // channels per lane in the age-out
+    constexpr int KSTEPS = D / 16, MT = D / 16;
+    constexpr int RS = D + 8;                // padded smem row (elements): conflict-free ldmatrix
+    constexpr int PCS = D / 8;               // 16-byte pieces per row
+    constexpr int DPL = D / 32;              // channels per lane in the age-out
     const int lane = threadIdx.x % 32, gid = lane >> 2, t = lane & 3;
     const int Z = p.B * p.Hkv;
     const int z0 = (int)((int64_t)c * Z / n_cta), z1 = (int)((int64_t)(c + 1) * Z / n_cta);
-    T* ab = reinterpret_cast<T*>(abuf);   // [2 tokens][K, V][D]: aged, new
+    T* ksm = reinterpret_cast<T*>(fsm);
+    T* vsm = ksm + kFpChunk * RS;
     for (int z = z0; z < z1; ++z) {
         const int b = z / p.Hkv, h = z % p.Hkv;
         // ---- FP segments of the row ----
@@ -609,103 +618,37 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
                 T_seg += sl[s];
             }
         }
-        // ---- fused age-out ----
-        int64_t n = 0, ft_aged = -1;
+        // ---- fused age-out bookkeeping ----
+        int64_t n = 0, ft_aged = -1, slot = 0;
         bool room = false;
         if (p.age) {
             n = p.mid_len[b];
             room = n < p.mid_cap;
         }
         if (room) {
-            int64_t slot = (n - p.ring_origin) % p.ring_cap;
+            slot = (n - p.ring_origin) % p.ring_cap;
             if (slot < 0) slot += p.ring_cap;
             ft_aged = slot;
             for (int s = 0; s < p.ring_fp; ++s) ft_aged += sl[s];
-            T* rk = reinterpret_cast<T*>(const_cast<void*>(p.fp[p.ring_fp].k)) + (sr[p.ring_fp] + slot) * D;
-            T* rv = reinterpret_cast<T*>(const_cast<void*>(p.fp[p.ring_fp].v)) + (sr[p.ring_fp] + slot) * D;
-            const T* kn = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
-            const T* vn = reinterpret_cast<const T*>(p.v_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
-            const T* ksc = reinterpret_cast<const T*>(p.k_scale) + (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
-            float kx[DPL], vx[DPL], sc[DPL];
-            T knv[DPL], vnv[DPL];
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) {
-                const int d = lane * DPL + i;
-                kx[i] = Elem<DT>::to_f(rk[d]);
-                vx[i] = Elem<DT>::to_f(rv[d]);
-                sc[i] = Elem<DT>::to_f(ksc[d]);
-                knv[i] = kn[d];
-                vnv[i] = vn[d];
-            }
-            float m = 0.f;
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) m = fmaxf(m, fabsf(vx[i]));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            m = fmaxf(m, Elem<DT>::eps());
-            const float inv = inv_scale<DT>(m, 7.f);
-            const float vsc = Elem<DT>::rnd(__fdiv_rn(m, 7.f));
-            const int64_t mrow = (p.row_base ? p.row_base[z] : (int64_t)b * p.row_sb + (int64_t)h * p.row_sh) + n;
-            if (lane == 0) reinterpret_cast<T*>(const_cast<void*>(p.v_scale))[mrow] = Elem<DT>::from_f(vsc);
-#pragma unroll
-            for (int i = 0; i < DPL; i += 2) {
-                int kq[2], vq[2];
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int d = lane * DPL + i + j;
-                    kq[j] = (sc[i + j] > 0.f) ? quant_code(__fdiv_rn(kx[i + j], sc[i + j]), -8.f, 7.f) : 0;
-                    vq[j] = quant_code(Elem<DT>::rnd(__fmul_rn(vx[i + j], inv)), -8.f, 7.f);
-                    ab[0 * 2 * D + d] = Elem<DT>::from_f((float)kq[j] * sc[i + j]);   // aged K
-                    ab[0 * 2 * D + D + d] = Elem<DT>::from_f((float)vq[j] * vsc);     // aged V
-                    ab[1 * 2 * D + d] = knv[i + j];                                   // new K
-                    ab[1 * 2 * D + D + d] = vnv[i + j];                               // new V
-                }
-                const int pp = (lane * DPL + i) / 2;
-                p.age_k[mrow * (D / 2) + pp] = (uint8_t)(((kq[0] & 15) << 4) | (kq[1] & 15));
-                p.age_v[mrow * (D / 2) + pp] = (uint8_t)(((vq[0] & 15) << 4) | (vq[1] & 15));
-            }
-            // the new token takes the freed ring slot (each lane wrote back
-            // only channels it read itself)
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) {
-                const int d = lane * DPL + i;
-                rk[d] = knv[i];
-                rv[d] = vnv[i];
-            }
         }
         if (p.age && lane == 0) p.ws_age[z] = (int)(room ? n + 1 : n);
-        __syncwarp();
-        const int64_t T_all = T_seg + (room ? 2 : 0);
-        auto row_ptr = [&](int64_t ft, bool vrow) -> const T* {
-            if (ft >= T_all) ft = 0;   // padding rows: any finite row (masked)
-            if (ft >= T_seg) return ab + (ft - T_seg) * 2 * D + (vrow ? D : 0);
-            int s = 0;
-            while (s < p.n_fp - 1 && ft >= sl[s]) { ft -= sl[s]; ++s; }
-            return reinterpret_cast<const T*>(vrow ? p.fp[s].v : p.fp[s].k) + (sr[s] + ft) * D;
-        };
-        // ---- query fragments (exact model-dtype q), ChanMap<4> order ----
+        const int64_t T_all = T_seg + (room ? 1 : 0);   // + the step's new token
+        const T* kn = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
+        const T* vn = reinterpret_cast<const T*>(p.v_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
+        // ---- query fragments (exact model-dtype q), natural channel order ----
         uint32_t qf[NT][KSTEPS][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int r = nt * 8 + gid;
             const bool rv = r < p.rows;
             const int j = rv ? r / p.n_q : 0, sq = rv ? r % p.n_q : 0;
-            const uint16_t* qp = reinterpret_cast<const uint16_t*>(p.qo) + (int64_t)b * p.qo_sb +
-                                 (int64_t)(h * p.g + j) * p.qo_sh + (int64_t)sq * p.qo_ss;
+            const uint32_t* qp = reinterpret_cast<const uint32_t*>(
+                reinterpret_cast<const T*>(p.qo) + (int64_t)b * p.qo_sb + (int64_t)(h * p.g + j) * p.qo_sh +
+                (int64_t)sq * p.qo_ss);
 #pragma unroll
-            for (int cb = 0; cb < NCB; ++cb) {
-                uint16_t e[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) e[i] = rv ? qp[32 * cb + 8 * t + i] : (uint16_t)0;
-#pragma unroll
-                for (int u = 0; u < 2; ++u)
-#pragma unroll
-                    for (int hs = 0; hs < 2; ++hs) {
-                        const int ks = cb * 2 + u;
-                        const int i0 = KMap::kdim(ks, 2 * hs, t) - 32 * cb - 8 * t;
-                        const int i1 = KMap::kdim(ks, 2 * hs + 1, t) - 32 * cb - 8 * t;
-                        qf[nt][ks][hs] = (uint32_t)e[i0] | ((uint32_t)e[i1] << 16);
-                    }
+            for (int ks = 0; ks < KSTEPS; ++ks) {
+                qf[nt][ks][0] = rv ? qp[ks * 8 + t] : 0u;       // channels 16ks + 2t, +1
+                qf[nt][ks][1] = rv ? qp[ks * 8 + 4 + t] : 0u;   // channels 16ks + 2t + 8, +9
             }
         }
         float m_run[NT][2], l_run[NT][2], o[NT][MT][4];
@@ -719,135 +662,171 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
                 for (int e = 0; e < 4; ++e) o[nt][mi][e] = 0.f;
         }
 #ifdef FADE_NO_FPATTN
-        for (int64_t t0 = 0; t0 < 0; t0 += 16) {   // profiling: FP tiers skipped
+        for (int64_t c0 = 0; c0 < 0; c0 += kFpChunk) {   // profiling: FP tiers skipped
 #else
-        for (int64_t t0 = 0; t0 < T_all; t0 += 16) {
+        for (int64_t c0 = 0; c0 < T_all; c0 += kFpChunk) {
 #endif
-            // ---- S^T = K . q^T (16 tokens) ----
-            float sacc[NT][4];
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) sacc[nt][e] = 0.f;
-            {
-                const T* k0 = row_ptr(t0 + gid, false);
-                const T* k1 = row_ptr(t0 + gid + 8, false);
-                uint4 kr0[NCB], kr1[NCB];
-#pragma unroll
-                for (int cb = 0; cb < NCB; ++cb) {
-                    kr0[cb] = *reinterpret_cast<const uint4*>(k0 + 32 * cb + 8 * t);
-                    kr1[cb] = *reinterpret_cast<const uint4*>(k1 + 32 * cb + 8 * t);
+            const int nc = (int)((T_all - c0) < kFpChunk ? (T_all - c0) : kFpChunk);
+            const int nc16 = (nc + 15) & ~15;
+            __syncwarp();   // the previous chunk's rows are no longer read
+            // ---- stage K and V rows (padding rows up to a multiple of 16: row 0) ----
+            for (int i = lane; i < nc16 * PCS; i += 32) {
+                const int tk = i / PCS, pc = i % PCS;
+                int64_t ft = c0 + (tk < nc ? tk : 0);
+                const T* ks;
+                const T* vs;
+                if (ft >= T_seg) {
+                    ks = kn + pc * 8;
+                    vs = vn + pc * 8;
+                } else {
+                    int s = 0;
+                    while (s < p.n_fp - 1 && ft >= sl[s]) { ft -= sl[s]; ++s; }
+                    const int64_t off = (sr[s] + ft) * D + pc * 8;
+                    ks = reinterpret_cast<const T*>(p.fp[s].k) + off;
+                    vs = reinterpret_cast<const T*>(p.fp[s].v) + off;
                 }
+                cp_async16(smem_u32(ksm + tk * RS + pc * 8), ks);
+                cp_async16(smem_u32(vsm + tk * RS + pc * 8), vs);
+            }
+            cp_async_wait_all();
+            __syncwarp();
+            if (ft_aged >= c0 && ft_aged < c0 + nc) {
+                // ---- the aged token: INT4 codes into the middle, its staged row
+                //      becomes rnd(code * scale); the new token takes its ring slot ----
+                T* kr = ksm + (ft_aged - c0) * RS;
+                T* vr = vsm + (ft_aged - c0) * RS;
+                const T* ksc = reinterpret_cast<const T*>(p.k_scale) + (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
+                float kx[DPL], vx[DPL], sc[DPL];
 #pragma unroll
-                for (int cb = 0; cb < NCB; ++cb) {
-                    // channels 8t+0..7 of the chunk as words w0=(0,1) w1=(2,3) w2=(4,5) w3=(6,7)
-                    const uint32_t a_w[2][4] = {{kr0[cb].x, kr0[cb].y, kr0[cb].z, kr0[cb].w},
-                                                {kr1[cb].x, kr1[cb].y, kr1[cb].z, kr1[cb].w}};
+                for (int i = 0; i < DPL; ++i) {
+                    const int d = lane * DPL + i;
+                    kx[i] = Elem<DT>::to_f(kr[d]);
+                    vx[i] = Elem<DT>::to_f(vr[d]);
+                    sc[i] = Elem<DT>::to_f(ksc[d]);
+                }
+                float m = 0.f;
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        // u=0: slots (1,5),(0,4); u=1: (3,7),(2,6)  (see ChanMap<4>::kdim)
-                        const uint32_t hi_sel = 0x7632u, lo_sel = 0x5410u;
-                        uint32_t a[4];
+                for (int i = 0; i < DPL; ++i) m = fmaxf(m, fabsf(vx[i]));
 #pragma unroll
-                        for (int rr = 0; rr < 2; ++rr) {
-                            const uint32_t wl = a_w[rr][u], wh = a_w[rr][2 + u];
-                            a[rr] = __byte_perm(wl, wh, hi_sel);       // (ch 2u+1, ch 2u+5)
-                            a[2 + rr] = __byte_perm(wl, wh, lo_sel);   // (ch 2u,   ch 2u+4)
-                        }
+                for (int o2 = 16; o2 > 0; o2 >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o2));
+                m = fmaxf(m, Elem<DT>::eps());
+                const float inv = inv_scale<DT>(m, 7.f);
+                const float vsc = Elem<DT>::rnd(__fdiv_rn(m, 7.f));
+                const int64_t mrow = (p.row_base ? p.row_base[z] : (int64_t)b * p.row_sb + (int64_t)h * p.row_sh) + n;
+                if (lane == 0) reinterpret_cast<T*>(const_cast<void*>(p.v_scale))[mrow] = Elem<DT>::from_f(vsc);
 #pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
-                            P::mma(sacc[nt], a[0], a[1], a[2], a[3], qf[nt][cb * 2 + u][0], qf[nt][cb * 2 + u][1]);
+                for (int i = 0; i < DPL; i += 2) {
+                    int kq[2], vq[2];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int d = lane * DPL + i + j;
+                        kq[j] = (sc[i + j] > 0.f) ? quant_code(__fdiv_rn(kx[i + j], sc[i + j]), -8.f, 7.f) : 0;
+                        vq[j] = quant_code(Elem<DT>::rnd(__fmul_rn(vx[i + j], inv)), -8.f, 7.f);
+                        kr[d] = Elem<DT>::from_f((float)kq[j] * sc[i + j]);
+                        vr[d] = Elem<DT>::from_f((float)vq[j] * vsc);
                     }
+                    const int pp = (lane * DPL + i) / 2;
+                    p.age_k[mrow * (D / 2) + pp] = (uint8_t)(((kq[0] & 15) << 4) | (kq[1] & 15));
+                    p.age_v[mrow * (D / 2) + pp] = (uint8_t)(((vq[0] & 15) << 4) | (vq[1] & 15));
                 }
+                // ring slot <- new token (this lane's channels; the old row was staged above)
+                T* rk = reinterpret_cast<T*>(const_cast<void*>(p.fp[p.ring_fp].k)) + (sr[p.ring_fp] + slot) * D;
+                T* rv = reinterpret_cast<T*>(const_cast<void*>(p.fp[p.ring_fp].v)) + (sr[p.ring_fp] + slot) * D;
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) {
+                    const int d = lane * DPL + i;
+                    rk[d] = kn[d];
+                    rv[d] = vn[d];
+                }
+                __syncwarp();
             }
-            // ---- online softmax (log2 domain); masked: padding, aged slot ----
-            bool grow = false;
-            float corr[NT][2];
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int64_t ft = t0 + gid + ((e >> 1) << 3);
-                    sacc[nt][e] = (ft >= T_all || ft == ft_aged) ? -INFINITY : sacc[nt][e] * p.qk_scale;
-                }
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    float mx = fmaxf(sacc[nt][e], sacc[nt][e + 2]);
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    const float mnew = fmaxf(m_run[nt][e], mx);
-                    grow |= mnew > m_run[nt][e];
-                    corr[nt][e] = ex2(m_run[nt][e] - mnew);
-                    m_run[nt][e] = mnew;
-                }
-            }
-            if (__any_sync(0xffffffffu, grow)) {
+            // ---- attention over the chunk, 16 tokens per m-tile ----
+            const uint32_t kbase = smem_u32(ksm), vbase = smem_u32(vsm);
+            const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8, lcol = (lane >> 4) * 8;       // K (A) tiles
+            const int vrow = (lane & 7) + (lane >> 4) * 8, vcol = ((lane >> 3) & 1) * 8;       // V^T (A) tiles
+            for (int t0 = 0; t0 < nc16; t0 += 16) {
+                float sacc[NT][4];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        l_run[nt][e] *= corr[nt][e];
+                    for (int e = 0; e < 4; ++e) sacc[nt][e] = 0.f;
 #pragma unroll
-                        for (int mi = 0; mi < MT; ++mi) {
-                            o[nt][mi][e] *= corr[nt][e];
-                            o[nt][mi][e + 2] *= corr[nt][e];
-                        }
-                    }
-            }
-            // P as hi + lo model-dtype parts (two MMAs): the FP tiers carry
-            // the sharpest scores, so P keeps ~16 significant bits here
-            uint32_t pb[NT][2], pl[NT][2];
+                for (int ks = 0; ks < KSTEPS; ++ks) {
+                    uint32_t a[4];
+                    ldsm_x4(kbase + (uint32_t)(((t0 + lrow) * RS + ks * 16 + lcol) * 2), a);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                float pv[4], lo[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    pv[e] = ex2(sacc[nt][e] - m_run[nt][e & 1]);
-                    l_run[nt][e & 1] += pv[e];
+                    for (int nt = 0; nt < NT; ++nt) P::mma(sacc[nt], a[0], a[1], a[2], a[3], qf[nt][ks][0], qf[nt][ks][1]);
                 }
-                const uint32_t h01 = P::pack(pv[0], pv[1]), h23 = P::pack(pv[2], pv[3]);
-                lo[0] = pv[0] - P::unpack_lo(h01);
-                lo[1] = pv[1] - P::unpack_lo(h01 >> 16);
-                lo[2] = pv[2] - P::unpack_lo(h23);
-                lo[3] = pv[3] - P::unpack_lo(h23 >> 16);
-                pb[nt][0] = movmatrix_t(h01);
-                pb[nt][1] = movmatrix_t(h23);
-                pl[nt][0] = movmatrix_t(P::pack(lo[0], lo[1]));
-                pl[nt][1] = movmatrix_t(P::pack(lo[2], lo[3]));
-            }
-            // ---- O^T += V^T . P^T: tokens 2t, 2t+1, 2t+8, 2t+9 x channels
-            //      32cb + 4gid .. +3 (8-byte loads) ----
-            {
-                const T* v0 = row_ptr(t0 + 2 * t, true);
-                const T* v1 = row_ptr(t0 + 2 * t + 1, true);
-                const T* v2 = row_ptr(t0 + 2 * t + 8, true);
-                const T* v3 = row_ptr(t0 + 2 * t + 9, true);
+                // ---- online softmax (log2 domain); padding rows masked ----
+                bool grow = false;
+                float corr[NT][2];
 #pragma unroll
-                for (int cb = 0; cb < NCB; ++cb) {
-                    const uint2 r0 = *reinterpret_cast<const uint2*>(v0 + 32 * cb + 4 * gid);
-                    const uint2 r1 = *reinterpret_cast<const uint2*>(v1 + 32 * cb + 4 * gid);
-                    const uint2 r2 = *reinterpret_cast<const uint2*>(v2 + 32 * cb + 4 * gid);
-                    const uint2 r3 = *reinterpret_cast<const uint2*>(v3 + 32 * cb + 4 * gid);
+                for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        // channel pair (c, c+1) = 32cb + 4gid + 2j: words .x (j=0) / .y (j=1)
-                        const uint32_t w0 = j ? r0.y : r0.x, w1 = j ? r1.y : r1.x;
-                        const uint32_t w2 = j ? r2.y : r2.x, w3 = j ? r3.y : r3.x;
-                        const uint32_t a0 = __byte_perm(w0, w1, 0x5410u);   // (tok 2t, 2t+1) @ c
-                        const uint32_t a1 = __byte_perm(w0, w1, 0x7632u);   // @ c+1
-                        const uint32_t a2 = __byte_perm(w2, w3, 0x5410u);   // (tok 2t+8, 2t+9) @ c
-                        const uint32_t a3 = __byte_perm(w2, w3, 0x7632u);
+                    for (int e = 0; e < 4; ++e) {
+                        const int tk = t0 + gid + ((e >> 1) << 3);
+                        sacc[nt][e] = (tk >= nc) ? -INFINITY : sacc[nt][e] * p.qk_scale;
+                    }
 #pragma unroll
-                        for (int nt = 0; nt < NT; ++nt) {
-                            P::mma(o[nt][cb * 2 + j], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
-                            P::mma(o[nt][cb * 2 + j], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+                    for (int e = 0; e < 2; ++e) {
+                        float mx = fmaxf(sacc[nt][e], sacc[nt][e + 2]);
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                        const float mnew = fmaxf(m_run[nt][e], mx);
+                        grow |= mnew > m_run[nt][e];
+                        corr[nt][e] = ex2(m_run[nt][e] - mnew);
+                        m_run[nt][e] = mnew;
+                    }
+                }
+                if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            l_run[nt][e] *= corr[nt][e];
+#pragma unroll
+                            for (int mi = 0; mi < MT; ++mi) {
+                                o[nt][mi][e] *= corr[nt][e];
+                                o[nt][mi][e + 2] *= corr[nt][e];
+                            }
                         }
+                }
+                // P as hi + lo model-dtype parts (two MMAs): the FP tiers carry
+                // the sharpest scores, so P keeps ~16 significant bits here
+                uint32_t pb[NT][2], pl[NT][2];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    float pv[4], lo[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        pv[e] = ex2(sacc[nt][e] - m_run[nt][e & 1]);
+                        l_run[nt][e & 1] += pv[e];
+                    }
+                    const uint32_t h01 = P::pack(pv[0], pv[1]), h23 = P::pack(pv[2], pv[3]);
+                    lo[0] = pv[0] - P::unpack_lo(h01);
+                    lo[1] = pv[1] - P::unpack_lo(h01 >> 16);
+                    lo[2] = pv[2] - P::unpack_lo(h23);
+                    lo[3] = pv[3] - P::unpack_lo(h23 >> 16);
+                    pb[nt][0] = movmatrix_t(h01);
+                    pb[nt][1] = movmatrix_t(h23);
+                    pl[nt][0] = movmatrix_t(P::pack(lo[0], lo[1]));
+                    pl[nt][1] = movmatrix_t(P::pack(lo[2], lo[3]));
+                }
+                // ---- O^T += V^T . P^T (V^T fragments by transposing ldmatrix) ----
+#pragma unroll
+                for (int mi = 0; mi < MT; ++mi) {
+                    uint32_t a[4];
+                    ldsm_x4_t(vbase + (uint32_t)(((t0 + vrow) * RS + mi * 16 + vcol) * 2), a);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        P::mma(o[nt][mi], a[0], a[1], a[2], a[3], pb[nt][0], pb[nt][1]);
+                        P::mma(o[nt][mi], a[0], a[1], a[2], a[3], pl[nt][0], pl[nt][1]);
                     }
                 }
             }
         }
-        // ---- partial of row z ----
+        // ---- partial of row z: O^T rows are channels mi*16 + gid (+8) ----
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -861,10 +840,12 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
                     if (gid == 0)
                         *reinterpret_cast<float2*>(p.ws_fpml + ((int64_t)z * p.rows + r) * 2) =
                             make_float2(m_run[nt][e], l);
+                    float* dst = p.ws_fpo + ((int64_t)z * p.rows + r) * D;
 #pragma unroll
-                    for (int mi = 0; mi < MT; ++mi)
-                        *reinterpret_cast<float2*>(p.ws_fpo + ((int64_t)z * p.rows + r) * D + VMap::vdim(mi, 0, gid)) =
-                            make_float2(o[nt][mi][e], o[nt][mi][e + 2]);
+                    for (int mi = 0; mi < MT; ++mi) {
+                        dst[mi * 16 + gid] = o[nt][mi][e];
+                        dst[mi * 16 + gid + 8] = o[nt][mi][e + 2];
+                    }
                 }
             }
         __syncwarp();
@@ -1613,12 +1594,6 @@ struct FinLayout {
     static_assert(ROWS * D * 4 <= V_OFF, "rotation scratch reuses the K region");
 };
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
 
 template <int DT, int D, int NT>
 __global__ void __launch_bounds__(kFinThreads)
@@ -2335,6 +2310,9 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
             mp.ring_cap = a->ring_cap;
             mp.ring_origin = a->ring_origin;
             mp.k_new = a->k_new; mp.v_new = a->v_new; mp.new_sb = a->new_sb; mp.new_sh = a->new_sh;
+            // the FP warp stages the new token with 16-byte copies
+            if (!aligned16(a->k_new) || !aligned16(a->v_new) || (a->new_sb * 2) % 16 || (a->new_sh * 2) % 16)
+                return FADE_ERR_ALIGN;
             mp.mid_cap = sg.max_len;
             mp.mid_len = sg.lens;
             mp.age_k = reinterpret_cast<uint8_t*>(const_cast<void*>(sg.k));
