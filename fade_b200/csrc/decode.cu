@@ -87,7 +87,7 @@ __host__ __device__ constexpr int mid_threads(int NT) {
     return (mid_groups(NT) * (kConsumerWarps + 1) + 1) * 32;
 }
 constexpr int kMidMaxStages = 15;
-constexpr int kFpChunk = 80;       // FP-tier tokens the FP warp stages per pass
+constexpr int kFpChunk = 48;       // FP-tier tokens the FP warp stages per pass
 constexpr int kSmemPerBlock = 232448;  // 227 KB opt-in shared memory per CTA
 constexpr float kLog2e = 1.4426950408889634f;
 // Initial running maximum of the middle kernel's online softmax: finite and
@@ -121,6 +121,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Non-blocking test of a phase.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(bar), "r"(parity)
@@ -448,19 +459,18 @@ struct MidLayout {
     static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
     static_assert(K_BYTES % 1024 == 0 && V_BYTES % 1024 == 0, "stage regions must stay 1 KB aligned");
     static constexpr int G = mid_groups(NT);
-    static constexpr int OBUF_BYTES = 2 * NT * 8 * D * 4;                 // per group: 2 half-sums of a partial
     static constexpr int ML_BYTES = 2 * kConsumerWarps * NT * 8 * 2 * 4;  // per group: per-warp row stats, 2 buffers
     // as many stages as shared memory holds (a multiple of G, so each ring
     // slot always serves the same group)
     static constexpr int AB_BYTES = 2 * kFpChunk * (D + 8) * 2;   // FP warp: staged K and V rows
     static constexpr int NS_FIT = (kSmemPerBlock - 1024 - 16 - AB_BYTES - 2 * kMidMaxStages * 8 -
-                                   G * (OBUF_BYTES + ML_BYTES)) /
+                                   G * ML_BYTES) /
                                   (STAGE_BYTES + SC_BYTES);
     static constexpr int NS = ((NS_FIT < kMidMaxStages ? NS_FIT : kMidMaxStages) / G) * G;
     static_assert(NS >= 2 * G, "shared memory too small for the stage ring");
     static constexpr int SC_BASE = NS * STAGE_BYTES;
     static constexpr int RING_BYTES = SC_BASE + NS * SC_BYTES;
-    static constexpr int BAR_OFF = RING_BYTES + G * (OBUF_BYTES + ML_BYTES);
+    static constexpr int BAR_OFF = RING_BYTES + G * ML_BYTES;
     static constexpr int FLAG_OFF = BAR_OFF + 2 * NS * 8;
     static constexpr int AB_OFF = FLAG_OFF + 16;
     static constexpr int SMEM_BYTES = AB_OFF + AB_BYTES + 1024;  // +1024 for alignment
@@ -1027,8 +1037,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     const int bar_id = 1 + grp;              // the group's named barrier
     const TileOffs<L::NCHK> koffs(gw * 32, lane);
     const TileOffs<L::NCHV> voffs(gw * 32, lane);
-    float* obuf = reinterpret_cast<float*>(smem + L::RING_BYTES + grp * (L::OBUF_BYTES + L::ML_BYTES));
-    float* mlbuf = obuf + L::OBUF_BYTES / 4;
+    float* mlbuf = reinterpret_cast<float*>(smem + L::RING_BYTES + grp * L::ML_BYTES);
     uint32_t qf[NQ][NT][KSTEPS][2];  // B fragments (exact model-dtype query)
     uint32_t ksc[KSTEPS][2];         // K scale pairs matching the A pairs
     float m_run[NT][2], l_run[NT][2];
@@ -1145,7 +1154,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // order ((w0 + w2) + (w1 + w3)): repeated calls give identical bits.
     constexpr int MLW = NT * 8;   // rows per gw in the statistics buffer
     int n_flush = 0;
-    auto flush = [&](int z) {
+    auto flush = [&](int z, float* scratch) {
         // 1) complete the per-thread row sums over the 8 token lanes
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -1188,11 +1197,16 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     o[nt][mi][e + 2] *= f;
                 }
             }
-        // 3) half-sums: warps 0/1 store into obuf halves 0/1, warps 2/3 add
-        //    theirs (channel pairs d, d+1 are adjacent: float2 accesses)
-        float* half = obuf + (gw & 1) * (NT * 8 * D);
-        for (int pass = 0; pass < 2; ++pass) {
-            if ((gw >> 1) == pass) {
+        // 3) combine the 4 warps in the scratch buffer (the group's stage that
+        //    was just consumed): FR regions of one warp's [rows][D] each; warps
+        //    0..FR-1 store, the others add in turn, always in the same order
+        //    (deterministic).  Channel pairs d, d+1 are adjacent: float2 stores.
+        constexpr int WB = NT * 8 * D * 4;                                  // one warp's partial
+        constexpr int FR = (L::STAGE_BYTES / WB) >= 4 ? 4 : ((L::STAGE_BYTES / WB) >= 2 ? 2 : 1);
+        static_assert(L::STAGE_BYTES >= WB, "stage buffer too small for a partial");
+        float* region = scratch + (gw % FR) * (NT * 8 * D);
+        for (int pass = 0; pass < kConsumerWarps / FR; ++pass) {
+            if (gw / FR == pass) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1201,12 +1215,12 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         if (r >= p.rows) continue;
 #pragma unroll
                         for (int mi = 0; mi < MT; ++mi) {
-                            float2* dst = reinterpret_cast<float2*>(half + r * D + VMap::vdim(mi, 0, gid));
+                            float2* dst = reinterpret_cast<float2*>(region + r * D + VMap::vdim(mi, 0, gid));
                             float2 v = make_float2(o[nt][mi][e], o[nt][mi][e + 2]);
-                            if (pass == 1) {
-                                const float2 a = *dst;
-                                v.x += a.x;
-                                v.y += a.y;
+                            if (pass > 0) {
+                                const float2 a2 = *dst;
+                                v.x += a2.x;
+                                v.y += a2.y;
                             }
                             *dst = v;
                         }
@@ -1218,11 +1232,14 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         //    group processed (unique per group and row)
         const int slot = z_first;
         float4* go = reinterpret_cast<float4*>(p.ws_o + (int64_t)slot * p.rows * D);
-        const float4* h0 = reinterpret_cast<const float4*>(obuf);
-        const float4* h1 = reinterpret_cast<const float4*>(obuf + NT * 8 * D);
         for (int i = ctid; i < p.rows * D / 4; i += kConsumerWarps * 32) {
-            const float4 a = h0[i], c = h1[i];
-            go[i] = make_float4(a.x + c.x, a.y + c.y, a.z + c.z, a.w + c.w);
+            float4 acc = reinterpret_cast<const float4*>(scratch)[i];
+#pragma unroll
+            for (int rg = 1; rg < FR; ++rg) {
+                const float4 x = reinterpret_cast<const float4*>(scratch + rg * (NT * 8 * D))[i];
+                acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+            }
+            go[i] = acc;
         }
         if (ctid < p.rows) {
             const int r = ctid;
@@ -1247,8 +1264,6 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         if (z != cur_z) {
             if (FADE_ABLATE != 6) {
                 FADE_TR(2 + 3 * (cur_z >= 0 ? 1 : 0));
-                if (cur_z >= 0) flush(cur_z);
-                FADE_TR(3 + 3 * (cur_z >= 0 ? 1 : 0));
                 setup_z(z);
                 FADE_TR(4 + 3 * (cur_z >= 0 ? 1 : 0));
             }
@@ -1269,13 +1284,13 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             // ---- S^T = K_deq . q^T for the gw's 2 m-tiles ----
             // two accumulators per m-tile (even / odd k-steps) halve the
             // dependent MMA chain; summed before the softmax
-            float sacc[2][NT][4], sacc2[2][NT][4];
+            float sacc[2][NT][4];
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = sacc2[mt][nt][e] = 0.f;
+                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = 0.f;
                 uint32_t kr[2][L::NCHK];
                 load_tiles_at<L::NCHK, false>(kbase, koffs, mt, kr);
 #pragma unroll
@@ -1301,7 +1316,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
                                 for (int nt = 0; nt < NT; ++nt)
-                                    P::mma((ks & 1) ? sacc2[mt][nt] : sacc[mt][nt], a0, a1, a2, a3,
+                                    P::mma(sacc[mt][nt], a0, a1, a2, a3,
                                            qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     } else {
@@ -1319,27 +1334,18 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
                                 for (int nt = 0; nt < NT; ++nt)
-                                    P::mma((ks & 1) ? sacc2[mt][nt] : sacc[mt][nt], a0, a1, a2, a3,
+                                    P::mma(sacc[mt][nt], a0, a1, a2, a3,
                                            qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     }
                 }
             }
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] += sacc2[mt][nt][e];
             // ---- online softmax over the 32 tokens (log2 domain) ----
-            // Running maxima start at kMaskedMax (finite), so masked scores
-            // (-inf) give exp2 = 0 and no difference of infinities arises.
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] *= p.qk_scale;
+            // Scores stay unscaled; the running maxima are in scaled units
+            // (qk_scale > 0 keeps the order) and exp2(s * qk_scale - m) is one
+            // FMA.  Running maxima start at kMaskedMax (finite), so masked
+            // scores (-inf) give exp2 = 0 and no difference of infinities arises.
+            const float qks = p.qk_scale;
             if (tw + 32 > clen) {   // gw-uniform: only the row's last tile is partial
 #pragma unroll
                 for (int mt = 0; mt < 2; ++mt)
@@ -1373,7 +1379,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    const float mnew = fmaxf(m_run[nt][e], mx);
+                    const float mnew = fmaxf(m_run[nt][e], mx * qks);
                     grow |= mnew > m_run[nt][e];
                     corr[nt][e] = ex2(m_run[nt][e] - mnew);
                     m_run[nt][e] = mnew;
@@ -1401,7 +1407,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     float pv[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float pe = ex2(sacc[mt][nt][e] - m_run[nt][e & 1]);
+                        const float pe = ex2(fmaf(sacc[mt][nt][e], qks, -m_run[nt][e & 1]));
                         l_run[nt][e & 1] += pe;
                         pv[e] = pe;
                     }
@@ -1503,13 +1509,22 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 }
             }
         }
+        // The group's last stage of this row: combine and store the row's
+        // partial in this stage's buffer before releasing it.
+        if (FADE_ABLATE != 6 && (ub + i + G >= ue || ub + i + G >= ze)) {
+            FADE_TR(5);
+            flush(cur_z, reinterpret_cast<float*>(smem + s * L::STAGE_BYTES));
+            // the buffer was written through the generic proxy; the next TMA
+            // load into it is an async-proxy write
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            FADE_TR(6);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(s));
         s += G;
         if (s >= NS) { s -= NS; ph ^= 1u; }
     }
     FADE_TR(36);
-    if (cur_z >= 0 && FADE_ABLATE != 6) flush(cur_z);
     FADE_TR(37);
 }
 
