@@ -41,10 +41,13 @@ def parse():
     ap.add_argument("--impl", choices=("fade", "reference"), default="fade")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--dtype", choices=("bf16", "f16"), default="bf16",
+                    help="model dtype (the benchmark configuration is bf16)")
     ap.add_argument("--layers", type=int, default=CFG["layers"],
                     help="layers per step (profiling captures use 1; the benchmark is 32)")
     args = ap.parse_args()
     CFG["layers"] = args.layers
+    CFG["dtype"] = args.dtype
     return args
 
 
@@ -187,6 +190,12 @@ def config_block(n):
 # --------------------------------------------------------------------------
 # fade arm (GPU)
 # --------------------------------------------------------------------------
+def _torch_dtype():
+    import torch
+
+    return {"bf16": torch.bfloat16, "f16": torch.float16}[CFG["dtype"]]
+
+
 def build_decoder(dev, total_steps, shard_start: int = 0):
     import torch
 
@@ -194,7 +203,7 @@ def build_decoder(dev, total_steps, shard_start: int = 0):
 
     n_mid = CFG["context"] - CFG["n_sink"] - CFG["recent"]
     dec = TieredDecoder(CFG["layers"], CFG["batch"], CFG["n_q_heads"], CFG["n_kv_heads"], CFG["head_dim"],
-                        dtype=torch.bfloat16, n_sink=CFG["n_sink"], recent_window=CFG["recent"],
+                        dtype=_torch_dtype(), n_sink=CFG["n_sink"], recent_window=CFG["recent"],
                         mid_capacity=n_mid + total_steps + 8, device=dev)
     gen = torch.Generator(device=dev)
     B, H, S, D = CFG["batch"], CFG["n_kv_heads"], CFG["context"], CFG["head_dim"]
@@ -206,7 +215,7 @@ def build_decoder(dev, total_steps, shard_start: int = 0):
             ch = torch.randperm(D, device=dev, generator=gen)[:4]
             k[:, h, :, ch] *= 8.0
             v[:, h, :, ch] *= 8.0
-        dec.load_prompt(layer, k.to(torch.bfloat16), v.to(torch.bfloat16))
+        dec.load_prompt(layer, k.to(_torch_dtype()), v.to(_torch_dtype()))
         del k, v
     torch.cuda.synchronize(dev)
     return dec, n_mid
@@ -229,9 +238,9 @@ def run_fade(args, ws, rank, local):
     dec, n_mid0 = build_decoder(dev, total, start)
     L = CFG["layers"]
     gen = torch.Generator(device=dev).manual_seed(7 + rank)
-    q = torch.randn(dec.q.shape, device=dev, generator=gen).to(torch.bfloat16)
-    kn = torch.randn(dec.k_new.shape, device=dev, generator=gen).to(torch.bfloat16)
-    vn = torch.randn(dec.v_new.shape, device=dev, generator=gen).to(torch.bfloat16)
+    q = torch.randn(dec.q.shape, device=dev, generator=gen).to(_torch_dtype())
+    kn = torch.randn(dec.k_new.shape, device=dev, generator=gen).to(_torch_dtype())
+    vn = torch.randn(dec.v_new.shape, device=dev, generator=gen).to(_torch_dtype())
     dec.step(q, kn, vn)                      # eager step: builds plans, validates
     torch.cuda.synchronize(dev)
     dec.capture()
@@ -345,7 +354,7 @@ def run_fade(args, ws, rank, local):
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": K, "warmup": W,
         "ms_per_step": round(step_ms, 4), "us_per_step": round(step_ms * 1e3, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4 codes -> bf16 (bf16 MMA, f32 accumulate)", "data": "synthetic", "config": config_block(ws),
+        "dtype": f"int4 codes -> {CFG['dtype']} ({CFG['dtype']} MMA, f32 accumulate)", "data": "synthetic", "config": config_block(ws),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "fade_decode_attn_age_out per layer (middle_kernel + finish_kernel)",

@@ -50,7 +50,8 @@ namespace fade {
 // 1 = consumers only cycle the pipeline, 2 = QK^T only, 3 = no scale multiply,
 // 4 = as 1 without the L2 cache hint, 5 = as 1 without the scale copy,
 // 6 = as 1 without per-row setup / flush / merge, 7 = no softmax (P = S),
-// 8 = no K dequantisation (raw code words into the MMA), 9 = no V dequantisation.
+// 8 = no K dequantisation (raw code words into the MMA), 9 = no V dequantisation,
+// 10 = no loads at all (consumers compute on stale stage buffers).
 #ifndef FADE_ABLATE
 #define FADE_ABLATE 0
 #endif
@@ -81,7 +82,10 @@ constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
 // head; 1 above, where the wider state needs the registers) share one
 // producer warp and one ring of stages; group g
 // consumes stages g, g+G, g+2G, ...
-__host__ __device__ constexpr int mid_groups(int NT) { return NT == 1 ? 3 : 1; }
+#ifndef FADE_MID_GROUPS
+#define FADE_MID_GROUPS 3
+#endif
+__host__ __device__ constexpr int mid_groups(int NT) { return NT == 1 ? FADE_MID_GROUPS : 1; }
 // + one producer warp per group + the FP-tier warp
 __host__ __device__ constexpr int mid_threads(int NT) {
     return (mid_groups(NT) * (kConsumerWarps + 1) + 1) * 32;
@@ -970,7 +974,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             // carry no tokens: complete the stage without a copy.
             uint8_t* scs = smem + L::SC_BASE + s * L::SC_BYTES;
             if (i < 40) FADE_TRP(40 + i);
-            if (lane == 0 && tok0 < len) {
+            if (lane == 0 && tok0 < len && FADE_ABLATE != 10) {   // 10: compute on stale stages, no loads
                 const uint32_t sc_bytes = (p.scale_tma && FADE_ABLATE != 5) ? (uint32_t)L::sc_box_bytes(p.group) : 0u;
                 mbar_expect_tx(full_bar(s), (uint32_t)(L::K_BYTES + L::V_BYTES) + sc_bytes);
                 // maps address 128-byte rows: token row0 starts at row0*RB/128
