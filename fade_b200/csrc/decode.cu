@@ -82,6 +82,12 @@ constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
 // head; 1 above, where the wider state needs the registers) share one
 // producer warp and one ring of stages; group g
 // consumes stages g, g+G, g+2G, ...
+#ifndef FADE_VPRE
+#define FADE_VPRE 0        // 1: load a stage's V tiles and scales before its K work
+#endif
+#ifndef FADE_LAZYMAX
+#define FADE_LAZYMAX 1     // keep the running maxima until a score exceeds them by 2^8
+#endif
 #ifndef FADE_MID_GROUPS
 #define FADE_MID_GROUPS 3
 #endif
@@ -307,14 +313,31 @@ template <> struct Pk<FADE_BF16> {
 // the reference's `q.to(dtype) * scale.to(dtype)` (fade/quant.py:124-127).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t shr_k(uint32_t x, int i) { return x >> (4 * (i + 1)); }
+__device__ __forceinline__ uint32_t hfma2_f16(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 template <int DT> struct Conv {
     // INT4: bytes b0..b3 of x hold elements (2j: high nibble, 2j+1: low).
     // h[0]=(e1,e5) h[1]=(e0,e4) h[2]=(e3,e7) h[3]=(e2,e6)
+    // fp16: the nibbles at bits 4-7 / 20-23 need no shift: masked in place
+    // they read fp16(1024 + 16 u) and one packed FMA (v / 16 - 72, exact)
+    // leaves the code, so 8 codes take one shift instead of three.  bf16 has
+    // too few mantissa bits for that and shifts every field down.
     __device__ __forceinline__ static void int4(uint32_t x, uint32_t (&h)[4]) {
-        h[0] = Pk<DT>::sub(lop3_and_xor(x, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
-        h[1] = Pk<DT>::sub(lop3_and_xor(shr_k(x, 0), 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
-        h[2] = Pk<DT>::sub(lop3_and_xor(shr_k(x, 1), 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
-        h[3] = Pk<DT>::sub(lop3_and_xor(shr_k(x, 2), 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+        if constexpr (DT == FADE_F16) {
+            const uint32_t y = x >> 8;
+            h[0] = Pk<DT>::sub(lop3_and_xor(x, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+            h[1] = hfma2_f16(lop3_and_xor(x, 0x00F000F0u, 0x64806480u), 0x2C002C00u, 0xD480D480u);
+            h[2] = Pk<DT>::sub(lop3_and_xor(y, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+            h[3] = hfma2_f16(lop3_and_xor(y, 0x00F000F0u, 0x64806480u), 0x2C002C00u, 0xD480D480u);
+        } else {
+            h[0] = Pk<DT>::sub(lop3_and_xor(x, 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+            h[1] = Pk<DT>::sub(lop3_and_xor(shr_k(x, 0), 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+            h[2] = Pk<DT>::sub(lop3_and_xor(shr_k(x, 1), 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+            h[3] = Pk<DT>::sub(lop3_and_xor(shr_k(x, 2), 0x000F000Fu, Pk<DT>::K4), Pk<DT>::B4);
+        }
     }
     // 2-bit: field f of a byte sits at bit 6-2f.  h[0..3] = fields 3,2,1,0 of
     // bytes (0,2); h[4..7] = fields 3,2,1,0 of bytes (1,3).
@@ -1289,6 +1312,21 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             // two accumulators per m-tile (even / odd k-steps) halve the
             // dependent MMA chain; summed before the softmax
             float sacc[2][NT][4];
+            // V tiles and per-token V scales of both m-tiles, issued before the
+            // K work so their shared-memory latency hides behind it
+            uint32_t vpre[2][2][L::NCHV];
+            uint32_t vspre[2][2];
+            if constexpr (FADE_VPRE != 0) {
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    load_tiles_at<L::NCHV, true>(vbase, voffs, mt, vpre[mt]);
+                    if constexpr (!VGROUP) {
+                        const uint32_t* sc32 = reinterpret_cast<const uint32_t*>(scb);
+                        vspre[mt][0] = sc32[(gw * 32 + mt * 16 + 2 * t) >> 1];
+                        vspre[mt][1] = sc32[(gw * 32 + mt * 16 + 8 + 2 * t) >> 1];
+                    }
+                }
+            }
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
@@ -1372,6 +1410,26 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 #else
             {
 #endif
+            // Lazy maxima: while every score of the stage stays within 2^8 of
+            // its row's running maximum (log2 units), the maxima are kept and
+            // the weights (<= 256, finite in the model dtype) use them as is;
+            // the shuffle reduction and rescale run only when some row exceeds
+            // that margin.  Maxima start at kMaskedMax, so a row's first stage
+            // always takes the full path.
+            bool full = true;
+            if constexpr (FADE_LAZYMAX != 0) {
+                bool need = false;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const float lm = fmaxf(fmaxf(sacc[0][nt][e], sacc[0][nt][e + 2]),
+                                               fmaxf(sacc[1][nt][e], sacc[1][nt][e + 2]));
+                        need |= lm * qks > m_run[nt][e] + 8.f;
+                    }
+                full = __any_sync(0xffffffffu, need);
+            }
+            if (full) {
             bool grow = false;
             float corr[NT][2];
 #pragma unroll
@@ -1404,6 +1462,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         }
                     }
             }
+            }   // full
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -1425,7 +1484,14 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             for (int mt = 0; mt < (FADE_ABLATE == 2 ? 0 : 2); ++mt) {
                 const int trow0 = gw * 32 + mt * 16;
                 uint32_t vr[2][L::NCHV];
-                load_tiles_at<L::NCHV, true>(vbase, voffs, mt, vr);
+                if constexpr (FADE_VPRE != 0) {
+#pragma unroll
+                    for (int a = 0; a < 2; ++a)
+#pragma unroll
+                        for (int cb = 0; cb < L::NCHV; ++cb) vr[a][cb] = vpre[mt][a][cb];
+                } else {
+                    load_tiles_at<L::NCHV, true>(vbase, voffs, mt, vr);
+                }
                 // tokens of this m-tile past the length: their scales may be
                 // stale bytes (NaN * 0 must not reach the MMA), so zero them;
                 // a tile entirely past the length is skipped.
@@ -1434,9 +1500,14 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 uint32_t vs0 = 0, vs1 = 0;
                 const uint16_t* gsc = nullptr;
                 if constexpr (!VGROUP) {
-                    const uint32_t* sc32 = reinterpret_cast<const uint32_t*>(scb);
-                    vs0 = sc32[(trow0 + 2 * t) >> 1];       // tokens 2t, 2t+1
-                    vs1 = sc32[(trow0 + 8 + 2 * t) >> 1];   // tokens 8+2t, 9+2t
+                    if constexpr (FADE_VPRE != 0) {
+                        vs0 = vspre[mt][0];
+                        vs1 = vspre[mt][1];
+                    } else {
+                        const uint32_t* sc32 = reinterpret_cast<const uint32_t*>(scb);
+                        vs0 = sc32[(trow0 + 2 * t) >> 1];       // tokens 2t, 2t+1
+                        vs1 = sc32[(trow0 + 8 + 2 * t) >> 1];   // tokens 8+2t, 9+2t
+                    }
                     const int rem = clen - tile_tok;  // valid tokens in this tile (> 0)
                     if (rem < 16) {
                         const int t0 = 2 * t, t1 = 8 + 2 * t;
