@@ -934,7 +934,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         *abort_flag = 0;
         for (int s = 0; s < NS; ++s) {
             mbar_init(full_bar(s), 32);
-            mbar_init(empty_bar(s), kConsumerWarps);
+            mbar_init(empty_bar(s), kConsumerWarps * 32);   // every consumer lane arrives
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1594,8 +1594,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             FADE_TR(6);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(s));
+        mbar_arrive(empty_bar(s));   // each lane after its own reads of the stage
         s += G;
         if (s >= NS) { s -= NS; ph ^= 1u; }
     }
