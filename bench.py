@@ -322,6 +322,7 @@ def run_fade(args, ws, rank, local):
         vh = vn.cpu().pin_memory()
         oh = torch.empty(dec.out.shape, dtype=dec.out.dtype).pin_memory()
         dec.step_host(qh, kh, vh, oh)
+        dec.capture_host(qh, kh, vh, oh)   # copies overlap the layers, one graph per step
         torch.cuda.synchronize(dev)
         if ws > 1:
             dist.barrier()

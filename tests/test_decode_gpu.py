@@ -277,3 +277,37 @@ def test_decoder_step_matches_oracle(cuda_device, fused, S, cap):
         np.testing.assert_array_equal(t_bits(ly.mid_vs[:, :, :n]), to_bits(s["mid_vs"], dt))
         np.testing.assert_array_equal(t_bits(ly.ring_k), to_bits(s["ring_k"], dt))
         np.testing.assert_array_equal(t_bits(ly.ring_v), to_bits(s["ring_v"], dt))
+
+
+def test_step_host_graph_matches_device_step(cuda_device):
+    """step_host replayed from capture_host (copies overlapping the layers)
+    gives the same bits and the same cache state as device-input steps."""
+    from fade_b200.decoder import TieredDecoder
+
+    dt = "bf16"
+    L, B, Hq, Hkv, D, S = 3, 2, 8, 2, 128, 400
+    decs = [TieredDecoder(L, B, Hq, Hkv, D, dtype=torch.bfloat16, n_sink=4, recent_window=64, mid_capacity=512)
+            for _ in range(2)]
+    for l in range(L):
+        k = np_to_dt_tensor(seeded_outliers((B, Hkv, S, D), 300 + l, dt), dt)
+        v = np_to_dt_tensor(seeded_outliers((B, Hkv, S, D), 400 + l, dt), dt)
+        for d in decs:
+            d.load_prompt(l, k, v)
+    dev_dec, host_dec = decs
+    qh = torch.empty(L, B, Hq, 1, D, dtype=torch.bfloat16).pin_memory()
+    kh = torch.empty(L, B, Hkv, D, dtype=torch.bfloat16).pin_memory()
+    vh = torch.empty(L, B, Hkv, D, dtype=torch.bfloat16).pin_memory()
+    oh = torch.empty(L, B, Hq, 1, D, dtype=torch.bfloat16).pin_memory()
+    gen = torch.Generator().manual_seed(7)
+    for step in range(4):
+        qh.copy_(torch.randn(qh.shape, generator=gen).to(torch.bfloat16))
+        kh.copy_(torch.randn(kh.shape, generator=gen).to(torch.bfloat16))
+        vh.copy_(torch.randn(vh.shape, generator=gen).to(torch.bfloat16))
+        if step == 1:
+            dev_dec.capture()
+            host_dec.capture_host(qh, kh, vh, oh)
+        ref = dev_dec.step(qh.to(cuda_device), kh.to(cuda_device), vh.to(cuda_device)).clone()
+        host_dec.step_host(qh, kh, vh, oh)
+        torch.cuda.synchronize()
+        assert torch.equal(oh, ref.cpu()), step
+    assert host_dec.mid_lengths() == dev_dec.mid_lengths() == [S - 68 + 4] * L
