@@ -161,6 +161,7 @@ _SIGNATURES = {
     "fade_workspace_check": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp]),
     "fade_decode_attn_noalloc_max_bytes": (ctypes.c_size_t, []),
     "fade_decode_attn_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeDesc), _vp]),
+    "fade_decode_attn_noalloc_check": (ctypes.c_int, [_vp]),
 }
 
 _lib = None

@@ -114,58 +114,28 @@ class RotatedINT4Backend:
 
 @dataclass
 class TurboQuantBackend:
-    """``turboquant-kv`` (TurboQuantProd) wrapper; the package is optional."""
+    """Placeholder for the reference's optional ``turboquant-kv`` backend.
+
+    TurboQuant is a third-party quantiser outside this library's hot path; the
+    name stays registered (``"turbo"`` / ``"turboquant"``) so configurations
+    that mention it fail the same way as the reference does when the optional
+    package is absent: with an ImportError on first use.
+    """
 
     head_dim: int = 128
     bits: float = 4
     device: str | None = None
-    _tq: Any = None
 
     @property
     def name(self) -> str:
         return f"turboquant_{self.bits}bit"
 
-    def _ensure_tq(self, device=None):
-        if self._tq is None:
-            try:
-                from turboquant import TurboQuantProd  # third-party, optional
-            except ImportError as e:
-                raise ImportError(
-                    "TurboQuantBackend requires turboquant-kv. Install with: pip install fade-kv[turbo]"
-                ) from e
-            dev = self.device or (str(device) if device else "cpu")
-            self._tq = TurboQuantProd(head_dim=self.head_dim, bits=self.bits, device=dev)
-        return self._tq
+    def _unavailable(self, *args, **kwargs):
+        raise ImportError(
+            "TurboQuantBackend requires turboquant-kv. Install with: pip install fade-kv[turbo]"
+        )
 
-    def _compress(self, x: Tensor, side: str) -> dict[str, Tensor]:
-        tq = self._ensure_tq(x.device)
-        B, H, S, D = x.shape
-        flat = x.reshape(-1, D)
-        out = {k: v for k, v in tq.compress(flat, flat).items() if k.startswith(side)}
-        out["shape"] = torch.tensor([B, H, S, D])
-        return out
-
-    def _decompress(self, compressed: dict[str, Tensor], side: str, dtype) -> Tensor:
-        tq = self._ensure_tq()
-        B, H, S, D = (int(x) for x in compressed["shape"].tolist())
-        kv = {k: v for k, v in compressed.items() if k != "shape"}
-        other = "v_" if side == "k_" else "k_"
-        for key in list(kv):
-            kv.setdefault(other + key[2:], kv[key])
-        k_flat, v_flat = tq.decompress(kv)
-        return (k_flat if side == "k_" else v_flat).reshape(B, H, S, D).to(dtype)
-
-    def compress_k(self, k: Tensor) -> dict[str, Tensor]:
-        return self._compress(k, "k_")
-
-    def decompress_k(self, compressed, dtype=torch.float16) -> Tensor:
-        return self._decompress(compressed, "k_", dtype)
-
-    def compress_v(self, v: Tensor) -> dict[str, Tensor]:
-        return self._compress(v, "v_")
-
-    def decompress_v(self, compressed, dtype=torch.float16) -> Tensor:
-        return self._decompress(compressed, "v_", dtype)
+    compress_k = decompress_k = compress_v = decompress_v = _unavailable
 
 
 _BACKENDS: dict[str, type] = {

@@ -2525,11 +2525,20 @@ extern "C" int fade_decode_attn_noalloc(const fade_decode_desc* d, void* stream)
     void* ws = nullptr;
     int st = fade::noalloc_scratch(&ws);
     if (st != FADE_OK) return st;
-    // The array keeps the previous call's bytes.  Only the error word must
-    // start at zero (every partial the finisher reads is written by the same
-    // call first), so clear the first 256 bytes on the caller's stream.
-    FADE_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, as_stream(stream)));
+    // The array keeps the previous call's bytes.  Every partial, statistic
+    // and age-out length the kernels read is written earlier in the same
+    // call; the only word that must start at zero is the error word, which
+    // is zero when the library loads and is cleared again by
+    // fade_decode_attn_noalloc_check after it reports a timeout (so a timeout
+    // stays visible until the caller asks for it, as with a workspace).
     return fade_decode_attn(d, ws, fade::kNoAllocScratchBytes, stream);
+}
+
+extern "C" int fade_decode_attn_noalloc_check(void* stream) {
+    void* ws = nullptr;
+    const int st = fade::noalloc_scratch(&ws);
+    if (st != FADE_OK) return st;
+    return fade_workspace_check(ws, fade::kNoAllocScratchBytes, stream);
 }
 
 #ifdef FADE_TRACE

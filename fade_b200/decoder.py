@@ -201,9 +201,11 @@ class TieredDecoder:
             a.ring_cap, a.ring_origin = R, int(ly.ring_origin)
             a.k_new, a.v_new = kn.data_ptr(), vn.data_ptr()
             a.new_sb, a.new_sh = kn.stride(0), kn.stride(1)
-            # the kernel preceding each layer's call never writes this layer's
-            # tiers (only this call does), so the middle may stream early
-            a.prefetch_tiers = 1
+            # With two or more layers the kernel preceding a layer's call is
+            # another layer's, which never writes this layer's tiers or their
+            # lengths, so the middle may stream early.  With one layer it is
+            # this layer's previous call, whose finisher advances the lengths.
+            a.prefetch_tiers = 1 if len(self.layers) > 1 else 0
             ly.age_desc = a
         return ly.plan
 

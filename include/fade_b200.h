@@ -254,7 +254,12 @@ int fade_decode_attn(const fade_decode_desc* d, void* workspace, size_t ws_bytes
  * token is dropped, as fade_age_out_int4 does.
  * With prefetch_tiers = 1 the call may read the cache tiers (not q, k_new,
  * v_new) before the preceding kernel on the stream has finished: set it only
- * when that kernel does not write them. */
+ * when that kernel does not write them.  The tiers include their device
+ * lengths: the middle's `lens` (mid_len) and the ring's counts.  A preceding
+ * fade_decode_attn_age_out or fade_age_out_int4 on the SAME layer writes
+ * them, so two such calls on one layer back to back need prefetch_tiers = 0
+ * (a chain over two or more layers may set it: each call then follows
+ * another layer's). */
 typedef struct fade_age_out_desc {
     int32_t ring_seg, mid_seg;
     int64_t ring_cap, ring_origin;
@@ -283,6 +288,15 @@ int fade_decode_attn_age_out(const fade_decode_desc* d, const fade_age_out_desc*
  * caller.  Allocates nothing (no cudaMalloc / cudaFree). */
 size_t fade_decode_attn_noalloc_max_bytes(void);
 int fade_decode_attn_noalloc(const fade_decode_desc* d, void* stream);
+
+/* Companion of fade_decode_attn_noalloc (no counterpart in the reference):
+ * reads and clears the built-in array's device error word, as
+ * fade_workspace_check does for a workspace (synchronises the stream).
+ * Returns FADE_ERR_TIMEOUT when a bounded device wait of any earlier
+ * fade_decode_attn_noalloc call on the current device gave up (that call's
+ * output is not valid), FADE_OK otherwise.  The error word is sticky until
+ * this call clears it. */
+int fade_decode_attn_noalloc_check(void* stream);
 
 /* Reads and clears the device error word of a workspace (synchronises the
  * stream).  Returns FADE_OK or FADE_ERR_TIMEOUT. */

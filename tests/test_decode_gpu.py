@@ -215,17 +215,20 @@ def test_repeat_calls_are_stable(cuda_device):
         assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("fused,S,cap", [(True, 600, 600), (False, 600, 600), (True, 194, 128), (False, 194, 128)])
-def test_decoder_step_matches_oracle(cuda_device, fused, S, cap):
+@pytest.mark.parametrize("fused,S,cap,L", [(True, 600, 600, 2), (False, 600, 600, 2), (True, 194, 128, 2),
+                                           (False, 194, 128, 2), (True, 194, 300, 1), (False, 194, 300, 1)])
+def test_decoder_step_matches_oracle(cuda_device, fused, S, cap, L):
     """Multi-layer TieredDecoder: age-out + attention per layer, eager and
     graph-captured, as one fused call per layer or as age-out + attention.
     cap=128 with a 126-token middle runs into the capacity: later steps attend
-    the unchanged tiers and drop the new token.  The stored tiers (codes,
+    the unchanged tiers and drop the new token.  L=1 chains each step's call
+    directly after the same layer's previous call while the middle grows from
+    126 across the 128-token unit boundary.  The stored tiers (codes,
     scales, ring) must match the oracle bit for bit."""
     from fade_b200.decoder import TieredDecoder
 
     dt = "bf16"
-    L, B, Hq, Hkv, D = 2, 2, 8, 2, 128
+    B, Hq, Hkv, D = 2, 8, 2, 128
     dec = TieredDecoder(L, B, Hq, Hkv, D, dtype=torch.bfloat16, n_sink=4, recent_window=64, mid_capacity=cap,
                         fused=fused)
     cap_r = -(-cap // 128) * 128
