@@ -69,9 +69,12 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // group's first warp), row 4c + 3 for the producer
 #define FADE_TR(slot) do { if ((threadIdx.x & 127) == 0 && threadIdx.x < blockDim.x - 32 && blockIdx.x < 192 && (slot) < kTraceEv) g_trace[(blockIdx.x * 4 + threadIdx.x / 128) * kTraceEv + (slot)] = gtimer(); } while (0)
 #define FADE_TRP(slot) do { if (threadIdx.x == (blockDim.x / 32 - 1) / 5 * 4 * 32 && blockIdx.x < 192 && (slot) < kTraceEv) g_trace[(blockIdx.x * 4 + 3) * kTraceEv + (slot)] = gtimer(); } while (0)
+// FP-tier warp (lane 0): row 4c + 3, slots 80..
+#define FADE_TRFP(slot) do { if ((threadIdx.x & 31) == 0 && blockIdx.x < 192) g_trace[(blockIdx.x * 4 + 3) * kTraceEv + 80 + (slot)] = gtimer(); } while (0)
 // finisher CTAs record into rows 768.. of the same array
 #define FADE_TRF(slot) do { if (threadIdx.x == 0 && blockIdx.x < 256) g_trace[(768 + blockIdx.x) * kTraceEv + (slot)] = gtimer(); } while (0)
 #else
+#define FADE_TRFP(slot) do {} while (0)
 #define FADE_TRF(slot) do {} while (0)
 #define FADE_TR(slot) do {} while (0)
 #define FADE_TRP(slot) do {} while (0)
@@ -97,7 +100,7 @@ __host__ __device__ constexpr int mid_threads(int NT) {
     return (mid_groups(NT) * (kConsumerWarps + 1) + 1) * 32;
 }
 constexpr int kMidMaxStages = 15;
-constexpr int kFpChunk = 48;       // FP-tier tokens the FP warp stages per pass
+constexpr int kFpChunk = 80;       // FP-tier tokens the FP warp stages per pass (sink + recent + new)
 constexpr int kSmemPerBlock = 232448;  // 227 KB opt-in shared memory per CTA
 constexpr float kLog2e = 1.4426950408889634f;
 // Initial running maximum of the middle kernel's online softmax: finite and
@@ -629,7 +632,7 @@ __device__ __forceinline__ void load_tiles(uint32_t base, int trow0, int lane, u
 // and the new token is written into the freed ring slot.
 // ---------------------------------------------------------------------------
 template <int DT, int D, int NT>
-__device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, uint8_t* fsm) {
+__device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, uint8_t* fsm, bool waited) {
     using T = typename Elem<DT>::T;
     using P = Pk<DT>;
     constexpr int KSTEPS = D / 16, MT = D / 16;
@@ -641,6 +644,7 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
     const int z0 = (int)((int64_t)c * Z / n_cta), z1 = (int)((int64_t)(c + 1) * Z / n_cta);
     T* ksm = reinterpret_cast<T*>(fsm);
     T* vsm = ksm + kFpChunk * RS;
+    FADE_TRFP(0);
     for (int z = z0; z < z1; ++z) {
         const int b = z / p.Hkv, h = z % p.Hkv;
         // ---- FP segments of the row ----
@@ -655,39 +659,38 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
                 T_seg += sl[s];
             }
         }
-        // ---- fused age-out bookkeeping ----
+        // ---- fused age-out bookkeeping (the middle length is read below,
+        //      together with the first chunk's copies: one memory round trip) ----
         int64_t n = 0, ft_aged = -1, slot = 0;
         bool room = false;
-        if (p.age) {
-            n = p.mid_len[b];
-            room = n < p.mid_cap;
-        }
-        if (room) {
-            slot = (n - p.ring_origin) % p.ring_cap;
-            if (slot < 0) slot += p.ring_cap;
-            ft_aged = slot;
-            for (int s = 0; s < p.ring_fp; ++s) ft_aged += sl[s];
-        }
-        if (p.age && lane == 0) p.ws_age[z] = (int)(room ? n + 1 : n);
-        const int64_t T_all = T_seg + (room ? 1 : 0);   // + the step's new token
+        // the step's new token is staged after the FP tokens whenever an
+        // age-out runs, and attended only when the middle has room
+        const int64_t T_stage = T_seg + (p.age ? 1 : 0);
+        int64_t T_all = T_seg;
+        float scpre[DPL];
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) scpre[i] = 0.f;
         const T* kn = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
         const T* vn = reinterpret_cast<const T*>(p.v_new) + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh;
-        // ---- query fragments (exact model-dtype q), natural channel order ----
+        // ---- query fragments (exact model-dtype q), natural channel order;
+        //      loaded after the grid dependency resolves ----
         uint32_t qf[NT][KSTEPS][2];
+        auto load_q = [&]() {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int r = nt * 8 + gid;
-            const bool rv = r < p.rows;
-            const int j = rv ? r / p.n_q : 0, sq = rv ? r % p.n_q : 0;
-            const uint32_t* qp = reinterpret_cast<const uint32_t*>(
-                reinterpret_cast<const T*>(p.qo) + (int64_t)b * p.qo_sb + (int64_t)(h * p.g + j) * p.qo_sh +
-                (int64_t)sq * p.qo_ss);
+            for (int nt = 0; nt < NT; ++nt) {
+                const int r = nt * 8 + gid;
+                const bool rv = r < p.rows;
+                const int j = rv ? r / p.n_q : 0, sq = rv ? r % p.n_q : 0;
+                const uint32_t* qp = reinterpret_cast<const uint32_t*>(
+                    reinterpret_cast<const T*>(p.qo) + (int64_t)b * p.qo_sb + (int64_t)(h * p.g + j) * p.qo_sh +
+                    (int64_t)sq * p.qo_ss);
 #pragma unroll
-            for (int ks = 0; ks < KSTEPS; ++ks) {
-                qf[nt][ks][0] = rv ? qp[ks * 8 + t] : 0u;       // channels 16ks + 2t, +1
-                qf[nt][ks][1] = rv ? qp[ks * 8 + 4 + t] : 0u;   // channels 16ks + 2t + 8, +9
+                for (int ks = 0; ks < KSTEPS; ++ks) {
+                    qf[nt][ks][0] = rv ? qp[ks * 8 + t] : 0u;       // channels 16ks + 2t, +1
+                    qf[nt][ks][1] = rv ? qp[ks * 8 + 4 + t] : 0u;   // channels 16ks + 2t + 8, +9
+                }
             }
-        }
+        };
         float m_run[NT][2], l_run[NT][2], o[NT][MT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -701,45 +704,77 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
 #ifdef FADE_NO_FPATTN
         for (int64_t c0 = 0; c0 < 0; c0 += kFpChunk) {   // profiling: FP tiers skipped
 #else
-        for (int64_t c0 = 0; c0 < T_all; c0 += kFpChunk) {
+        for (int64_t c0 = 0; c0 < T_stage; c0 += kFpChunk) {
 #endif
-            const int nc = (int)((T_all - c0) < kFpChunk ? (T_all - c0) : kFpChunk);
+            const int nc = (int)((T_stage - c0) < kFpChunk ? (T_stage - c0) : kFpChunk);
             const int nc16 = (nc + 15) & ~15;
             __syncwarp();   // the previous chunk's rows are no longer read
-            // ---- stage K and V rows (padding rows up to a multiple of 16: row 0) ----
-            for (int i = lane; i < nc16 * PCS; i += 32) {
-                const int tk = i / PCS, pc = i % PCS;
-                int64_t ft = c0 + (tk < nc ? tk : 0);
-                const T* ks;
-                const T* vs;
-                if (ft >= T_seg) {
-                    ks = kn + pc * 8;
-                    vs = vn + pc * 8;
-                } else {
-                    int s = 0;
-                    while (s < p.n_fp - 1 && ft >= sl[s]) { ft -= sl[s]; ++s; }
-                    const int64_t off = (sr[s] + ft) * D + pc * 8;
-                    ks = reinterpret_cast<const T*>(p.fp[s].k) + off;
-                    vs = reinterpret_cast<const T*>(p.fp[s].v) + off;
+            // ---- stage K and V rows (padding rows up to a multiple of 16: row 0).
+            //      The cache tiers first; the step's new token (written by the
+            //      preceding kernel) only after the grid dependency resolves. ----
+            auto stage = [&](bool new_token) {
+                for (int i = lane; i < nc16 * PCS; i += 32) {
+                    const int tk = i / PCS, pc = i % PCS;
+                    int64_t ft = c0 + (tk < nc ? tk : 0);
+                    if ((ft >= T_seg) != new_token) continue;
+                    const T* ks;
+                    const T* vs;
+                    if (ft >= T_seg) {
+                        ks = kn + pc * 8;
+                        vs = vn + pc * 8;
+                    } else {
+                        int s = 0;
+                        while (s < p.n_fp - 1 && ft >= sl[s]) { ft -= sl[s]; ++s; }
+                        const int64_t off = (sr[s] + ft) * D + pc * 8;
+                        ks = reinterpret_cast<const T*>(p.fp[s].k) + off;
+                        vs = reinterpret_cast<const T*>(p.fp[s].v) + off;
+                    }
+                    cp_async16(smem_u32(ksm + tk * RS + pc * 8), ks);
+                    cp_async16(smem_u32(vsm + tk * RS + pc * 8), vs);
                 }
-                cp_async16(smem_u32(ksm + tk * RS + pc * 8), ks);
-                cp_async16(smem_u32(vsm + tk * RS + pc * 8), vs);
+            };
+            stage(false);
+            if (c0 == 0 && p.age) {
+                // loads in flight with the copies above
+                n = p.mid_len[b];
+                const T* ksc = reinterpret_cast<const T*>(p.k_scale) + (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) scpre[i] = Elem<DT>::to_f(ksc[lane * DPL + i]);
+                room = n < p.mid_cap;
+                if (room) {
+                    slot = (n - p.ring_origin) % p.ring_cap;
+                    if (slot < 0) slot += p.ring_cap;
+                    ft_aged = slot;
+                    for (int s = 0; s < p.ring_fp; ++s) ft_aged += sl[s];
+                    T_all = T_seg + 1;
+                }
+            }
+            FADE_TRFP(1);
+            if (!waited) {
+                griddep_wait();
+                waited = true;
+            }
+            FADE_TRFP(2);
+            stage(true);
+            if (c0 == 0) {
+                load_q();
+                if (p.age && lane == 0) p.ws_age[z] = (int)(room ? n + 1 : n);
             }
             cp_async_wait_all();
+            FADE_TRFP(3);
             __syncwarp();
             if (ft_aged >= c0 && ft_aged < c0 + nc) {
                 // ---- the aged token: INT4 codes into the middle, its staged row
                 //      becomes rnd(code * scale); the new token takes its ring slot ----
                 T* kr = ksm + (ft_aged - c0) * RS;
                 T* vr = vsm + (ft_aged - c0) * RS;
-                const T* ksc = reinterpret_cast<const T*>(p.k_scale) + (int64_t)b * p.ks_sb + (int64_t)h * p.ks_sh;
                 float kx[DPL], vx[DPL], sc[DPL];
 #pragma unroll
                 for (int i = 0; i < DPL; ++i) {
                     const int d = lane * DPL + i;
                     kx[i] = Elem<DT>::to_f(kr[d]);
                     vx[i] = Elem<DT>::to_f(vr[d]);
-                    sc[i] = Elem<DT>::to_f(ksc[d]);
+                    sc[i] = scpre[i];
                 }
                 float m = 0.f;
 #pragma unroll
@@ -802,7 +837,7 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int tk = t0 + gid + ((e >> 1) << 3);
-                        sacc[nt][e] = (tk >= nc) ? -INFINITY : sacc[nt][e] * p.qk_scale;
+                        sacc[nt][e] = (c0 + tk >= T_all) ? -INFINITY : sacc[nt][e] * p.qk_scale;
                     }
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
@@ -863,6 +898,12 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
                 }
             }
         }
+        if (!waited) {   // no FP token: the workspace is written only after the dependency
+            griddep_wait();
+            waited = true;
+        }
+        if (T_stage == 0 && p.age && lane == 0) p.ws_age[z] = (int)n;
+        FADE_TRFP(4);
         // ---- partial of row z: O^T rows are channels mi*16 + gid (+8) ----
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -887,6 +928,7 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
             }
         __syncwarp();
     }
+    FADE_TRFP(5);
 }
 
 // ---------------------------------------------------------------------------
@@ -953,11 +995,14 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // next kernel in the stream start its prologue.  With `early` the tiers
     // are known not to be written by that kernel: the producer starts
     // streaming at once and only the consumers (queries, partial slots) wait.
-    if (!(p.early && is_producer)) griddep_wait();
+    // The FP warp, too, streams its cache tiers before the dependency with
+    // `early`; it waits itself before touching q, the new token or the workspace.
+    const bool fp_early = p.early && warp == FPWARP;
+    if (!(p.early && is_producer) && !fp_early) griddep_wait();
     if (warp < PRODUCER) griddep_launch_dependents();
     FADE_TR(1);
     if (warp == FPWARP) {
-        fp_rows_warp<DT, D, NT>(p, c, (int)gridDim.x, smem + L::AB_OFF);
+        fp_rows_warp<DT, D, NT>(p, c, (int)gridDim.x, smem + L::AB_OFF, !fp_early);
         return;
     }
     if (ub >= ue) return;
