@@ -152,8 +152,13 @@ class TieredKVCache(DynamicCache):
         middle_k_bits: int = 4,
         middle_v_bits: int = 4,
         quant_backend: str | QuantBackend = "int4",
+        *,
+        v_int2_group_size: int = DEFAULT_INT2_GROUP_SIZE,
     ) -> None:
         super().__init__()
+        # tokens per scale group of the 2-bit V middle (middle_v_bits=2); the
+        # reference fixes it at DEFAULT_INT2_GROUP_SIZE (fade/cache.py:986)
+        self.v_int2_group_size = int(v_int2_group_size)
         self.n_sink = n_sink
         self.recent_window = recent_window
         self.int4_budget = int4_budget
@@ -445,7 +450,7 @@ class TieredKVCache(DynamicCache):
         if self.middle_v_bits == 4:
             v = dequant_int4(st.int4_vq, st.int4_vs, dtype=self.dtype)
         else:
-            v = dequant_v_int2(st.int4_vq, st.int4_vs, group_size=DEFAULT_INT2_GROUP_SIZE, dtype=self.dtype)
+            v = dequant_v_int2(st.int4_vq, st.int4_vs, group_size=self.v_int2_group_size, dtype=self.dtype)
             n = int(st.int4_pos.shape[0]) if st.int4_pos is not None else 0
             if 0 < n < v.shape[-2]:
                 v = v[..., :n, :]
@@ -483,7 +488,7 @@ class TieredKVCache(DynamicCache):
             else:
                 n = int(st.int4_pos.shape[0])
                 mid = Int4K2VTier(st.int4_kq, st.int4_ks, _pack_int2_last_dim(st.int4_vq), st.int4_vs,
-                                  group=DEFAULT_INT2_GROUP_SIZE, length=n)
+                                  group=self.v_int2_group_size, length=n)
         elif st.backend_k is not None:
             be = self._quant_backend
             if isinstance(be, RotatedINT4Backend) and be.bits in (2, 4):
@@ -542,8 +547,8 @@ class TieredKVCache(DynamicCache):
             if self.middle_v_bits == 4:
                 st.int4_vq, st.int4_vs = quant_v_int4(v_sub)
             else:
-                vp, _ = pad_to_group(v_sub, DEFAULT_INT2_GROUP_SIZE)
-                st.int4_vq, st.int4_vs = quant_v_int2(vp, group_size=DEFAULT_INT2_GROUP_SIZE)
+                vp, _ = pad_to_group(v_sub, self.v_int2_group_size)
+                st.int4_vq, st.int4_vs = quant_v_int2(vp, group_size=self.v_int2_group_size)
             st.int4_pos = pos
             st.backend_k = st.backend_v = st.backend_pos = None
         else:

@@ -44,7 +44,8 @@ def materialize(tiers: dict, dt: str, rotation: np.ndarray | None = None):
       int4_kq/int4_ks/int4_vq/int4_vs  (INT4 K per-channel, INT4 V per-token)
       int4_vq2/int4_vs2/v_group        (V grouped INT2 instead of INT4 V, codes int8 [B,H,S_pad,D])
       n_mid                            (valid middle tokens; padding trimmed)
-      rot_kq/rot_ks/rot_vq/rot_vs/rot_bits  (rotated middle)
+      rot_kq/rot_ks/rot_vq/rot_vs/rot_bits  (rotated middle; rot_exact=True skips the
+                                             reference's rounding of the un-rotated K/V)
     Order of the concatenation does not change attention; the reference's is kept."""
     parts_k, parts_v = [], []
     if "sink_k" in tiers:
@@ -61,8 +62,16 @@ def materialize(tiers: dict, dt: str, rotation: np.ndarray | None = None):
         parts_v.append(v4)
     if "rot_kq" in tiers:
         bits = int(tiers["rot_bits"])
-        parts_k.append(oq.rotated_dequant(tiers["rot_kq"], tiers["rot_ks"], rotation, bits, dt))
-        parts_v.append(oq.rotated_dequant(tiers["rot_vq"], tiers["rot_vs"], rotation, bits, dt))
+        if tiers.get("rot_exact"):
+            # diagnostic form: rnd(code * scale) @ R in float64, without the
+            # reference's final rounding of the un-rotated K/V to the dtype
+            unpack = oq.unpack_int4 if bits == 4 else oq.unpack2
+            Rd = np.asarray(rotation, dtype=np.float64)
+            for key_q, key_s, parts in (("rot_kq", "rot_ks", parts_k), ("rot_vq", "rot_vs", parts_v)):
+                parts.append(oq.dequant(unpack(tiers[key_q]), tiers[key_s], dt).astype(np.float64) @ Rd)
+        else:
+            parts_k.append(oq.rotated_dequant(tiers["rot_kq"], tiers["rot_ks"], rotation, bits, dt))
+            parts_v.append(oq.rotated_dequant(tiers["rot_vq"], tiers["rot_vs"], rotation, bits, dt))
     if "recent_k" in tiers:
         parts_k.append(tiers["recent_k"])
         parts_v.append(tiers["recent_v"])

@@ -20,6 +20,8 @@ import numpy as np
 import torch
 
 OUT = Path(__file__).resolve().parent
+sys.path.insert(0, str(OUT))
+from inputs import CFG3, CFG4, cfg3_inputs, cfg4_inputs, checksum, outlier_tensor  # noqa: E402
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -28,15 +30,6 @@ def bits(t: torch.Tensor) -> np.ndarray:
     if t.dtype == torch.float32:
         return t.contiguous().numpy().view(np.uint32).copy()
     return t.contiguous().numpy().copy()
-
-
-def outlier_tensor(shape, gen, n_out=4, mult=8.0):
-    x = torch.randn(*shape, generator=gen)
-    H, D = shape[1], shape[-1]
-    for h in range(H):
-        ch = torch.randperm(D, generator=gen)[:n_out]
-        x[:, h, :, ch] *= mult
-    return x
 
 
 def rope_schemes(ref: str) -> None:
@@ -269,18 +262,99 @@ def main(ref: str) -> None:
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 
+def decode_cfg3_g32(ref: str) -> None:
+    """Config 3 at BASELINE's settings (batch sliced to 1): H2O survivors of a
+    4096-token prompt (_assign_one_layer, budget 400) through the reference's
+    evicting apply_tier_assignment (un-RoPE / re-RoPE), K INT4, V grouped INT2
+    with group 32 (quant_v_int2(pad_to_group(v, 32), 32)), then the reference's
+    dequant + SDPA over sink | middle | recent."""
+    sys.path.insert(0, ref)
+    import torch.nn.functional as F
+    from fade.cache import TIER_FP16, TIER_INT4, TieredKVCache
+    from fade.policy import _assign_one_layer
+    from fade.quant import dequant_int4, dequant_v_int2, pad_to_group, quant_v_int2
+    from fade.rope import Vanilla
+
+    c = CFG3
+    dt = torch.float16
+    scheme = Vanilla(theta=c["theta"], head_dim=c["D"])
+    k, v, q, scores = cfg3_inputs(lambda pos: scheme.compute_cos_sin(pos, torch.device("cpu"), model_dtype=dt))
+    cache = TieredKVCache(n_sink=c["n_sink"], recent_window=c["recent"], int4_budget=c["budget"], dtype=dt,
+                          rope_theta=c["theta"], head_dim=c["D"], rope_scheme=scheme)
+    cache.update(k, v, 0)
+    tiers = _assign_one_layer(c["S"], scores, c["n_sink"], c["recent"], c["budget"], 0)
+    cache.apply_tier_assignment(0, tiers)
+    st = cache._layers[0]
+    keep = tiers != 3
+    kept = tiers[keep]
+    v_mid = v[:, :, keep.nonzero().squeeze(-1)][:, :, (kept == TIER_INT4).nonzero().squeeze(-1)]
+    n_mid = v_mid.shape[2]
+    vq, vs = quant_v_int2(pad_to_group(v_mid, c["group"])[0], group_size=c["group"])
+    k_mid = dequant_int4(st.int4_kq, st.int4_ks, dtype=dt)
+    v_deq = dequant_v_int2(vq, vs, group_size=c["group"], dtype=dt)[:, :, :n_mid]
+    K = torch.cat([st.sink_k, k_mid, st.fp16_k], dim=2)
+    V = torch.cat([st.sink_v, v_deq, st.fp16_v], dim=2)
+    out32 = F.scaled_dot_product_attention(q.float(), K.float(), V.float(), enable_gqa=True)
+    out = F.scaled_dot_product_attention(q, K, V, enable_gqa=True)
+    d = {"k_sum": np.int64(checksum(k)), "v_sum": np.int64(checksum(v)), "q": bits(q), "tiers": tiers.numpy(),
+         "sink_k": bits(st.sink_k), "sink_v": bits(st.sink_v), "recent_k": bits(st.fp16_k),
+         "recent_v": bits(st.fp16_v), "int4_kq": st.int4_kq.numpy(), "int4_ks": bits(st.int4_ks),
+         "v_mid": bits(v_mid), "int2_vq": vq.numpy(), "int2_vs": bits(vs), "n_mid": np.int64(n_mid),
+         "out_ref": bits(out), "out_ref32": bits(out32)}
+    np.savez_compressed(OUT / "decode_cfg3_g32.npz", **d)
+
+
+def decode_cfg4_ragged(ref: str) -> None:
+    """Config 4 shape: ragged sequences, rotated 2-bit middle.  The reference
+    has no batched ragged path, so this is its per-sequence loop: each
+    sequence's middle through rotated_quant_k / rotated_quant_v, then
+    rotated_dequant + cat(sink, middle, recent) + SDPA."""
+    sys.path.insert(0, ref)
+    import torch.nn.functional as F
+    from fade.rotated_quant import (_random_orthogonal, rotated_dequant_k, rotated_dequant_v,
+                                    rotated_quant_k, rotated_quant_v)
+
+    c = CFG4
+    R = _random_orthogonal(c["D"], 42)
+    lens, seqs, q = cfg4_inputs()
+    d = {"lens": np.array(lens, dtype=np.int64), "q": bits(q), "R": R.numpy()}
+    ns, nr = c["n_sink"], c["recent"]
+    for i, (k, v) in enumerate(seqs):
+        n = k.shape[2]
+        kq, ks = rotated_quant_k(k[:, :, ns:n - nr], R, bits=c["bits"])
+        vq, vs = rotated_quant_v(v[:, :, ns:n - nr], R, bits=c["bits"])
+        kd = rotated_dequant_k(kq, ks, R, bits=c["bits"], dtype=torch.bfloat16)
+        vd = rotated_dequant_v(vq, vs, R, bits=c["bits"], dtype=torch.bfloat16)
+        K = torch.cat([k[:, :, :ns], kd, k[:, :, n - nr:]], dim=2)
+        V = torch.cat([v[:, :, :ns], vd, v[:, :, n - nr:]], dim=2)
+        qi = q[i:i + 1]
+        d[f"s{i}_k_sum"] = np.int64(checksum(k))
+        d[f"s{i}_v_sum"] = np.int64(checksum(v))
+        d[f"s{i}_kq"], d[f"s{i}_ks"] = kq.numpy(), bits(ks)
+        d[f"s{i}_vq"], d[f"s{i}_vs"] = vq.numpy(), bits(vs)
+        d[f"s{i}_out_ref32"] = bits(F.scaled_dot_product_attention(qi.float(), K.float(), V.float(),
+                                                                    enable_gqa=True))
+        d[f"s{i}_out_ref"] = bits(F.scaled_dot_product_attention(qi, K, V, enable_gqa=True))
+    np.savez_compressed(OUT / "decode_cfg4_ragged.npz", **d)
+
+
 if __name__ == "__main__":
     import os
 
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     ref_path = args[0] if args else os.environ.get("FADE_REFERENCE_PATH")
     if not ref_path:
-        raise SystemExit("usage: make_golden.py <path to the reference checkout> [--only-rope-schemes|--only-cache-perseq]")
+        raise SystemExit("usage: make_golden.py <path to the reference checkout> [--only-rope-schemes|--only-cache-perseq|--only-cfg3-cfg4]")
     if "--only-rope-schemes" in sys.argv:
         rope_schemes(ref_path)
+    elif "--only-cfg3-cfg4" in sys.argv:
+        decode_cfg3_g32(ref_path)
+        decode_cfg4_ragged(ref_path)
     elif "--only-cache-perseq" in sys.argv:
         cache_perseq(ref_path)
     else:
         main(ref_path)
         rope_schemes(ref_path)
         cache_perseq(ref_path)
+        decode_cfg3_g32(ref_path)
+        decode_cfg4_ragged(ref_path)

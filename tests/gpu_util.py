@@ -72,5 +72,7 @@ def assert_attn_close(out: np.ndarray, ref: np.ndarray, dt: str, atol: float, ul
     lim = atol + u if additive else np.maximum(atol, u)
     ratio = np.abs(out - ref) / lim
     worst = float(ratio.max()) if ratio.size else 0.0
+    maxabs = float(np.abs(out - ref).max()) if ratio.size else 0.0
+    print(f"[attn {dt}] max|out-ref| = {maxabs:.3e} (north-star atol {atol:g}), worst err/limit {worst:.3f}")
     assert worst <= 1.0, f"max |out-ref| {np.abs(out - ref).max():.3e}, worst err/limit {worst:.3f}"
     return worst
