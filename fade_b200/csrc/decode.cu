@@ -2311,6 +2311,9 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+#ifdef FADE_NO_PDL
+    cfg.numAttrs = 0;
+#endif
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 

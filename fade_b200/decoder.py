@@ -234,7 +234,8 @@ class TieredDecoder:
             if after is not None:
                 after(i)
 
-    def step(self, q: Tensor | None = None, k_new: Tensor | None = None, v_new: Tensor | None = None) -> Tensor:
+    def step(self, q: Tensor | None = None, k_new: Tensor | None = None, v_new: Tensor | None = None,
+             after=None) -> Tensor:
         """One decode step over all layers.  q [L,B,Hq,1,D], k_new/v_new [L,B,Hkv,D]
         (copied into the static input buffers when given).  Returns the static
         output buffer [L,B,Hq,1,D]."""
@@ -243,17 +244,19 @@ class TieredDecoder:
         if k_new is not None:
             self.k_new.copy_(k_new, non_blocking=True)
             self.v_new.copy_(v_new, non_blocking=True)
-        if self._graph is not None:
+        if self._graph is not None and after is None:
             self._graph.replay()
         else:
-            self._launch_all()
+            self._launch_all(after=after)
         return self.out
 
-    def capture(self, layer_events: list | None = None) -> torch.cuda.CUDAGraph:
+    def capture(self, layer_events: list | None = None, after=None) -> torch.cuda.CUDAGraph:
         """Record one full step (every layer's age-out + attention) as a CUDA graph.
         Call after a warm-up step; replays then advance the cache like step().
         `layer_events` (pairs of ``torch.cuda.Event(enable_timing=True,
-        external=True)``) bracket each layer's attention call inside the graph."""
+        external=True)``) bracket each layer's attention call inside the graph.
+        `after(i)` is called after layer i's launch on the capture stream (e.g.
+        a collective over that layer's output); it is recorded into the graph."""
         for i in range(self.L):
             self._plan(i)
         torch.cuda.synchronize(self.device)
@@ -262,10 +265,10 @@ class TieredDecoder:
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
-                self._launch_all(layer_events)
+                self._launch_all(layer_events, after=after)
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
-        if layer_events is None:
+        if layer_events is None and after is None:
             self._graph = g
         return g
 
