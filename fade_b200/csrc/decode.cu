@@ -947,6 +947,11 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     constexpr int KSTEPS = D / 16;   // k-steps of the QK product
     constexpr int MT = D / 16;       // m-tiles of the PV product (rows = channels)
     constexpr int NQ = QSPLIT ? 2 : 1;
+    // 2-bit codes c in {-2,-1,0,1}: c * scale is exactly representable, so the
+    // reference's rnd(c * scale) equals c * scale and the scales can be folded
+    // exactly: K's per-channel scale into the fp32 query (before its hi + lo
+    // split), V's per-token scale into P.  The codes enter the MMA as is.
+    constexpr bool FOLD2 = KB == 2 && VB == 2 && !VGROUP && QSPLIT;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1172,6 +1177,12 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         const float4 v4 = rv ? __ldg(reinterpret_cast<const float4*>(ptr) + c4)
                                              : make_float4(0.f, 0.f, 0.f, 0.f);
                         e[4 * c4] = v4.x; e[4 * c4 + 1] = v4.y; e[4 * c4 + 2] = v4.z; e[4 * c4 + 3] = v4.w;
+                    }
+                    if constexpr (FOLD2) {
+                        uint16_t kse[CH];
+                        load_block_bits(p.k_scale, ks_off + cb * CHW + CH * t, kse);
+#pragma unroll
+                        for (int jj = 0; jj < CH; ++jj) e[jj] *= P::unpack_lo((uint32_t)kse[jj]);
                     }
 #pragma unroll
                     for (int u = 0; u < CHW / 16; ++u) {
@@ -1413,10 +1424,10 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 #pragma unroll
                         for (int u4 = 0; u4 < 4; ++u4) {
                             const int ks = cb * 4 + u4;
-                            const uint32_t a0 = P::mul(h0[2 * u4], ksc[ks][0]);
-                            const uint32_t a1 = P::mul(h1[2 * u4], ksc[ks][0]);
-                            const uint32_t a2 = P::mul(h0[2 * u4 + 1], ksc[ks][1]);
-                            const uint32_t a3 = P::mul(h1[2 * u4 + 1], ksc[ks][1]);
+                            const uint32_t a0 = FOLD2 ? h0[2 * u4] : P::mul(h0[2 * u4], ksc[ks][0]);
+                            const uint32_t a1 = FOLD2 ? h1[2 * u4] : P::mul(h1[2 * u4], ksc[ks][0]);
+                            const uint32_t a2 = FOLD2 ? h0[2 * u4 + 1] : P::mul(h0[2 * u4 + 1], ksc[ks][1]);
+                            const uint32_t a3 = FOLD2 ? h1[2 * u4 + 1] : P::mul(h1[2 * u4 + 1], ksc[ks][1]);
 #pragma unroll
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
@@ -1508,6 +1519,19 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     }
             }
             }   // full
+            // FOLD2: V scales of the C-fragment rows (tokens gid, gid + 8 of
+            // each m-tile); zero past the length, where the bytes are stale
+            float tsc[2][2];
+            if constexpr (FOLD2) {
+                const uint16_t* sc16 = reinterpret_cast<const uint16_t*>(scb);
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr) {
+                        const int tl = gw * 32 + mt * 16 + gid + 8 * hr;
+                        tsc[mt][hr] = (tw - gw * 32 + tl < clen) ? P::unpack_lo((uint32_t)sc16[tl]) : 0.f;
+                    }
+            }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -1517,7 +1541,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     for (int e = 0; e < 4; ++e) {
                         const float pe = ex2(fmaf(sacc[mt][nt][e], qks, -m_run[nt][e & 1]));
                         l_run[nt][e & 1] += pe;
-                        pv[e] = pe;
+                        pv[e] = FOLD2 ? pe * tsc[mt][e >> 1] : pe;
                     }
                     pb[mt][nt][0] = movmatrix_t(P::pack(pv[0], pv[1]));
                     pb[mt][nt][1] = movmatrix_t(P::pack(pv[2], pv[3]));
@@ -1608,7 +1632,12 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         for (int j = 0; j < 4; ++j) {
                             const int mi = cb * 4 + j;
                             uint32_t a0, a1, a2, a3;
-                            if constexpr (!VGROUP) {
+                            if constexpr (FOLD2) {
+                                a0 = h0[lo[j]];
+                                a1 = h0[hi[j]];
+                                a2 = h1[lo[j]];
+                                a3 = h1[hi[j]];
+                            } else if constexpr (!VGROUP) {
                                 a0 = P::mul(h0[lo[j]], vs0);
                                 a1 = P::mul(h0[hi[j]], vs0);
                                 a2 = P::mul(h1[lo[j]], vs1);
@@ -1650,24 +1679,48 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 // ---------------------------------------------------------------------------
 // k0: q_rot = q @ R^T (fp32), one CTA per query row
 // ---------------------------------------------------------------------------
+constexpr int kRotRows = 16;   // query rows per rotate_queries CTA
+
+// q_rot[row][d] = sum_e q[row][e] * R[d][e] in fp32, summed in e order with
+// no FMA contraction (deterministic).  One CTA per kRotRows query rows, one
+// thread per output channel; R is staged once per CTA, transposed, so the
+// threads of a warp read consecutive words.
 template <int DT>
 __global__ void rotate_queries_kernel(const void* q, int Hq, int n_q, int D, int64_t q_sb,
                                       int64_t q_sh, int64_t q_ss, const float* __restrict__ R,
-                                      float* __restrict__ q_rot) {
-    griddep_wait();
+                                      float* __restrict__ q_rot, int n_rows) {
+    extern __shared__ float rsm[];
+    float* rt = rsm;               // [D][D]: rt[e*D + d] = R[d][e]
+    float* qs = rsm + D * D;       // [kRotRows][D]
+    griddep_wait();              // q and R may come from the preceding kernel
     griddep_launch_dependents();
-    extern __shared__ float qs[];
-    const int row = blockIdx.x;  // (b*Hq + hq)*n_q + s
-    const int s = row % n_q, bh = row / n_q;
-    const int hq = bh % Hq, b = bh / Hq;
-    const int64_t off = (int64_t)b * q_sb + (int64_t)hq * q_sh + (int64_t)s * q_ss;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) qs[d] = load_f<DT>(q, off + d);
-    __syncthreads();
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float acc = 0.f;
-        for (int e = 0; e < D; ++e) acc = __fadd_rn(acc, __fmul_rn(qs[e], R[(int64_t)d * D + e]));
-        q_rot[(int64_t)row * D + d] = acc;
+    for (int i = threadIdx.x; i < D * D; i += blockDim.x) {
+        const int d = i / D, e = i % D;
+        rt[e * D + d] = R[i];
     }
+    const int row0 = blockIdx.x * kRotRows;
+    const int nr = (n_rows - row0) < kRotRows ? (n_rows - row0) : kRotRows;
+    for (int i = threadIdx.x; i < nr * D; i += blockDim.x) {
+        const int r = i / D, d = i % D;
+        const int row = row0 + r;   // (b*Hq + hq)*n_q + s
+        const int s = row % n_q, bh = row / n_q;
+        const int hq = bh % Hq, b = bh / Hq;
+        qs[r * D + d] = load_f<DT>(q, (int64_t)b * q_sb + (int64_t)hq * q_sh + (int64_t)s * q_ss + d);
+    }
+    __syncthreads();
+    const int d = threadIdx.x;
+    if (d >= D) return;
+    float acc[kRotRows];
+#pragma unroll
+    for (int r = 0; r < kRotRows; ++r) acc[r] = 0.f;
+    for (int e = 0; e < D; ++e) {
+        const float re = rt[e * D + d];
+#pragma unroll
+        for (int r = 0; r < kRotRows; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(qs[r * D + e], re));
+    }
+#pragma unroll
+    for (int r = 0; r < kRotRows; ++r)
+        if (r < nr) q_rot[(int64_t)(row0 + r) * D + d] = acc[r];
 }
 
 // ---------------------------------------------------------------------------
@@ -2299,6 +2352,24 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
     return FADE_OK;
 }
 
+// The query rotation stages R (up to 64 KB) in shared memory: opt in once per
+// device and kernel instantiation.
+static cudaError_t rotate_queries_smem_attr(const void* fn, int which) {
+    static bool done[kMaxDevices][2] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) dev = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev][which]) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (128 * 128 + kRotRows * 128) * 4);
+        if (e != cudaSuccess) return e;
+        done[dev][which] = true;
+    }
+    return cudaSuccess;
+}
+
 static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                               void** args) {
     cudaLaunchConfig_t cfg = {};
@@ -2359,9 +2430,12 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
         int Hq = d->Hq, nq = d->n_q, D = d->D;
         int64_t a = d->q_sb, b2 = d->q_sh, c2 = d->q_ss;
         const float* R = d->rotation;
-        void* args[] = {(void*)&qp, &Hq, &nq, &D, &a, &b2, &c2, (void*)&R, (void*)&qrot};
-        FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)(d->B * d->Hq * d->n_q)), dim3(128),
-                                 (size_t)d->D * 4, s, args));
+        int n_rows = d->B * d->Hq * d->n_q;
+        void* args[] = {(void*)&qp, &Hq, &nq, &D, &a, &b2, &c2, (void*)&R, (void*)&qrot, &n_rows};
+        const size_t rsmem = (size_t)(D * D + kRotRows * D) * 4;
+        FADE_CUDA_TRY(rotate_queries_smem_attr(fn, d->dtype == FADE_F16 ? 0 : 1));
+        FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)((n_rows + kRotRows - 1) / kRotRows)), dim3((unsigned)D),
+                                 rsmem, s, args));
     }
     if (has_mid) {
         const fade_kv_segment& sg = d->seg[pl.mid_idx];
