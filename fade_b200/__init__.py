@@ -17,6 +17,7 @@ _LAZY = {
     "create_tiered_cache": ("fade_b200.patch", "create_tiered_cache"),
     "get_backend": ("fade_b200.backends", "get_backend"),
     "tiered_decode_attention": ("fade_b200.attention", "tiered_decode_attention"),
+    "fused_int4_sdpa": ("fade_b200.attention", "fused_int4_sdpa"),
     "TieredDecoder": ("fade_b200.decoder", "TieredDecoder"),
 }
 

@@ -326,11 +326,63 @@ def tiered_decode_attention(q: Tensor, tiers: list, sm_scale: float | None = Non
     return plan.run()
 
 
+def fused_int4_sdpa(q: Tensor, k_packed: Tensor, k_scale: Tensor, v_packed: Tensor, v_scale: Tensor,
+                    is_causal: bool = False) -> Tensor:
+    """Drop-in for the reference's ``fused_int4_sdpa``
+    (fade/kernels/fused_int4_attn.py:277-342): attention of q [B, Hq, S_q, D]
+    over one bit-packed INT4 segment (k_packed / v_packed [B, Hkv, S_k, D/2],
+    k_scale [B, Hkv, 1, D] per channel, v_scale [B, Hkv, S_k, 1] per token),
+    sm_scale = 1/sqrt(D), GQA without repeating K/V.  Returns [B, Hq, S_q, D]
+    in q's dtype (fp16 for the reference's fp16 inputs).
+
+    ``is_causal`` follows the reference kernel's mask, which is aligned at the
+    first key: query m attends keys 0..m (fade/kernels/fused_int4_attn.py:
+    166-169).  Each (sequence, query position) then becomes one row of a single
+    decode call, all rows of a sequence reading the same code rows (a
+    zero-stride batch view) with their own length m + 1.
+    Dequantisation rounds each element to the model dtype like the reference's
+    dequant_int4 (the reference's Triton kernel keeps it in fp32); both lie
+    within the attention tolerance of each other."""
+    import math
+
+    dev = _lib.require_cuda(q, k_packed, k_scale, v_packed, v_scale)
+    if q.dim() != 4 or k_packed.dim() != 4:
+        raise ValueError("q must be [B, H_q, S_q, D] and k_packed [B, H_kv, S_k, D//2]")
+    B, Hq, Sq, D = q.shape
+    Hkv, Sk = k_packed.shape[1], k_packed.shape[2]
+    if Hq % Hkv:
+        raise ValueError(f"H_q={Hq} must be a multiple of H_kv={Hkv}")
+    sm = 1.0 / math.sqrt(D)
+    base = align_tier(Int4Tier(k_packed, k_scale.contiguous(), v_packed, v_scale.contiguous()), D)
+    out = torch.empty_like(q)
+    if Sk == 0:
+        return out.zero_()
+    if not is_causal:
+        per = max(1, 16 // (Hq // Hkv))          # query positions per call (rows <= 16)
+        for s0 in range(0, Sq, per):
+            s1 = min(Sq, s0 + per)
+            tiered_decode_attention(q[:, :, s0:s1], [base], sm_scale=sm, out=out[:, :, s0:s1])
+        return out
+    lens = torch.clamp(torch.arange(1, Sq + 1, device=dev, dtype=torch.int32), max=Sk)
+    cap = base.k_packed.shape[2]
+    for b in range(B):
+        def rows(t):                              # the sequence's tensor, once per query position
+            return t[b:b + 1].expand(Sq, *t.shape[1:])
+        tier = Int4Tier(rows(base.k_packed), rows(base.k_scale), rows(base.v_packed), rows(base.v_scale),
+                        lens=lens, max_len=cap)
+        qb = q[b].transpose(0, 1).unsqueeze(2)    # [S_q, Hq, 1, D], query position as the batch
+        ob = torch.empty((Sq, Hq, 1, D), dtype=q.dtype, device=dev)
+        tiered_decode_attention(qb, [tier], sm_scale=sm, out=ob)
+        out[b] = ob[:, :, 0].transpose(0, 1)
+    return out
+
+
 __all__ = [
     "DecodePlan",
     "FPTier",
     "Int4K2VTier",
     "Int4Tier",
     "RotTier",
+    "fused_int4_sdpa",
     "tiered_decode_attention",
 ]

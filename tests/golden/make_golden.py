@@ -338,18 +338,41 @@ def decode_cfg4_ragged(ref: str) -> None:
     np.savez_compressed(OUT / "decode_cfg4_ragged.npz", **d)
 
 
+def cache_state(ref: str) -> None:
+    """The reference's own checkpoint of a cache (cache_state_dict,
+    fade/cache.py:510-559) for the config-1 state: the prompt of
+    decode_cfg1.npz through update + apply_tier_assignment, saved with
+    torch.save, for loading into fade_b200's TieredKVCache."""
+    sys.path.insert(0, ref)
+    from fade.cache import TieredKVCache
+    from fade.policy import _assign_one_layer
+
+    g = np.load(OUT / "decode_cfg1.npz")
+    k = torch.from_numpy(g["k_roped"].view(np.int16)).view(torch.float16)
+    v = torch.from_numpy(g["v"].view(np.int16)).view(torch.float16)
+    S = k.shape[2]
+    cache = TieredKVCache(n_sink=4, recent_window=64, int4_budget=None, dtype=torch.float16, rope_theta=1e6,
+                          head_dim=64)
+    cache.update(k, v, 0)
+    cache.apply_tier_assignment(0, _assign_one_layer(S, torch.arange(S, dtype=torch.float32), 4, 64, None, 0))
+    torch.save(cache.cache_state_dict(), OUT / "cache_state_cfg1.pt")
+
+
 if __name__ == "__main__":
     import os
 
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     ref_path = args[0] if args else os.environ.get("FADE_REFERENCE_PATH")
     if not ref_path:
-        raise SystemExit("usage: make_golden.py <path to the reference checkout> [--only-rope-schemes|--only-cache-perseq|--only-cfg3-cfg4]")
+        raise SystemExit("usage: make_golden.py <path to the reference checkout> [--only-rope-schemes|--only-cache-perseq|--only-cfg3-cfg4|--only-cache-state]")
     if "--only-rope-schemes" in sys.argv:
         rope_schemes(ref_path)
+    elif "--only-cache-state" in sys.argv:
+        cache_state(ref_path)
     elif "--only-cfg3-cfg4" in sys.argv:
         decode_cfg3_g32(ref_path)
         decode_cfg4_ragged(ref_path)
+        cache_state(ref_path)
     elif "--only-cache-perseq" in sys.argv:
         cache_perseq(ref_path)
     else:
@@ -358,3 +381,4 @@ if __name__ == "__main__":
         cache_perseq(ref_path)
         decode_cfg3_g32(ref_path)
         decode_cfg4_ragged(ref_path)
+        cache_state(ref_path)

@@ -187,3 +187,30 @@ def test_cache_rejects_cpu_tensors_and_bad_shapes():
     assert cache.get_mask_sizes(5) == (5, 0)
     with pytest.raises(NotImplementedError):
         cache.set_codebooks(None)
+
+
+def test_fade_import_alias():
+    """Code importing the reference package by name resolves to fade_b200."""
+    import sys
+
+    from fade_b200 import compat
+
+    saved = {k: v for k, v in sys.modules.items() if k == "fade" or k.startswith("fade.")}
+    for k in saved:
+        del sys.modules[k]
+    try:
+        compat.install_fade_alias()
+        from fade import FadeConfig, TieredKVCache, create_tiered_cache, get_backend  # noqa: F401
+        from fade.cache import TIER_INT4
+        from fade.kernels.fused_int4_attn import fused_int4_sdpa
+        from fade.policy import _assign_one_layer
+        from fade.quant import quant_k_int4
+
+        import fade_b200.attention as att
+        import fade_b200.cache as cache
+        assert TieredKVCache is cache.TieredKVCache and TIER_INT4 == cache.TIER_INT4
+        assert fused_int4_sdpa is att.fused_int4_sdpa
+        assert FadeConfig.safe().n_sink == 4 and callable(_assign_one_layer) and callable(quant_k_int4)
+    finally:
+        compat.uninstall_fade_alias()
+        sys.modules.update(saved)

@@ -206,6 +206,35 @@ def test_checkpoint_roundtrip(cuda_device):
     assert a.storage_bytes() == a.compressed_storage_bytes() - sinks
 
 
+def test_load_reference_checkpoint(cuda_device):
+    """A cache_state_dict written by the reference itself (fade/cache.py:
+    510-559; tests/golden/cache_state_cfg1.pt) loads into fade_b200's cache:
+    the same tiers bit for bit, and the fused decode over them matches the
+    reference's SDPA output."""
+    from conftest import ROOT
+    from fade_b200.cache import TieredKVCache
+
+    sd = torch.load(ROOT / "tests" / "golden" / "cache_state_cfg1.pt", weights_only=True)
+    g = golden("decode_cfg1")
+    cache = TieredKVCache(n_sink=4, recent_window=64, dtype=torch.float16, rope_theta=1e6, head_dim=64)
+    cache.load_cache_state_dict(sd, device=cuda_device)
+    st = cache._layers[0]
+    _eq(st.sink_k, g["sink_k"], "sink_k")
+    _eq(st.fp16_v, g["recent_v"], "recent_v")
+    np.testing.assert_array_equal(st.int4_kq.cpu().numpy(), g["int4_kq"])
+    np.testing.assert_array_equal(st.int4_vq.cpu().numpy(), g["int4_vq"])
+    _eq(st.int4_ks, g["int4_ks"], "int4_ks")
+    _eq(st.int4_vs, g["int4_vs"], "int4_vs")
+    assert cache.get_seq_length(0) == 2048 and st.next_position == 2048
+    out = cache.decode_attention(0, t_from_bits(g["q"], "f16"))
+    assert_attn_close(t_vals(out), t_vals(t_from_bits(g["out_ref32"], "f32")), "f16", TOL["f16"])
+    # and back: our checkpoint of it carries the reference's keys and values
+    sd2 = cache.cache_state_dict()
+    for key, val in sd.items():
+        if key.startswith("layer.") and isinstance(val, torch.Tensor):
+            assert torch.equal(sd2[key].cpu(), val), key
+
+
 def _tiny_llama(dev):
     from transformers import LlamaConfig, LlamaForCausalLM
 

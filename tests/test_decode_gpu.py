@@ -314,3 +314,31 @@ def test_step_host_graph_matches_device_step(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(oh, ref.cpu()), step
     assert host_dec.mid_lengths() == dev_dec.mid_lengths() == [S - 68 + 4] * L
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("Sq,Sk", [(1, 301), (5, 301), (7, 1000)])
+def test_fused_int4_sdpa_dropin(cuda_device, causal, Sq, Sk):
+    """fused_int4_sdpa (fade/kernels/fused_int4_attn.py:277-342): S_q >= 1,
+    GQA, fp16, with the reference kernel's causal mask (query m attends keys
+    0..m) against the oracle's dequant + SDPA with that mask."""
+    from fade_b200.attention import fused_int4_sdpa
+
+    dt = "f16"
+    B, Hq, Hkv, D = 2, 8, 2, 128
+    k = seeded_outliers((B, Hkv, Sk, D), 71, dt)
+    v = seeded_outliers((B, Hkv, Sk, D), 72, dt)
+    kp, ks = oq.quant_k_int4(k, dt)
+    vp, vs = oq.quant_v_int4(v, dt)
+    q = from_bits_dt(np.random.default_rng(73).standard_normal((B, Hq, Sq, D)).astype(np.float32), dt)
+    out = t_vals(fused_int4_sdpa(np_to_dt_tensor(q, dt), torch.from_numpy(kp).cuda(), np_to_dt_tensor(ks, dt),
+                                 torch.from_numpy(vp).cuda(), np_to_dt_tensor(vs, dt), is_causal=causal))
+    kd, vd = oq.dequant_int4(kp, ks, dt), oq.dequant_int4(vp, vs, dt)
+    # The middle tier rounds P to fp16 for the PV product; with a handful of
+    # keys (the first causal rows) single weights dominate and that rounding
+    # reaches 2 output ulps.  The reference's Triton kernel feeds P to tl.dot
+    # in fp32, i.e. TF32 on the tensor cores: the same precision class.
+    for m in range(Sq):
+        n = min(m + 1, Sk) if causal else Sk
+        ref = oa.sdpa(q[:, :, m:m + 1], kd[:, :, :n], vd[:, :, :n])
+        assert_attn_close(out[:, :, m:m + 1], ref, dt, TOL[dt], ulps=2 if n <= 16 else 1)
