@@ -289,6 +289,24 @@ class DecodePlan:
         self.ws_bytes = workspace.numel()
         self.device = dev
 
+    def rebind(self, q: Tensor, out: Tensor | None = None) -> Tensor:
+        """Point the plan at a new query (same shape, dtype and strides) and
+        output tensor; the tiers, workspace and sizes stay.  Returns `out`."""
+        d = self.desc
+        if (tuple(q.shape) != (d.B, d.Hq, d.n_q, d.D) or _lib.dtype_code(q.dtype) != d.dtype
+                or (q.stride(0), q.stride(1), q.stride(2)) != (d.q_sb, d.q_sh, d.q_ss)):
+            raise ValueError("rebind needs a query with the plan's shape, dtype and strides")
+        if out is None:
+            out = torch.empty_like(q, memory_format=torch.contiguous_format)
+        if out.shape != q.shape or out.dtype != q.dtype or out.stride(-1) != 1:
+            raise ValueError("out must match the query's shape and dtype")
+        d.q = q.data_ptr()
+        d.out = out.data_ptr()
+        d.o_sb, d.o_sh, d.o_ss = out.stride(0), out.stride(1), out.stride(2)
+        self._keep[0], self._keep[1] = q, out
+        self.out = out
+        return out
+
     def run(self) -> Tensor:
         lib = _lib.load()
         st = _lib.bind(self.device)

@@ -102,6 +102,10 @@ class LayerState:
     _fp16_buf_v: Tensor | None = None
     _fp16_buf_pos: Tensor | None = None
     _fp16_len: int = 0
+    _fp16_len_dev: Tensor | None = None   # int32 [B] on the device: _fp16_len, for the decode kernel
+    _plan: object = None                  # cached DecodePlan and the tier key it was built for
+    _mid_full: tuple | None = None        # (k codes, v codes, v scales) padded to a multiple of 8
+                                          # tokens; int4_kq/vq/vs are views of their first rows
     _dequant_age: int = 0
     pq_codes: Tensor | None = None
     pq_v_codes: Tensor | None = None
@@ -123,6 +127,20 @@ class LayerState:
 
 def _nbytes(t) -> int:
     return int(t.element_size() * t.numel()) if isinstance(t, Tensor) else 0
+
+
+def _tier_key(t) -> tuple:
+    """Identity of a tier's tensors (addresses, shapes, strides): equal keys
+    mean a DecodePlan built for one describes the other."""
+    out = [type(t).__name__]
+    for name in ("k", "v", "k_packed", "k_scale", "v_packed", "v_scale", "lens", "rotation"):
+        x = getattr(t, name, None)
+        if isinstance(x, torch.Tensor):
+            out.append((name, x.data_ptr(), tuple(x.shape), tuple(x.stride())))
+    for name in ("group", "length", "max_len", "bits"):
+        if hasattr(t, name):
+            out.append((name, getattr(t, name)))
+    return tuple(out)
 
 
 class TieredKVCache(DynamicCache):
@@ -378,6 +396,7 @@ class TieredKVCache(DynamicCache):
         st._fp16_buf_v[:, :, cur:cur + n] = v
         st._fp16_buf_pos[cur:cur + n] = pos
         st._fp16_len = cur + n
+        self._sync_fp16_len(st)
         st.fp16_k = st._fp16_buf_k[:, :, :st._fp16_len]
         st.fp16_v = st._fp16_buf_v[:, :, :st._fp16_len]
         st.fp16_pos = st._fp16_buf_pos[:st._fp16_len]
@@ -483,11 +502,18 @@ class TieredKVCache(DynamicCache):
         D = int(self.head_dim)
         mid, extra = None, []
         if st.int4_kq is not None:
+            n = int(st.int4_kq.shape[-2])
+            full = st._mid_full
+            if full is None or full[0].data_ptr() != st.int4_kq.data_ptr():
+                full = None                # tiers replaced since (e.g. a loaded checkpoint)
             if self.middle_v_bits == 4:
-                mid = Int4Tier(st.int4_kq, st.int4_ks, st.int4_vq, st.int4_vs)
+                if full is not None:       # the padded buffers the tiers are views of: no copy
+                    mid = Int4Tier(full[0], st.int4_ks, full[1], full[2], max_len=n)
+                else:
+                    mid = Int4Tier(st.int4_kq, st.int4_ks, st.int4_vq, st.int4_vs)
             else:
-                n = int(st.int4_pos.shape[0])
-                mid = Int4K2VTier(st.int4_kq, st.int4_ks, _pack_int2_last_dim(st.int4_vq), st.int4_vs,
+                kq = full[0] if full is not None else st.int4_kq
+                mid = Int4K2VTier(kq, st.int4_ks, _pack_int2_last_dim(st.int4_vq), st.int4_vs,
                                   group=self.v_int2_group_size, length=n)
         elif st.backend_k is not None:
             be = self._quant_backend
@@ -516,15 +542,35 @@ class TieredKVCache(DynamicCache):
         if mid is not None:
             tiers.append(mid)
         tiers.extend(extra)
-        if st.fp16_k is not None and st.fp16_k.shape[-2] > 0:
+        if st._fp16_buf_k is not None and st._fp16_len > 0:
+            # the whole buffer with its device fill level: stable across steps
+            tiers.append(FPTier(st._fp16_buf_k, st._fp16_buf_v, lens=st._fp16_len_dev))
+        elif st.fp16_k is not None and st.fp16_k.shape[-2] > 0:
             tiers.append(FPTier(st.fp16_k, st.fp16_v))   # before a reassignment: sinks included
         return tiers
 
     def decode_attention(self, layer_idx: int, query: Tensor, scaling: float | None = None,
                          out: Tensor | None = None) -> Tensor:
         """softmax(q K^T * scaling) V over every retained token of the layer,
-        from the compressed tiers: query [B, Hq, n_q, D] -> [B, Hq, n_q, D]."""
-        return tiered_decode_attention(query, self.decode_tiers(layer_idx), sm_scale=scaling, out=out)
+        from the compressed tiers: query [B, Hq, n_q, D] -> [B, Hq, n_q, D].
+
+        The layer keeps one DecodePlan (descriptor + workspace) between
+        reassignments; a call whose tiers are unchanged only re-points it at
+        the new query and output."""
+        from fade_b200 import attention as att
+
+        st = self._layers[layer_idx]
+        tiers = self.decode_tiers(layer_idx)
+        key = (tuple(query.shape), tuple(query.stride()), query.dtype, scaling, tuple(_tier_key(t) for t in tiers))
+        if st._plan is not None and st._plan[0] == key:
+            plan = st._plan[1]
+            plan.rebind(query, out)
+            return plan.run()
+        dev = query.device
+        plan = att.DecodePlan(query, tiers, out=out, sm_scale=scaling, workspace=att._workspace(dev))
+        att._WS[(dev, torch.cuda.current_stream(dev).cuda_stream)] = plan.workspace
+        st._plan = (key, plan)
+        return plan.run()
 
     # -------------------------------------------------- tier management
     def _rerope(self, k: Tensor, v: Tensor, pos: Tensor, keep_idx: Tensor):
@@ -543,12 +589,28 @@ class TieredKVCache(DynamicCache):
 
     def _quant_int4_tier(self, st: LayerState, k_sub: Tensor, v_sub: Tensor, pos: Tensor) -> None:
         if isinstance(self._quant_backend, SymmetricINT4Backend):
-            st.int4_kq, st.int4_ks = quant_k_int4(k_sub)
-            if self.middle_v_bits == 4:
-                st.int4_vq, st.int4_vs = quant_v_int4(v_sub)
+            # Quantise over the tokens padded with zeros to a multiple of 8 (of
+            # the V group with 2-bit V): every (b, h) segment then starts on a
+            # 128-byte code row and the decode kernel streams these buffers as
+            # they are.  Zero tokens change no per-channel K absmax and get
+            # their own V scales; the stored tiers are views of the first n.
+            n = int(k_sub.shape[-2])
+            mult = 8 if self.middle_v_bits == 4 else self.v_int2_group_size
+            n_pad = -(-n // mult) * mult
+            if n_pad != n:
+                z = k_sub.new_zeros(k_sub.shape[:2] + (n_pad - n, k_sub.shape[-1]))
+                k_pad, v_pad = torch.cat([k_sub, z], dim=-2), torch.cat([v_sub, z], dim=-2)
             else:
-                vp, _ = pad_to_group(v_sub, self.v_int2_group_size)
-                st.int4_vq, st.int4_vs = quant_v_int2(vp, group_size=self.v_int2_group_size)
+                k_pad, v_pad = k_sub, v_sub
+            kq, st.int4_ks = quant_k_int4(k_pad)
+            st.int4_kq = kq[:, :, :n]
+            if self.middle_v_bits == 4:
+                vq, vs = quant_v_int4(v_pad)
+                st.int4_vq, st.int4_vs = vq[:, :, :n], vs[:, :, :n]
+                st._mid_full = (kq, vq, vs)
+            else:
+                st.int4_vq, st.int4_vs = quant_v_int2(v_pad, group_size=self.v_int2_group_size)
+                st._mid_full = (kq, None, None)
             st.int4_pos = pos
             st.backend_k = st.backend_v = st.backend_pos = None
         else:
@@ -565,6 +627,7 @@ class TieredKVCache(DynamicCache):
             st._fp16_buf_v[:, :, :n] = st.fp16_v
             st._fp16_buf_pos[:n] = st.fp16_pos
             st._fp16_len = n
+            self._sync_fp16_len(st)
             st.fp16_k, st.fp16_v = st._fp16_buf_k[:, :, :n], st._fp16_buf_v[:, :, :n]
             st.fp16_pos = st._fp16_buf_pos[:n]
         else:
@@ -575,6 +638,18 @@ class TieredKVCache(DynamicCache):
         st.int4_k_deq = st.int4_v_deq = st.int2_k_deq = st.int2_v_deq = None
         st.pq_k_deq = st.pq_v_deq = None
         st._kernel_mid = st._kernel_extra = None
+        st._plan = None
+
+    @staticmethod
+    def _sync_fp16_len(st: LayerState) -> None:
+        """The recent tier's fill level as a device int32 [B] (the decode
+        kernel reads the fixed-capacity buffer up to it, so one plan serves
+        every step between reassignments)."""
+        B = int(st._fp16_buf_k.shape[0])
+        if st._fp16_len_dev is None or st._fp16_len_dev.numel() != B or \
+                st._fp16_len_dev.device != st._fp16_buf_k.device:
+            st._fp16_len_dev = torch.empty(B, dtype=torch.int32, device=st._fp16_buf_k.device)
+        st._fp16_len_dev.fill_(st._fp16_len)
 
     def apply_tier_assignment(self, layer_idx: int, tiers: Tensor, scores: Tensor | None = None) -> None:
         """Move tokens between tiers (``fade/cache.py:881-1057``): ``tiers``

@@ -256,6 +256,21 @@ def test_hf_decode_fused_matches_sdpa(cuda_device):
     c_fused = create_tiered_cache(m_fused, dtype=torch.bfloat16, n_sink=4, recent_window=64)
     c_ref = create_tiered_cache(m_ref, dtype=torch.bfloat16, n_sink=4, recent_window=64, fused_attention=False)
     assert c_fused.fused_decode and not c_ref.fused_decode
+    # Every fused attention call is also checked on its own, at the north-star
+    # tolerance: against fp32 SDPA over the same cache materialised with the
+    # reference's dequantisation (sink | dequant middle | recent).
+    checked = []
+    fused_call = c_fused.decode_attention
+
+    def checking(layer, query, scaling=None, out=None):
+        res = fused_call(layer, query, scaling=scaling, out=out)
+        K, V = c_fused._materialize(layer)
+        ref = torch.nn.functional.scaled_dot_product_attention(query.float(), K.float(), V.float(),
+                                                               scale=scaling, enable_gqa=True)
+        checked.append(assert_attn_close(t_vals(res), t_vals(ref), "bf16", TOL["bf16"]))
+        return res
+
+    c_fused.decode_attention = checking
     ids = torch.randint(0, 256, (2, 300), generator=torch.Generator().manual_seed(1)).to(dev)
     with torch.no_grad():
         lf = m_fused(input_ids=ids, past_key_values=c_fused, use_cache=True).logits[:, -1]
@@ -274,3 +289,4 @@ def test_hf_decode_fused_matches_sdpa(cuda_device):
             assert err < 0.05 * max(1.0, lr.abs().max().item()), (step, err)
             nxt = lr.argmax(-1, keepdim=True)
     assert c_fused.get_seq_length(0) == c_ref.get_seq_length(0) == 306
+    assert len(checked) == 2 * 6 and max(checked) <= 1.0
