@@ -84,6 +84,8 @@ def parse():
     ap.add_argument("--gather-stream", choices=("inline", "side"), default="side",
                     help="multi-GPU heads partition: all-gather each layer on the compute stream, or on a side "
                          "stream overlapping the next layers")
+    ap.add_argument("--reassign", action="store_true",
+                    help="time the tier-reassignment kernels (quantisers, rotation, re-RoPE, dequant) instead")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="layers per step (profiling captures use 1)")
@@ -818,6 +820,78 @@ def run_rot(args):
     print(json.dumps(_fixed_tier_line(args, ms, clocks, hot, layer_bytes, extra, 3 * L)), flush=True)
 
 
+# --------------------------------------------------------------------------
+# reassignment-time kernels (run on tier reassignment, not per decode step)
+# --------------------------------------------------------------------------
+def run_reassign(args):
+    """Each reassignment kernel on inputs larger than L2, CUDA-event timed
+    over --steps calls after --warmup: microseconds per call and achieved
+    GB/s of its algorithmic bytes (every input read once, every output written
+    once) against the measured HBM copy bandwidth.  Shapes: configuration 2's
+    middle (16 x 8 x 8124 x 128, bf16) for the quantisers and the dequant;
+    configuration 3's eviction (8 x 8 x 4096 -> 468 survivors, fp16; batch
+    scaled x8 so the inputs exceed L2) for the re-RoPE gather."""
+    import torch
+
+    from fade_b200.quant import dequant_int4, quant_int2_grouped_packed, quant_k_int4, quant_v_int4
+    from fade_b200.rope import Vanilla
+    from fade_b200.rope_kernels import rerope_gather
+    from fade_b200.rotated_quant import _random_orthogonal, rotated_quant_k, rotated_quant_v
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(9)
+    B, H, S, D = 16, 8, 8124, 128
+    x = torch.randn(B, H, S, D, device=dev, generator=gen).to(torch.bfloat16)
+    n = x.numel()
+    R = _random_orthogonal(D, 42).to(dev)
+    kp, ks = quant_k_int4(x)
+    vp, vs = quant_v_int4(x)
+    S3, keep_n, B3 = 4096, 468, 64
+    k3 = torch.randn(B3, 8, S3, D, device=dev, generator=gen).to(torch.float16)
+    v3 = torch.randn_like(k3)
+    keep = torch.sort(torch.randperm(S3, device=dev, generator=gen)[:keep_n]).values
+    sc = Vanilla(theta=1e6, head_dim=D)
+    co, so = sc.compute_cos_sin(torch.arange(S3, device=dev), dev, model_dtype=torch.float16)
+    cn, sn = sc.compute_cos_sin(torch.arange(keep_n, device=dev), dev, model_dtype=torch.float16)
+    co, so, cn, sn = (t.reshape(-1, D).contiguous() for t in (co, so, cn, sn))
+    n3 = B3 * 8 * keep_n * D
+    cases = [
+        ("quant_int4_k (per-channel over S, pack)", lambda: quant_k_int4(x), n * 2 + n // 2 + B * H * D * 2),
+        ("quant_int4_v (per-token, pack)", lambda: quant_v_int4(x), n * 2 + n // 2 + B * H * S * 2),
+        ("quant_int2_grouped G=32 (4 codes per byte)", lambda: quant_int2_grouped_packed(x[:, :, :8096], 32),
+         (n * 8096 // S) * 2 + (n * 8096 // S) // 4 + B * H * (8096 // 32) * D * 2),
+        ("rotated_quant_k 2-bit (x R^T, per-channel)", lambda: rotated_quant_k(x, R, bits=2),
+         n * 2 + n // 4 + B * H * D * 2),
+        ("rotated_quant_v 2-bit (x R^T, per-token)", lambda: rotated_quant_v(x, R, bits=2),
+         n * 2 + n // 4 + B * H * S * 2),
+        ("dequant_int4 (K, per-channel scale)", lambda: dequant_int4(kp, ks, dtype=torch.bfloat16),
+         n // 2 + B * H * D * 2 + n * 2),
+        ("rerope_gather (un-RoPE + re-RoPE + gather K, gather V)",
+         lambda: rerope_gather(k3, v3, keep, co, so, cn, sn), 4 * n3 * 2 + (S3 + keep_n) * D * 4 * 2),
+    ]
+    peaks = _measured_peaks()
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    res = []
+    for name, fn, nbytes in cases:
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) / args.steps * 1e3
+        gbs = nbytes / (us / 1e6) / 1e9
+        res.append({"kernel": name, "us_per_call": round(us, 2), "algorithmic_bytes": int(nbytes),
+                    "achieved_gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 3)})
+    print(json.dumps({"reassignment_kernels": res, "peak_gbs": peak,
+                      "note": "per call; each call allocates its outputs through torch (cached allocator)"}),
+          flush=True)
+
+
 def run_fade(args, ws, rank, local):
     kind = CFG["kind"]
     if kind == "int4":
@@ -841,7 +915,9 @@ def main():
         else:
             dist.init_process_group("gloo")
     try:
-        if args.impl == "reference":
+        if args.reassign:
+            run_reassign(args)
+        elif args.impl == "reference":
             run_reference(args, ws, rank)
         else:
             run_fade(args, ws, rank, local)

@@ -82,7 +82,17 @@ quant_int4_k_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, in
 #pragma unroll
     for (int i = 0; i < E; ++i) amax[i] = 0.f;
     if (active) {
-        for (int64_t s = slot; s < v.S; s += rows_per_iter) {
+        int64_t s = slot;
+        for (; s + 3 * rows_per_iter < v.S; s += 4 * rows_per_iter) {   // four rows in flight
+            float e[4][E];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) load_elems<DT, E>(xb + (s + u * rows_per_iter) * v.ss, v.sd, vec, e[u]);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int i = 0; i < E; ++i) amax[i] = fmaxf(amax[i], fabsf(e[u][i]));
+        }
+        for (; s < v.S; s += rows_per_iter) {
             float e[E];
             load_elems<DT, E>(xb + s * v.ss, v.sd, vec, e);
 #pragma unroll
@@ -113,7 +123,20 @@ quant_int4_k_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, in
 #pragma unroll
     for (int i = 0; i < E; ++i) inv[i] = s_inv[dg - d_lo + i];
     uint8_t* pb = packed + (int64_t)z * v.S * (D / 2) + dg / 2;
-    for (int64_t s = slot; s < v.S; s += rows_per_iter) {
+    int64_t s = slot;
+    for (; s + 3 * rows_per_iter < v.S; s += 4 * rows_per_iter) {   // four rows in flight
+        float e[4][E];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) load_elems<DT, E>(xb + (s + u * rows_per_iter) * v.ss, v.sd, vec, e[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            int q[E];
+#pragma unroll
+            for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[u][i], inv[i])), -8.f, 7.f);
+            store_int4<E>(pb + (s + u * rows_per_iter) * (D / 2), q);
+        }
+    }
+    for (; s < v.S; s += rows_per_iter) {
         float e[E];
         load_elems<DT, E>(xb + s * v.ss, v.sd, vec, e);
         int q[E];
@@ -132,33 +155,46 @@ __global__ void __launch_bounds__(kQuantThreads)
 quant_int4_v_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, int tpr_pow2,
                     uint8_t* __restrict__ packed, typename Elem<DT>::T* __restrict__ scale,
                     bool vec) {
+    constexpr int U = 4;       // rows in flight per thread (loads issued before any math)
     const int D = (int)v.D;
     const int tpr = tpr_pow2;  // power of two >= D / E, <= 32
+    const int rows_per_cta = kQuantThreads / tpr;
     const int64_t rows = v.B * v.H * v.S;
-    const int64_t row = (int64_t)blockIdx.x * (kQuantThreads / tpr) + threadIdx.x / tpr;
     const int lane_in_row = threadIdx.x % tpr;
-    const bool active = row < rows;
     const bool has_elems = lane_in_row * E < D;
-    float e[E];
-    float m = 0.f;
-    if (active && has_elems) {
-        const int64_t s = row % v.S, bh = row / v.S;
-        const int64_t b = bh / v.H, h = bh % v.H;
-        load_elems<DT, E>(x + b * v.sb + h * v.sh + s * v.ss + (int64_t)lane_in_row * E * v.sd,
-                          v.sd, vec, e);
+    const int64_t step = (int64_t)gridDim.x * rows_per_cta;
+    for (int64_t base = (int64_t)blockIdx.x * rows_per_cta + threadIdx.x / tpr; base < rows; base += U * step) {
+        float e[U][E];
 #pragma unroll
-        for (int i = 0; i < E; ++i) m = fmaxf(m, fabsf(e[i]));
+        for (int u = 0; u < U; ++u) {
+            const int64_t row = base + u * step;
+#pragma unroll
+            for (int i = 0; i < E; ++i) e[u][i] = 0.f;
+            if (row < rows && has_elems) {
+                const int64_t s = row % v.S, bh = row / v.S;
+                const int64_t b = bh / v.H, h = bh % v.H;
+                load_elems<DT, E>(x + b * v.sb + h * v.sh + s * v.ss + (int64_t)lane_in_row * E * v.sd,
+                                  v.sd, vec, e[u]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t row = base + u * step;
+            float m = 0.f;
+#pragma unroll
+            for (int i = 0; i < E; ++i) m = fmaxf(m, fabsf(e[u][i]));
+            for (int off = tpr / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            if (row >= rows) continue;
+            m = fmaxf(m, Elem<DT>::eps());
+            const float inv = inv_scale<DT>(m, 7.f);
+            if (lane_in_row == 0) scale[row] = Elem<DT>::from_f(Elem<DT>::rnd(__fdiv_rn(m, 7.f)));
+            if (!has_elems) continue;
+            int q[E];
+#pragma unroll
+            for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[u][i], inv)), -8.f, 7.f);
+            store_int4<E>(packed + row * (D / 2) + lane_in_row * (E / 2), q);
+        }
     }
-    for (int off = tpr / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if (!active) return;
-    m = fmaxf(m, Elem<DT>::eps());
-    const float inv = inv_scale<DT>(m, 7.f);
-    if (lane_in_row == 0) scale[row] = Elem<DT>::from_f(Elem<DT>::rnd(__fdiv_rn(m, 7.f)));
-    if (!has_elems) return;
-    int q[E];
-#pragma unroll
-    for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[i], inv)), -8.f, 7.f);
-    store_int4<E>(packed + row * (D / 2) + lane_in_row * (E / 2), q);
 }
 
 // ---------------------------------------------------------------------------
@@ -298,6 +334,48 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ codes, int bits,
     }
 }
 
+// INT4 with per-channel (mode 0) or per-token (mode 1) scales, D % 8 == 0:
+// one thread per 8 codes (one 32-bit code word -> one 16-byte store for
+// 16-bit dtypes), grid-stride.  Same rounding as dequant_kernel.
+template <int DT>
+__global__ void dequant_int4_vec_kernel(const uint32_t* __restrict__ codes,
+                                        const typename Elem<DT>::T* __restrict__ scale, int scale_mode,
+                                        int64_t S, int D, int64_t n8, typename Elem<DT>::T* __restrict__ out) {
+    using T = typename Elem<DT>::T;
+    const int w_per_row = D / 8;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / w_per_row;
+        const int d0 = (int)(i - row * w_per_row) * 8;
+        const uint32_t w = codes[i];
+        float sc[8];
+        if (scale_mode == 0) {
+            const T* sp = scale + (row / S) * D + d0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sc[j] = Elem<DT>::to_f(sp[j]);
+        } else {
+            const float s1 = Elem<DT>::to_f(scale[row]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sc[j] = s1;
+        }
+        T o[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t byte = (w >> (8 * j)) & 0xFFu;
+            const int hi = (int)((byte >> 4) & 7u) - (int)(byte & 0x80u ? 8 : 0);
+            const int lo = (int)(byte & 7u) - (int)(byte & 0x8u ? 8 : 0);
+            o[2 * j] = Elem<DT>::from_f(__fmul_rn((float)hi, sc[2 * j]));
+            o[2 * j + 1] = Elem<DT>::from_f(__fmul_rn((float)lo, sc[2 * j + 1]));
+        }
+        T* dst = out + i * 8;
+        if constexpr (sizeof(T) == 2) {
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(o);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst[j] = o[j];
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Age-out: the oldest recent-ring token of every (b, h) joins the INT4 middle;
 // the new token takes its ring slot.  One CTA per batch row b, one warp per
@@ -399,7 +477,7 @@ static int launch_quant_k(const void* x, const fade_view4& v, uint8_t* packed, v
     const int E = e8 ? 8 : 2;
     int dims_per_cta = (int)(v.D < 256 ? v.D : 256);
     // For few (b,h) pairs, split channels across CTAs to fill the machine.
-    while (Z * (v.D / dims_per_cta) < 148 && dims_per_cta > 8 * E && dims_per_cta % (2 * E) == 0 &&
+    while (Z * (v.D / dims_per_cta) < 148 * 8 && dims_per_cta > 2 * E && dims_per_cta % (2 * E) == 0 &&
            (dims_per_cta / 2) % E == 0 && v.D % (dims_per_cta / 2) == 0)
         dims_per_cta /= 2;
     dim3 grid((unsigned)Z, (unsigned)((v.D + dims_per_cta - 1) / dims_per_cta));
@@ -425,7 +503,9 @@ static int launch_quant_v(const void* x, const fade_view4& v, uint8_t* packed, v
     while (tpr * E < v.D) tpr *= 2;
     if (tpr > 32) return FADE_ERR_UNSUPPORTED;
     const int rows_per_cta = kQuantThreads / tpr;
-    const unsigned grid = (unsigned)((rows + rows_per_cta - 1) / rows_per_cta);
+    int64_t g = (rows + rows_per_cta - 1) / rows_per_cta;
+    if (g > 148 * 8) g = 148 * 8;   // resident grid; each thread keeps 4 rows in flight
+    const unsigned grid = (unsigned)g;
     if (E == 8)
         quant_int4_v_kernel<DT, 8><<<grid, kQuantThreads, 0, st>>>(
             (const T*)x, v, tpr, packed, (T*)scale, can_vec(x, v, sizeof(T)));
@@ -552,6 +632,22 @@ extern "C" int fade_dequant(const void* codes, int bits, const void* scale, int 
     if (!codes || !scale || !out) return FADE_ERR_INVALID_ARG;
     const auto* c = reinterpret_cast<const uint8_t*>(codes);
     cudaStream_t st = as_stream(stream);
+    if (bits == 4 && scale_mode != 2 && D % 8 == 0 && dtype != FADE_F32 &&
+        reinterpret_cast<uintptr_t>(codes) % 4 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+        const int64_t n8 = n / 8;
+        int64_t g = (n8 + 255) / 256;
+        if (g > 148 * 16) g = 148 * 16;
+        if (dtype == FADE_F16)
+            dequant_int4_vec_kernel<FADE_F16><<<(unsigned)g, 256, 0, st>>>(
+                reinterpret_cast<const uint32_t*>(codes), (const __half*)scale, scale_mode, S, (int)D, n8,
+                (__half*)out);
+        else
+            dequant_int4_vec_kernel<FADE_BF16><<<(unsigned)g, 256, 0, st>>>(
+                reinterpret_cast<const uint32_t*>(codes), (const __nv_bfloat16*)scale, scale_mode, S, (int)D, n8,
+                (__nv_bfloat16*)out);
+        FADE_LAUNCH_CHECK();
+        return FADE_OK;
+    }
     switch (dtype) {
         case FADE_F16:
             dequant_kernel<FADE_F16><<<ew_grid(n), 256, 0, st>>>(

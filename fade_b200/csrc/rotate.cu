@@ -9,16 +9,60 @@
 
 namespace fade {
 
-constexpr int kRotTokens = 32;   // tokens per CTA
+constexpr int kRotTokens = 64;   // tokens per CTA
+constexpr int kRotAcc = 32;      // tokens per thread: independent accumulation chains
 constexpr int kRotThreads = 256;
+
+// y[t][d] = sum_e in[t][e] * M[e][d] for the kRotTokens tokens of a tile,
+// each output summed in e order with separately rounded products and sums.
+// Thread (d, g) computes channel d of kRotTokens / (blockDim.x / D) tokens:
+// that many independent chains, inputs read four channels at a time (one
+// broadcast 16-byte load).  DC > 0 fixes D at compile time (no predication);
+// DC == 0 is the generic form.  `y` may alias `in`: the results are written
+// after a block-wide barrier.
+template <int DC>
+__device__ __forceinline__ void rot_matmul(const float* in, const float* __restrict__ M, float* y, int D_rt) {
+    const int D = DC > 0 ? DC : D_rt;
+    const int groups = blockDim.x / D;                          // >= 2 for D <= 128
+    const int tpg = (kRotTokens + groups - 1) / groups;         // <= kRotAcc
+    const int d = threadIdx.x % D, t0 = (threadIdx.x / D) * tpg;
+    const bool on = threadIdx.x < groups * D;
+    const int nj = !on ? 0 : ((kRotTokens - t0) < tpg ? (kRotTokens - t0) : tpg);
+    constexpr int NJ = DC > 0 ? kRotTokens / (256 / (DC > 0 ? DC : 1)) : kRotAcc;
+    float acc[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) acc[j] = 0.f;
+    if (on) {
+        for (int e = 0; e < D; e += 4) {
+            const float m0 = M[e * D + d], m1 = M[(e + 1) * D + d], m2 = M[(e + 2) * D + d],
+                        m3 = M[(e + 3) * D + d];
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                if (DC > 0 || j < nj) {
+                    const float4 x = *reinterpret_cast<const float4*>(in + (t0 + j) * D + e);
+                    float a = acc[j];
+                    a = __fadd_rn(a, __fmul_rn(x.x, m0));
+                    a = __fadd_rn(a, __fmul_rn(x.y, m1));
+                    a = __fadd_rn(a, __fmul_rn(x.z, m2));
+                    a = __fadd_rn(a, __fmul_rn(x.w, m3));
+                    acc[j] = a;
+                }
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+        if (DC > 0 || j < nj) y[(t0 + j) * D + d] = acc[j];
+}
 
 __device__ __forceinline__ void qrange(int bits, float& lo, float& hi) {
     lo = (float)(-(1 << (bits - 1)));
     hi = (float)((1 << (bits - 1)) - 1);
 }
 
-// Rotate kRotTokens rows of (b,h) into xs (fp32 [kRotTokens][D]).
-template <int DT>
+// Rotate kRotTokens rows of (b,h) into xs (fp32 [kRotTokens][D]; xs may be xin).
+template <int DT, int DC>
 __device__ void rotate_tile(const typename Elem<DT>::T* __restrict__ x, const fade_view4& v, int64_t b,
                             int64_t h, int64_t t0, int nt, const float* __restrict__ Rt, float* xin,
                             float* xs) {
@@ -28,18 +72,13 @@ __device__ void rotate_tile(const typename Elem<DT>::T* __restrict__ x, const fa
         xin[i] = (t < nt) ? Elem<DT>::to_f(x[b * v.sb + h * v.sh + (t0 + t) * v.ss + (int64_t)e * v.sd]) : 0.f;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < kRotTokens * D; i += blockDim.x) {
-        const int t = i / D, d = i % D;
-        float acc = 0.f;
-        for (int e = 0; e < D; ++e) acc = __fadd_rn(acc, __fmul_rn(xin[t * D + e], Rt[e * D + d]));
-        xs[i] = acc;
-    }
+    rot_matmul<DC>(xin, Rt, xs, D);
     __syncthreads();
 }
 
 // pass 0 (K only): per-channel absmax of x_rot into amax (float bits, atomicMax).
 // pass 1: quantise.  kind 0 = K (per-channel scale from amax), 1 = V (per-token).
-template <int DT>
+template <int DT, int DC>
 __global__ void __launch_bounds__(kRotThreads)
 rotated_quant_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, const float* __restrict__ R,
                      int bits, int kind, int pass, float* __restrict__ amax, uint8_t* __restrict__ packed,
@@ -48,8 +87,8 @@ rotated_quant_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, c
     const int D = (int)v.D;
     float* Rt = sm;                    // [D][D] transposed: Rt[e][d] = R[d][e]
     float* xin = Rt + D * D;           // [kRotTokens][D]
-    float* xs = xin + kRotTokens * D;  // [kRotTokens][D]
-    float* tsc = xs + kRotTokens * D;  // [kRotTokens] per-token inv
+    float* xs = xin;                   // the rotation is written over its input
+    float* tsc = xin + kRotTokens * D; // [kRotTokens] per-token inv
     const int64_t tiles = (v.S + kRotTokens - 1) / kRotTokens;
     const int64_t bh = blockIdx.x / tiles, tile = blockIdx.x % tiles;
     const int64_t b = bh / v.H, h = bh % v.H;
@@ -60,7 +99,7 @@ rotated_quant_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, c
         Rt[e * D + d] = R[i];
     }
     __syncthreads();
-    rotate_tile<DT>(x, v, b, h, t0, nt, Rt, xin, xs);
+    rotate_tile<DT, DC>(x, v, b, h, t0, nt, Rt, xin, xs);
     float lo, hi;
     qrange(bits, lo, hi);
     if (kind == 0 && pass == 0) {
@@ -124,7 +163,7 @@ __device__ __forceinline__ int unpack_code(const uint8_t* __restrict__ p, int bi
 }
 
 // out = rnd_dt( sum_e rnd_dt(q*scale)[e] * R[e][d] )
-template <int DT>
+template <int DT, int DC>
 __global__ void __launch_bounds__(kRotThreads)
 rotated_dequant_kernel(const uint8_t* __restrict__ packed, int bits, const typename Elem<DT>::T* __restrict__ scale,
                        int scale_mode, const float* __restrict__ R, int64_t H, int64_t S, int D,
@@ -148,17 +187,66 @@ rotated_dequant_kernel(const uint8_t* __restrict__ packed, int bits, const typen
         xs[i] = val;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < nt * D; i += blockDim.x) {
-        const int t = i / D, d = i % D;
-        float acc = 0.f;
-        for (int e = 0; e < D; ++e) acc = __fadd_rn(acc, __fmul_rn(xs[t * D + e], Rs[e * D + d]));
-        out[(bh * S + t0 + t) * D + d] = Elem<DT>::from_f(acc);
-    }
+    rot_matmul<DC>(xs, Rs, xs, D);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * D; i += blockDim.x)
+        out[(bh * S + t0) * D + i] = Elem<DT>::from_f(xs[i]);
 }
 
 }  // namespace fade
 
 using namespace fade;
+
+namespace fade {
+
+template <int DT, int DC>
+static int launch_rotated_quant(const void* x, fade_view4 xv, const float* R, int bits, int kind, float* amax,
+                                size_t need, uint8_t* packed, void* scale, size_t smem, unsigned grid,
+                                cudaStream_t st) {
+    using T = typename Elem<DT>::T;
+    auto k = rotated_quant_kernel<DT, DC>;
+    FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (kind == 0) {   // pass 0: per-channel absmax of the rotated values
+        FADE_CUDA_TRY(cudaMemsetAsync(amax, 0, need, st));
+        k<<<grid, kRotThreads, smem, st>>>((const T*)x, xv, R, bits, kind, 0, amax, packed, (T*)scale);
+        FADE_LAUNCH_CHECK();
+    }
+    k<<<grid, kRotThreads, smem, st>>>((const T*)x, xv, R, bits, kind, 1, amax, packed, (T*)scale);
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}
+
+template <int DT>
+static int rotated_quant_d(int D, const void* x, fade_view4 xv, const float* R, int bits, int kind, float* amax,
+                           size_t need, uint8_t* packed, void* scale, size_t smem, unsigned grid, cudaStream_t st) {
+    if (D == 128) return launch_rotated_quant<DT, 128>(x, xv, R, bits, kind, amax, need, packed, scale, smem, grid, st);
+    if (D == 64) return launch_rotated_quant<DT, 64>(x, xv, R, bits, kind, amax, need, packed, scale, smem, grid, st);
+    return launch_rotated_quant<DT, 0>(x, xv, R, bits, kind, amax, need, packed, scale, smem, grid, st);
+}
+
+template <int DT, int DC>
+static int launch_rotated_dequant(const uint8_t* packed, int bits, const void* scale, int scale_mode,
+                                  const float* R, int64_t H, int64_t S, int D, void* out, size_t smem,
+                                  unsigned grid, cudaStream_t st) {
+    using T = typename Elem<DT>::T;
+    auto k = rotated_dequant_kernel<DT, DC>;
+    FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<grid, kRotThreads, smem, st>>>(packed, bits, (const T*)scale, scale_mode, R, H, S, D, (T*)out);
+    FADE_LAUNCH_CHECK();
+    return FADE_OK;
+}
+
+template <int DT>
+static int rotated_dequant_d(const uint8_t* packed, int bits, const void* scale, int scale_mode, const float* R,
+                             int64_t H, int64_t S, int D, void* out, size_t smem, unsigned grid, cudaStream_t st) {
+    if (D == 128)
+        return launch_rotated_dequant<DT, 128>(packed, bits, scale, scale_mode, R, H, S, D, out, smem, grid, st);
+    if (D == 64)
+        return launch_rotated_dequant<DT, 64>(packed, bits, scale, scale_mode, R, H, S, D, out, smem, grid, st);
+    return launch_rotated_dequant<DT, 0>(packed, bits, scale, scale_mode, R, H, S, D, out, smem, grid, st);
+}
+
+}  // namespace fade
 
 extern "C" int fade_rotated_quant(const void* x, int dtype, fade_view4 xv, const float* R, int bits,
                                   int kind, uint8_t* packed, void* scale, void* workspace,
@@ -167,7 +255,7 @@ extern "C" int fade_rotated_quant(const void* x, int dtype, fade_view4 xv, const
     if (bits != 2 && bits != 3 && bits != 4) return FADE_ERR_INVALID_ARG;
     if (kind != 0 && kind != 1) return FADE_ERR_INVALID_ARG;
     if ((bits == 4 && xv.D % 2) || (bits == 2 && xv.D % 4)) return FADE_ERR_ODD_DIM;
-    if (xv.D > 128) return FADE_ERR_UNSUPPORTED;
+    if (xv.D > 128 || xv.D % 4) return FADE_ERR_UNSUPPORTED;
     const int64_t Z = xv.B * xv.H;
     if (Z == 0 || xv.S == 0) return FADE_OK;
     if (!x || !R || !packed || !scale) return FADE_ERR_INVALID_ARG;
@@ -175,50 +263,17 @@ extern "C" int fade_rotated_quant(const void* x, int dtype, fade_view4 xv, const
     if (kind == 0 && (!workspace || ws_bytes < need)) return FADE_ERR_WORKSPACE;
     cudaStream_t st = as_stream(stream);
     const int D = (int)xv.D;
-    const size_t smem = ((size_t)D * D + 2 * kRotTokens * D + kRotTokens) * 4;
+    // R (transposed) + one token tile, rotated in place + per-token scales
+    const size_t smem = ((size_t)D * D + kRotTokens * D + kRotTokens) * 4;
     const int64_t tiles = (xv.S + kRotTokens - 1) / kRotTokens;
     const unsigned grid = (unsigned)(Z * tiles);
     float* amax = reinterpret_cast<float*>(workspace);
     switch (dtype) {
-        case FADE_F16: {
-            auto k = rotated_quant_kernel<FADE_F16>;
-            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            if (kind == 0) {
-                FADE_CUDA_TRY(cudaMemsetAsync(amax, 0, need, st));
-                k<<<grid, kRotThreads, smem, st>>>((const __half*)x, xv, R, bits, kind, 0, amax, packed, (__half*)scale);
-                FADE_LAUNCH_CHECK();
-            }
-            k<<<grid, kRotThreads, smem, st>>>((const __half*)x, xv, R, bits, kind, 1, amax, packed, (__half*)scale);
-            break;
-        }
-        case FADE_BF16: {
-            auto k = rotated_quant_kernel<FADE_BF16>;
-            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            if (kind == 0) {
-                FADE_CUDA_TRY(cudaMemsetAsync(amax, 0, need, st));
-                k<<<grid, kRotThreads, smem, st>>>((const __nv_bfloat16*)x, xv, R, bits, kind, 0, amax, packed,
-                                                   (__nv_bfloat16*)scale);
-                FADE_LAUNCH_CHECK();
-            }
-            k<<<grid, kRotThreads, smem, st>>>((const __nv_bfloat16*)x, xv, R, bits, kind, 1, amax, packed,
-                                               (__nv_bfloat16*)scale);
-            break;
-        }
-        case FADE_F32: {
-            auto k = rotated_quant_kernel<FADE_F32>;
-            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            if (kind == 0) {
-                FADE_CUDA_TRY(cudaMemsetAsync(amax, 0, need, st));
-                k<<<grid, kRotThreads, smem, st>>>((const float*)x, xv, R, bits, kind, 0, amax, packed, (float*)scale);
-                FADE_LAUNCH_CHECK();
-            }
-            k<<<grid, kRotThreads, smem, st>>>((const float*)x, xv, R, bits, kind, 1, amax, packed, (float*)scale);
-            break;
-        }
+        case FADE_F16: return rotated_quant_d<FADE_F16>(D, x, xv, R, bits, kind, amax, need, packed, scale, smem, grid, st);
+        case FADE_BF16: return rotated_quant_d<FADE_BF16>(D, x, xv, R, bits, kind, amax, need, packed, scale, smem, grid, st);
+        case FADE_F32: return rotated_quant_d<FADE_F32>(D, x, xv, R, bits, kind, amax, need, packed, scale, smem, grid, st);
         default: return FADE_ERR_INVALID_ARG;
     }
-    FADE_LAUNCH_CHECK();
-    return FADE_OK;
 }
 
 extern "C" int fade_rotated_dequant(const uint8_t* packed, int bits, const void* scale, int scale_mode,
@@ -227,38 +282,18 @@ extern "C" int fade_rotated_dequant(const uint8_t* packed, int bits, const void*
     if (B < 0 || H < 0 || S < 0 || D <= 0) return FADE_ERR_INVALID_ARG;
     if (bits != 2 && bits != 3 && bits != 4) return FADE_ERR_INVALID_ARG;
     if (scale_mode != 0 && scale_mode != 1) return FADE_ERR_INVALID_ARG;
-    if (D > 128) return FADE_ERR_UNSUPPORTED;
+    if (D > 128 || D % 4) return FADE_ERR_UNSUPPORTED;
     const int64_t Z = B * H;
     if (Z == 0 || S == 0) return FADE_OK;
     if (!packed || !scale || !R || !out) return FADE_ERR_INVALID_ARG;
-    const size_t smem = ((size_t)D * D + kRotTokens * D) * 4;
+    const size_t smem = ((size_t)D * D + kRotTokens * D) * 4;   // R + one tile, rotated in place
     const int64_t tiles = (S + kRotTokens - 1) / kRotTokens;
     const unsigned grid = (unsigned)(Z * tiles);
     cudaStream_t st = as_stream(stream);
     switch (dtype) {
-        case FADE_F16: {
-            auto k = rotated_dequant_kernel<FADE_F16>;
-            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            k<<<grid, kRotThreads, smem, st>>>(packed, bits, (const __half*)scale, scale_mode, R, H, S, (int)D,
-                                               (__half*)out);
-            break;
-        }
-        case FADE_BF16: {
-            auto k = rotated_dequant_kernel<FADE_BF16>;
-            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            k<<<grid, kRotThreads, smem, st>>>(packed, bits, (const __nv_bfloat16*)scale, scale_mode, R, H, S,
-                                               (int)D, (__nv_bfloat16*)out);
-            break;
-        }
-        case FADE_F32: {
-            auto k = rotated_dequant_kernel<FADE_F32>;
-            FADE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            k<<<grid, kRotThreads, smem, st>>>(packed, bits, (const float*)scale, scale_mode, R, H, S, (int)D,
-                                               (float*)out);
-            break;
-        }
+        case FADE_F16: return rotated_dequant_d<FADE_F16>(packed, bits, scale, scale_mode, R, H, S, (int)D, out, smem, grid, st);
+        case FADE_BF16: return rotated_dequant_d<FADE_BF16>(packed, bits, scale, scale_mode, R, H, S, (int)D, out, smem, grid, st);
+        case FADE_F32: return rotated_dequant_d<FADE_F32>(packed, bits, scale, scale_mode, R, H, S, (int)D, out, smem, grid, st);
         default: return FADE_ERR_INVALID_ARG;
     }
-    FADE_LAUNCH_CHECK();
-    return FADE_OK;
 }
