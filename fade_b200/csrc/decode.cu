@@ -8,37 +8,44 @@
 // merged: the token order of the reference's cat() does not matter.
 //
 // Launch sequence (one stream, chained with programmatic dependent launch):
-//   k0  rotate_queries   (only with a rotated tier): q_rot = q @ R^T, fp32.
-//   k1  middle_kernel    persistent stream-K over the quantised middle; every
-//                        CTA stores one un-normalised partial per (b, kv-head)
-//                        row it touched (plain stores: no fences, counters or
-//                        waits between CTAs).
-//   k2  finish_kernel    one CTA per (b, kv-head): attention over the FP
-//                        sink/recent tiers while k1 drains, then (after k1
-//                        completes) the merge of that partial with the row's
-//                        middle partials -> `out`.
-//
-// k1 data path per CTA (5 warps):
-//   warp 4 (producer): 2-D TMA (cp.async.bulk.tensor, no multicast) of 128
-//     token rows of packed K and V codes into a 4-stage ring, swizzled so the
-//     ldmatrix reads below are bank-conflict free; it also stages the V scales
-//     (normalised per 32-token slice) with plain loads.  mbarrier full/empty.
-//   warps 0-3 (consumers): each owns 32 tokens of a stage.
-//     S^T[16 tok x 8 rows] = K_codes[16 x D] . (q*k_scale/qn)^T   (mma.sync
-//       m16n8k16 f16 -> f32; the GQA query rows of one kv head are the N dim)
-//     codes are turned into exact fp16 integers in registers with the
-//     magic-exponent trick (LUT-free int4 -> fp16 conversion, as used in
-//     FasterTransformer's mixed-precision GEMMs): (x & mask) ^ (0x6400|sign)
-//     makes 1024 + u (or 1024 + 16u), one HADD2 removes the bias.
-//     online softmax in log2 space; P (fp16, V scale folded in) is transposed
-//     with movmatrix and O^T[D x 8] += V_codes^T . P^T (mma.sync again).
-//   The channel order inside a thread is permuted to match the packed layout;
-//   q fragments are built with the same permutation, so nothing is shuffled.
+//   k0  rotate_queries   (only with a rotated tier): q_rot = q @ R^T in fp32,
+//                        16 query rows per CTA, R staged in shared memory.
+//   k1  middle_kernel    one persistent CTA per SM, 16 warps:
+//       * 3 consumer groups x 4 warps.  The CTA owns a contiguous range of
+//         128-token units of the quantised middle (stream-K over all (b, kv-
+//         head) rows); group g takes units g, g+3, ... of it.
+//       * 3 producer warps (one per group): 2-D TMA (cp.async.bulk.tensor, no
+//         multicast) of 128-byte swizzled rows of packed K and V codes, plus V
+//         scales, into a ring of up to 12 stages with full/empty mbarriers.
+//         With `early` (prefetch_tiers) they stream before the grid
+//         dependency resolves.
+//       * consumer warp = 32 tokens of a stage: ldmatrix -> exact code
+//         conversion (shift + lop3 magic exponent, the LUT-free int4 -> half
+//         conversion of FasterTransformer's mixed-precision GEMMs, then one
+//         packed subtract) -> packed multiply by the scale, which rounds each
+//         element exactly like the reference's rnd(q * scale) -> mma.sync
+//         m16n8k16 in the model dtype (the GQA query rows are N) -> online
+//         softmax in log2 space with lazy maxima -> movmatrix transposes P ->
+//         O^T += V^T P^T.  2-bit rotated codes fold their scales exactly
+//         (c * s is representable) into q and P.  At a row boundary the
+//         group's 4 warps combine in shared memory in a fixed order and store
+//         one partial (plain stores: no fences, counters or waits between CTAs).
+//       * one FP-tier warp: attention over the sink / recent tokens of its rows
+//         (all of them staged with one cp.async pass), P split hi + lo; with
+//         the fused age-out it quantises the oldest ring token into the middle,
+//         attends its INT4 round trip and the new token, and writes the new
+//         token into the ring.
+//       * every mbarrier wait is bounded; a stalled pipeline sets the
+//         workspace error word (fade_workspace_check) instead of hanging.
+//   k2  finish_kernel    one CTA per (b, kv-head), after the middle grid: merge
+//                        of the FP partial with the row's middle partials (the
+//                        rotation R applied back for rotated tiers), normalise,
+//                        write `out`, advance the age-out lengths.  Without a
+//                        quantised tier it computes the FP tiers itself.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <cstdio>
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -46,55 +53,13 @@
 
 namespace fade {
 
-// Ablation switch for profiling builds only (default 0 = full kernel):
-// 1 = consumers only cycle the pipeline, 2 = QK^T only, 3 = no scale multiply,
-// 4 = as 1 without the L2 cache hint, 5 = as 1 without the scale copy,
-// 6 = as 1 without per-row setup / flush / merge, 7 = no softmax (P = S),
-// 8 = no K dequantisation (raw code words into the MMA), 9 = no V dequantisation,
-// 10 = no loads at all (consumers compute on stale stage buffers).
-#ifndef FADE_ABLATE
-#define FADE_ABLATE 0
-#endif
-// Timeline tracing for profiling builds only (FADE_TRACE defined): per CTA
-// event timestamps into a device array read back by fade_trace_read().
-#ifdef FADE_TRACE
-constexpr int kTraceEv = 96;
-__device__ unsigned long long g_trace[1024 * kTraceEv];
-__device__ __forceinline__ unsigned long long gtimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-// middle CTA c: row 4c + group for the consumer groups (lane 0 of the
-// group's first warp), row 4c + 3 for the producer
-#define FADE_TR(slot) do { if ((threadIdx.x & 127) == 0 && threadIdx.x < blockDim.x - 32 && blockIdx.x < 192 && (slot) < kTraceEv) g_trace[(blockIdx.x * 4 + threadIdx.x / 128) * kTraceEv + (slot)] = gtimer(); } while (0)
-#define FADE_TRP(slot) do { if (threadIdx.x == (blockDim.x / 32 - 1) / 5 * 4 * 32 && blockIdx.x < 192 && (slot) < kTraceEv) g_trace[(blockIdx.x * 4 + 3) * kTraceEv + (slot)] = gtimer(); } while (0)
-// FP-tier warp (lane 0): row 4c + 3, slots 80..
-#define FADE_TRFP(slot) do { if ((threadIdx.x & 31) == 0 && blockIdx.x < 192) g_trace[(blockIdx.x * 4 + 3) * kTraceEv + 80 + (slot)] = gtimer(); } while (0)
-// finisher CTAs record into rows 768.. of the same array
-#define FADE_TRF(slot) do { if (threadIdx.x == 0 && blockIdx.x < 256) g_trace[(768 + blockIdx.x) * kTraceEv + (slot)] = gtimer(); } while (0)
-#else
-#define FADE_TRFP(slot) do {} while (0)
-#define FADE_TRF(slot) do {} while (0)
-#define FADE_TR(slot) do {} while (0)
-#define FADE_TRP(slot) do {} while (0)
-#endif
 constexpr int kConsumerWarps = 4;  // per consumer group; 32 tokens of a stage each
 constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
 // One middle CTA per SM: G consumer groups (3 for up to 8 query rows per kv
 // head; 1 above, where the wider state needs the registers) share one
 // producer warp and one ring of stages; group g
 // consumes stages g, g+G, g+2G, ...
-#ifndef FADE_VPRE
-#define FADE_VPRE 0        // 1: load a stage's V tiles and scales before its K work
-#endif
-#ifndef FADE_LAZYMAX
-#define FADE_LAZYMAX 1     // keep the running maxima until a score exceeds them by 2^8
-#endif
-#ifndef FADE_MID_GROUPS
-#define FADE_MID_GROUPS 3
-#endif
-__host__ __device__ constexpr int mid_groups(int NT) { return NT == 1 ? FADE_MID_GROUPS : 1; }
+__host__ __device__ constexpr int mid_groups(int NT) { return NT == 1 ? 3 : 1; }
 // + one producer warp per group + the FP-tier warp
 __host__ __device__ constexpr int mid_threads(int NT) {
     return (mid_groups(NT) * (kConsumerWarps + 1) + 1) * 32;
@@ -107,10 +72,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 // below any real score, so exp2(score - max) never sees inf - inf.
 constexpr float kMaskedMax = -1e30f;
 constexpr uint32_t kWaitPolls = 1u << 15;   // bounded mbarrier polling ...
-#ifndef FADE_WAIT_HINT_NS
-#define FADE_WAIT_HINT_NS 10000
-#endif
-constexpr uint32_t kWaitHintNs = FADE_WAIT_HINT_NS;   // ... of up to 10 us each
+constexpr uint32_t kWaitHintNs = 10000;   // ... of up to 10 us each
 
 // ---------------------------------------------------------------------------
 // PTX wrappers (mbarrier, TMA, ldmatrix, movmatrix, mma)
@@ -252,7 +214,6 @@ template <> struct Pk<FADE_F16> {
         return d;
     }
     __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
-        if (FADE_ABLATE == 3) return a ^ (b & 1u);
         uint32_t d;
         asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
         return d;
@@ -283,7 +244,6 @@ template <> struct Pk<FADE_BF16> {
         return d;
     }
     __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
-        if (FADE_ABLATE == 3) return a ^ (b & 1u);
         uint32_t d;
         asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
         return d;
@@ -348,6 +308,11 @@ template <int DT> struct Conv {
 #pragma unroll
         for (int i = 0; i < 8; ++i)
             h[i] = Pk<DT>::sub(lop3_and_xor(x >> (2 * i), 0x00030003u, Pk<DT>::K2), Pk<DT>::B2);
+    }
+    // the same fields as the biased values kBias2 + code (no subtraction)
+    __device__ __forceinline__ static void int2_biased(uint32_t x, uint32_t (&h)[8]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = lop3_and_xor(x >> (2 * i), 0x00030003u, Pk<DT>::K2);
     }
 };
 
@@ -644,7 +609,6 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
     const int z0 = (int)((int64_t)c * Z / n_cta), z1 = (int)((int64_t)(c + 1) * Z / n_cta);
     T* ksm = reinterpret_cast<T*>(fsm);
     T* vsm = ksm + kFpChunk * RS;
-    FADE_TRFP(0);
     for (int z = z0; z < z1; ++z) {
         const int b = z / p.Hkv, h = z % p.Hkv;
         // ---- FP segments of the row ----
@@ -701,11 +665,7 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
 #pragma unroll
                 for (int e = 0; e < 4; ++e) o[nt][mi][e] = 0.f;
         }
-#ifdef FADE_NO_FPATTN
-        for (int64_t c0 = 0; c0 < 0; c0 += kFpChunk) {   // profiling: FP tiers skipped
-#else
         for (int64_t c0 = 0; c0 < T_stage; c0 += kFpChunk) {
-#endif
             const int nc = (int)((T_stage - c0) < kFpChunk ? (T_stage - c0) : kFpChunk);
             const int nc16 = (nc + 15) & ~15;
             __syncwarp();   // the previous chunk's rows are no longer read
@@ -749,19 +709,16 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
                     T_all = T_seg + 1;
                 }
             }
-            FADE_TRFP(1);
             if (!waited) {
                 griddep_wait();
                 waited = true;
             }
-            FADE_TRFP(2);
             stage(true);
             if (c0 == 0) {
                 load_q();
                 if (p.age && lane == 0) p.ws_age[z] = (int)(room ? n + 1 : n);
             }
             cp_async_wait_all();
-            FADE_TRFP(3);
             __syncwarp();
             if (ft_aged >= c0 && ft_aged < c0 + nc) {
                 // ---- the aged token: INT4 codes into the middle, its staged row
@@ -903,7 +860,6 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
             waited = true;
         }
         if (T_stage == 0 && p.age && lane == 0) p.ws_age[z] = (int)n;
-        FADE_TRFP(4);
         // ---- partial of row z: O^T rows are channels mi*16 + gid (+8) ----
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -928,7 +884,6 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
             }
         __syncwarp();
     }
-    FADE_TRFP(5);
 }
 
 // ---------------------------------------------------------------------------
@@ -952,6 +907,12 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // exactly: K's per-channel scale into the fp32 query (before its hi + lo
     // split), V's per-token scale into P.  The codes enter the MMA as is.
     constexpr bool FOLD2 = KB == 2 && VB == 2 && !VGROUP && QSPLIT;
+    // bf16 with folded scales: the codes enter the MMA as 130 + c (the magic-
+    // exponent value, no subtraction) and the bias is removed algebraically:
+    // K: scores start from -130 * sum_d q'_d; V: O loses 130 * sum_t p'_t
+    // (accumulated from the same rounded P' the MMA consumes) at each flush.
+    constexpr bool FOLD2B = FOLD2 && DT == FADE_BF16;
+    constexpr float kBias2 = 130.f;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -987,14 +948,6 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     __syncthreads();
-    FADE_TR(0);
-#ifdef FADE_TRACE
-    if (threadIdx.x == 0 && blockIdx.x < 192) {
-        unsigned smid;
-        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-        g_trace[(blockIdx.x * 4) * kTraceEv + 95] = smid + 1;
-    }
-#endif
     // Inputs may be produced by the previous kernel in the stream (age-out,
     // query rotation): wait for it before touching global memory, then let the
     // next kernel in the stream start its prologue.  With `early` the tiers
@@ -1005,7 +958,6 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     const bool fp_early = p.early && warp == FPWARP;
     if (!(p.early && is_producer) && !fp_early) griddep_wait();
     if (warp < PRODUCER) griddep_launch_dependents();
-    FADE_TR(1);
     if (warp == FPWARP) {
         fp_rows_warp<DT, D, NT>(p, c, (int)gridDim.x, smem + L::AB_OFF, !fp_early);
         return;
@@ -1046,23 +998,13 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             // Units past this row's length (uniform grid over a capacity bound)
             // carry no tokens: complete the stage without a copy.
             uint8_t* scs = smem + L::SC_BASE + s * L::SC_BYTES;
-            if (i < 40) FADE_TRP(40 + i);
-            if (lane == 0 && tok0 < len && FADE_ABLATE != 10) {   // 10: compute on stale stages, no loads
-                const uint32_t sc_bytes = (p.scale_tma && FADE_ABLATE != 5) ? (uint32_t)L::sc_box_bytes(p.group) : 0u;
+            if (lane == 0 && tok0 < len) {
+                const uint32_t sc_bytes = p.scale_tma ? (uint32_t)L::sc_box_bytes(p.group) : 0u;
                 mbar_expect_tx(full_bar(s), (uint32_t)(L::K_BYTES + L::V_BYTES) + sc_bytes);
                 // maps address 128-byte rows: token row0 starts at row0*RB/128
-#if FADE_ABLATE == 4
-                asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-                             ::"r"(smem_u32(st + L::K_OFF)), "l"(reinterpret_cast<uint64_t>(&tmap_k)), "r"(0),
-                             "r"((int)(row0 * L::RBK / 128)), "r"(full_bar(s)) : "memory");
-                asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-                             ::"r"(smem_u32(st + L::V_OFF)), "l"(reinterpret_cast<uint64_t>(&tmap_v)), "r"(0),
-                             "r"((int)(row0 * L::RBV / 128)), "r"(full_bar(s)) : "memory");
-#else
                 tma_load_2d(smem_u32(st + L::K_OFF), &tmap_k, 0, (int)(row0 * L::RBK / 128), full_bar(s), policy);
                 tma_load_2d(smem_u32(st + L::V_OFF), &tmap_v, 0, (int)(row0 * L::RBV / 128), full_bar(s), policy);
-#endif
-                if (p.scale_tma && FADE_ABLATE != 5) {
+                if (p.scale_tma) {
                     // per-token: 1-D map over rows; grouped: 2-D map [groups][D].
                     // Past the map's extent the TMA unit writes zeros.
                     if constexpr (!VGROUP) tma_load_1d(smem_u32(scs), &tmap_s, (int)row0, full_bar(s), policy);
@@ -1118,6 +1060,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     uint32_t qf[NQ][NT][KSTEPS][2];  // B fragments (exact model-dtype query)
     uint32_t ksc[KSTEPS][2];         // K scale pairs matching the A pairs
     float m_run[NT][2], l_run[NT][2];
+    float kb[NT][2];                 // FOLD2B: 130 * sum of the row's query channels
+    float lp[NT][2];                 // FOLD2B: running sum of the rounded P' of the row
     float o[NT][MT][4];
     int cur_z = -1, z_first = 0;
     int64_t cur_len = 0;
@@ -1221,10 +1165,27 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         for (int nt = 0; nt < NT; ++nt) {
             m_run[nt][0] = m_run[nt][1] = kMaskedMax;
             l_run[nt][0] = l_run[nt][1] = 0.f;
+            lp[nt][0] = lp[nt][1] = 0.f;
 #pragma unroll
             for (int mi = 0; mi < MT; ++mi)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) o[nt][mi][e] = 0.f;
+            if constexpr (FOLD2B) {
+                // this lane's query channels (row gid), both hi and lo parts
+                float sum = 0.f;
+#pragma unroll
+                for (int qs = 0; qs < NQ; ++qs)
+#pragma unroll
+                    for (int ks = 0; ks < KSTEPS; ++ks)
+#pragma unroll
+                        for (int hs = 0; hs < 2; ++hs)
+                            sum += P::unpack_lo(qf[qs][nt][ks][hs]) + P::unpack_lo(qf[qs][nt][ks][hs] >> 16);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                // C-fragment columns 2t, 2t+1 are query rows held by lanes 8t, 8t+4
+                kb[nt][0] = kBias2 * __shfl_sync(0xffffffffu, sum, (2 * t) * 4);
+                kb[nt][1] = kBias2 * __shfl_sync(0xffffffffu, sum, (2 * t + 1) * 4);
+            }
         }
         cur_len = seg_len(p, b);
     };
@@ -1264,6 +1225,23 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 }
         }
         named_bar_sync(bar_id, kConsumerWarps * 32);
+        if constexpr (FOLD2B) {   // remove the code bias: O -= 130 * sum_t P'
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    float q = lp[nt][e];
+                    q += __shfl_xor_sync(0xffffffffu, q, 4);
+                    q += __shfl_xor_sync(0xffffffffu, q, 8);
+                    q += __shfl_xor_sync(0xffffffffu, q, 16);
+                    const float bias = kBias2 * q;
+#pragma unroll
+                    for (int mi = 0; mi < MT; ++mi) {
+                        o[nt][mi][e] -= bias;
+                        o[nt][mi][e + 2] -= bias;
+                    }
+                }
+        }
         // 2) rescale this gw's O to the CTA max
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -1345,17 +1323,11 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         const int u = ub + i;
         while (u >= ze) { ++z; zb = ze; ze = units_begin(p, z + 1); }
         if (z != cur_z) {
-            if (FADE_ABLATE != 6) {
-                FADE_TR(2 + 3 * (cur_z >= 0 ? 1 : 0));
-                setup_z(z);
-                FADE_TR(4 + 3 * (cur_z >= 0 ? 1 : 0));
-            }
+            setup_z(z);
             cur_z = z;
             z_first = u;
         }
-        if (i / G < 24) FADE_TR(40 + i / G);
         const bool ready = mbar_wait(full_bar(s), ph, abort_flag, p.ws_err);
-        if (i / G < 24) FADE_TR(10 + i / G);
         const int tw = (u - zb) * kStageTokens + gw * 32;  // first token of this gw (row-relative)
         const int clen = (int)cur_len;
         const uint8_t* st = smem + s * L::STAGE_BYTES;
@@ -1363,53 +1335,30 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         const uint32_t vbase = smem_u32(st + L::V_OFF);
         const uint8_t* scb = smem + L::SC_BASE + s * L::SC_BYTES;
 
-        if (ready && tw < clen && FADE_ABLATE != 1 && FADE_ABLATE != 4 && FADE_ABLATE != 5 && FADE_ABLATE != 6) {
+        if (ready && tw < clen) {
             // ---- S^T = K_deq . q^T for the gw's 2 m-tiles ----
-            // two accumulators per m-tile (even / odd k-steps) halve the
-            // dependent MMA chain; summed before the softmax
             float sacc[2][NT][4];
-            // V tiles and per-token V scales of both m-tiles, issued before the
-            // K work so their shared-memory latency hides behind it
-            uint32_t vpre[2][2][L::NCHV];
-            uint32_t vspre[2][2];
-            if constexpr (FADE_VPRE != 0) {
-#pragma unroll
-                for (int mt = 0; mt < 2; ++mt) {
-                    load_tiles_at<L::NCHV, true>(vbase, voffs, mt, vpre[mt]);
-                    if constexpr (!VGROUP) {
-                        const uint32_t* sc32 = reinterpret_cast<const uint32_t*>(scb);
-                        vspre[mt][0] = sc32[(gw * 32 + mt * 16 + 2 * t) >> 1];
-                        vspre[mt][1] = sc32[(gw * 32 + mt * 16 + 8 + 2 * t) >> 1];
-                    }
-                }
-            }
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = 0.f;
+                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = FOLD2B ? -kb[nt][e & 1] : 0.f;
                 uint32_t kr[2][L::NCHK];
                 load_tiles_at<L::NCHK, false>(kbase, koffs, mt, kr);
 #pragma unroll
                 for (int cb = 0; cb < L::NCHK; ++cb) {
                     if constexpr (KB == 4) {
                         uint32_t h0[4], h1[4];
-                        if constexpr (FADE_ABLATE == 8) {
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) { h0[j] = kr[0][cb]; h1[j] = kr[1][cb]; }
-                        } else {
-                            Conv<DT>::int4(kr[0][cb], h0);
-                            Conv<DT>::int4(kr[1][cb], h1);
-                        }
+                        Conv<DT>::int4(kr[0][cb], h0);
+                        Conv<DT>::int4(kr[1][cb], h1);
 #pragma unroll
                         for (int u2 = 0; u2 < 2; ++u2) {
                             const int ks = cb * 2 + u2;
-                            const bool raw = FADE_ABLATE == 8;
-                            const uint32_t a0 = raw ? h0[2 * u2] : P::mul(h0[2 * u2], ksc[ks][0]);
-                            const uint32_t a1 = raw ? h1[2 * u2] : P::mul(h1[2 * u2], ksc[ks][0]);
-                            const uint32_t a2 = raw ? h0[2 * u2 + 1] : P::mul(h0[2 * u2 + 1], ksc[ks][1]);
-                            const uint32_t a3 = raw ? h1[2 * u2 + 1] : P::mul(h1[2 * u2 + 1], ksc[ks][1]);
+                            const uint32_t a0 = P::mul(h0[2 * u2], ksc[ks][0]);
+                            const uint32_t a1 = P::mul(h1[2 * u2], ksc[ks][0]);
+                            const uint32_t a2 = P::mul(h0[2 * u2 + 1], ksc[ks][1]);
+                            const uint32_t a3 = P::mul(h1[2 * u2 + 1], ksc[ks][1]);
 #pragma unroll
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
@@ -1419,8 +1368,13 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         }
                     } else {
                         uint32_t h0[8], h1[8];
-                        Conv<DT>::int2(kr[0][cb], h0);
-                        Conv<DT>::int2(kr[1][cb], h1);
+                        if constexpr (FOLD2B) {
+                            Conv<DT>::int2_biased(kr[0][cb], h0);
+                            Conv<DT>::int2_biased(kr[1][cb], h1);
+                        } else {
+                            Conv<DT>::int2(kr[0][cb], h0);
+                            Conv<DT>::int2(kr[1][cb], h1);
+                        }
 #pragma unroll
                         for (int u4 = 0; u4 < 4; ++u4) {
                             const int ks = cb * 4 + u4;
@@ -1454,18 +1408,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             if (tw + mt * 16 + gid + ((e >> 1) << 3) >= clen) sacc[mt][nt][e] = -INFINITY;
             }
             uint32_t pb[2][NT][2];
-#if FADE_ABLATE == 7
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    pb[mt][nt][0] = movmatrix_t(P::pack(sacc[mt][nt][0], sacc[mt][nt][1]));
-                    pb[mt][nt][1] = movmatrix_t(P::pack(sacc[mt][nt][2], sacc[mt][nt][3]));
-                }
-            if (false) {
-#else
             {
-#endif
             // Lazy maxima: while every score of the stage stays within 2^8 of
             // its row's running maximum (log2 units), the maxima are kept and
             // the weights (<= 256, finite in the model dtype) use them as is;
@@ -1473,7 +1416,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             // that margin.  Maxima start at kMaskedMax, so a row's first stage
             // always takes the full path.
             bool full = true;
-            if constexpr (FADE_LAZYMAX != 0) {
+            {
                 bool need = false;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
@@ -1511,6 +1454,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         l_run[nt][e] *= corr[nt][e];
+                        lp[nt][e] *= corr[nt][e];
 #pragma unroll
                         for (int mi = 0; mi < MT; ++mi) {
                             o[nt][mi][e] *= corr[nt][e];
@@ -1543,24 +1487,22 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         l_run[nt][e & 1] += pe;
                         pv[e] = FOLD2 ? pe * tsc[mt][e >> 1] : pe;
                     }
-                    pb[mt][nt][0] = movmatrix_t(P::pack(pv[0], pv[1]));
-                    pb[mt][nt][1] = movmatrix_t(P::pack(pv[2], pv[3]));
+                    const uint32_t p01 = P::pack(pv[0], pv[1]), p23 = P::pack(pv[2], pv[3]);
+                    if constexpr (FOLD2B) {   // exactly the P' the MMA sees
+                        lp[nt][0] += P::unpack_lo(p01) + P::unpack_lo(p23);
+                        lp[nt][1] += P::unpack_lo(p01 >> 16) + P::unpack_lo(p23 >> 16);
+                    }
+                    pb[mt][nt][0] = movmatrix_t(p01);
+                    pb[mt][nt][1] = movmatrix_t(p23);
                 }
             }
             }   // softmax
             // ---- O^T += V_deq^T . P^T ----
 #pragma unroll
-            for (int mt = 0; mt < (FADE_ABLATE == 2 ? 0 : 2); ++mt) {
+            for (int mt = 0; mt < 2; ++mt) {
                 const int trow0 = gw * 32 + mt * 16;
                 uint32_t vr[2][L::NCHV];
-                if constexpr (FADE_VPRE != 0) {
-#pragma unroll
-                    for (int a = 0; a < 2; ++a)
-#pragma unroll
-                        for (int cb = 0; cb < L::NCHV; ++cb) vr[a][cb] = vpre[mt][a][cb];
-                } else {
-                    load_tiles_at<L::NCHV, true>(vbase, voffs, mt, vr);
-                }
+                load_tiles_at<L::NCHV, true>(vbase, voffs, mt, vr);
                 // tokens of this m-tile past the length: their scales may be
                 // stale bytes (NaN * 0 must not reach the MMA), so zero them;
                 // a tile entirely past the length is skipped.
@@ -1569,14 +1511,9 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 uint32_t vs0 = 0, vs1 = 0;
                 const uint16_t* gsc = nullptr;
                 if constexpr (!VGROUP) {
-                    if constexpr (FADE_VPRE != 0) {
-                        vs0 = vspre[mt][0];
-                        vs1 = vspre[mt][1];
-                    } else {
-                        const uint32_t* sc32 = reinterpret_cast<const uint32_t*>(scb);
-                        vs0 = sc32[(trow0 + 2 * t) >> 1];       // tokens 2t, 2t+1
-                        vs1 = sc32[(trow0 + 8 + 2 * t) >> 1];   // tokens 8+2t, 9+2t
-                    }
+                    const uint32_t* sc32 = reinterpret_cast<const uint32_t*>(scb);
+                    vs0 = sc32[(trow0 + 2 * t) >> 1];       // tokens 2t, 2t+1
+                    vs1 = sc32[(trow0 + 8 + 2 * t) >> 1];   // tokens 8+2t, 9+2t
                     const int rem = clen - tile_tok;  // valid tokens in this tile (> 0)
                     if (rem < 16) {
                         const int t0 = 2 * t, t1 = 8 + 2 * t;
@@ -1590,21 +1527,14 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 for (int cb = 0; cb < L::NCHV; ++cb) {
                     if constexpr (VB == 4) {
                         uint32_t h0[4], h1[4];
-                        if constexpr (FADE_ABLATE == 9) {
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) { h0[j] = vr[0][cb]; h1[j] = vr[1][cb]; }
-                        } else {
-                            Conv<DT>::int4(vr[0][cb], h0);   // tokens 2t,2t+1
-                            Conv<DT>::int4(vr[1][cb], h1);   // tokens 8+2t, 9+2t
-                        }
+                        Conv<DT>::int4(vr[0][cb], h0);   // tokens 2t,2t+1
+                        Conv<DT>::int4(vr[1][cb], h1);   // tokens 8+2t, 9+2t
                         // m-tile j: rows (gid: e_{2j} -> h[2j+1]), (gid+8: e_{2j+1} -> h[2j])
 #pragma unroll
                         for (int j = 0; j < 2; ++j) {
                             const int mi = cb * 2 + j;
                             uint32_t a0, a1, a2, a3;
-                            if constexpr (FADE_ABLATE == 9) {
-                                a0 = h0[2 * j + 1]; a1 = h0[2 * j]; a2 = h1[2 * j + 1]; a3 = h1[2 * j];
-                            } else if constexpr (!VGROUP) {
+                            if constexpr (!VGROUP) {
                                 a0 = P::mul(h0[2 * j + 1], vs0);
                                 a1 = P::mul(h0[2 * j], vs0);
                                 a2 = P::mul(h1[2 * j + 1], vs1);
@@ -1623,8 +1553,13 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         }
                     } else {
                         uint32_t h0[8], h1[8];
-                        Conv<DT>::int2(vr[0][cb], h0);
-                        Conv<DT>::int2(vr[1][cb], h1);
+                        if constexpr (FOLD2B) {
+                            Conv<DT>::int2_biased(vr[0][cb], h0);
+                            Conv<DT>::int2_biased(vr[1][cb], h1);
+                        } else {
+                            Conv<DT>::int2(vr[0][cb], h0);
+                            Conv<DT>::int2(vr[1][cb], h1);
+                        }
                         // channels +0 h[3], +1 h[2], +2 h[1], +3 h[0], +4 h[7], +5 h[6], +6 h[5], +7 h[4]
                         const int lo[4] = {3, 1, 7, 5};
                         const int hi[4] = {2, 0, 6, 4};
@@ -1660,20 +1595,16 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
         }
         // The group's last stage of this row: combine and store the row's
         // partial in this stage's buffer before releasing it.
-        if (FADE_ABLATE != 6 && (ub + i + G >= ue || ub + i + G >= ze)) {
-            FADE_TR(5);
+        if (ub + i + G >= ue || ub + i + G >= ze) {
             flush(cur_z, reinterpret_cast<float*>(smem + s * L::STAGE_BYTES));
             // the buffer was written through the generic proxy; the next TMA
             // load into it is an async-proxy write
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            FADE_TR(6);
         }
         mbar_arrive(empty_bar(s));   // each lane after its own reads of the stage
         s += G;
         if (s >= NS) { s -= NS; ph ^= 1u; }
     }
-    FADE_TR(36);
-    FADE_TR(37);
 }
 
 // ---------------------------------------------------------------------------
@@ -1690,13 +1621,20 @@ __global__ void rotate_queries_kernel(const void* q, int Hq, int n_q, int D, int
                                       int64_t q_sh, int64_t q_ss, const float* __restrict__ R,
                                       float* __restrict__ q_rot, int n_rows) {
     extern __shared__ float rsm[];
-    float* rt = rsm;               // [D][D]: rt[e*D + d] = R[d][e]
-    float* qs = rsm + D * D;       // [kRotRows][D]
+    const int RS = D + 1;          // padded row: the transposed store is conflict-free
+    float* rt = rsm;               // [D][RS]: rt[e*RS + d] = R[d][e]
+    float* qs = rsm + D * RS;      // [kRotRows][D]
     griddep_wait();              // q and R may come from the preceding kernel
     griddep_launch_dependents();
-    for (int i = threadIdx.x; i < D * D; i += blockDim.x) {
+    // R in 16-byte pieces, 8 loads in flight per thread
+#pragma unroll 8
+    for (int i = threadIdx.x * 4; i < D * D; i += blockDim.x * 4) {
+        const float4 r4 = __ldg(reinterpret_cast<const float4*>(R + i));
         const int d = i / D, e = i % D;
-        rt[e * D + d] = R[i];
+        rt[e * RS + d] = r4.x;
+        rt[(e + 1) * RS + d] = r4.y;
+        rt[(e + 2) * RS + d] = r4.z;
+        rt[(e + 3) * RS + d] = r4.w;
     }
     const int row0 = blockIdx.x * kRotRows;
     const int nr = (n_rows - row0) < kRotRows ? (n_rows - row0) : kRotRows;
@@ -1714,7 +1652,7 @@ __global__ void rotate_queries_kernel(const void* q, int Hq, int n_q, int D, int
 #pragma unroll
     for (int r = 0; r < kRotRows; ++r) acc[r] = 0.f;
     for (int e = 0; e < D; ++e) {
-        const float re = rt[e * D + d];
+        const float re = rt[e * RS + d];
 #pragma unroll
         for (int r = 0; r < kRotRows; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(qs[r * D + e], re));
     }
@@ -1809,7 +1747,6 @@ finish_kernel(const __grid_constant__ FinParams p) {
     const int b = z / p.Hkv, h = z % p.Hkv;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int rows = p.rows;
-    FADE_TRF(0);
     float acc_f[OUTS][2];
 #pragma unroll
     for (int k = 0; k < OUTS; ++k) acc_f[k][0] = acc_f[k][1] = 0.f;
@@ -1821,7 +1758,6 @@ finish_kernel(const __grid_constant__ FinParams p) {
         // starts from that partial (its loads overlap the slot lookup).
         griddep_wait();
         griddep_launch_dependents();
-        FADE_TRF(2);
         if (tid < rows) fp_ml = *reinterpret_cast<const float2*>(p.ws_fpml + ((int64_t)z * rows + tid) * 2);
 #pragma unroll
         for (int k = 0; k < OUTS; ++k) {
@@ -1966,7 +1902,6 @@ finish_kernel(const __grid_constant__ FinParams p) {
             }
         }
     }
-    FADE_TRF(1);
 
     // ---- merge the middle partials ----
     float acc_m[OUTS][2];
@@ -2076,7 +2011,6 @@ finish_kernel(const __grid_constant__ FinParams p) {
         }
     }
     __syncthreads();
-    FADE_TRF(11);
     if (tid < rows) f_row[tid] = l_row[tid] > 0.f ? 1.f / l_row[tid] : 0.f;
     if (p.rotation && nsl > 0) {
         // middle part is in the rotated basis: mid @ R (rows via shared memory)
@@ -2116,7 +2050,6 @@ finish_kernel(const __grid_constant__ FinParams p) {
         o[0] = Elem<DT>::from_f((acc_f[k][0] + acc_m[k][0]) * inv);
         o[1] = Elem<DT>::from_f((acc_f[k][1] + acc_m[k][1]) * inv);
     }
-    FADE_TRF(3);
 }
 
 // ---------------------------------------------------------------------------
@@ -2313,6 +2246,7 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
             if (s.bits != 2 && s.bits != 4) return FADE_ERR_UNSUPPORTED;
             pl->kb = s.bits; pl->vb = s.bits; pl->vg = false;
             if (!d->rotation) return FADE_ERR_INVALID_ARG;
+            if (!aligned16(d->rotation)) return FADE_ERR_ALIGN;   // R is staged with 16-byte loads
         } else return FADE_ERR_INVALID_ARG;
         if (!s.k || !s.v || !s.k_scale || !s.v_scale) return FADE_ERR_INVALID_ARG;
         if (!aligned16(s.k) || !aligned16(s.v)) return FADE_ERR_ALIGN;
@@ -2363,7 +2297,7 @@ static cudaError_t rotate_queries_smem_attr(const void* fn, int which) {
     if (dev < 0 || dev >= kMaxDevices) dev = 0;
     std::lock_guard<std::mutex> lock(mu);
     if (!done[dev][which]) {
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (128 * 128 + kRotRows * 128) * 4);
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (128 * 129 + kRotRows * 128) * 4);
         if (e != cudaSuccess) return e;
         done[dev][which] = true;
     }
@@ -2382,9 +2316,6 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-#ifdef FADE_NO_PDL
-    cfg.numAttrs = 0;
-#endif
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
@@ -2432,7 +2363,7 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
         const float* R = d->rotation;
         int n_rows = d->B * d->Hq * d->n_q;
         void* args[] = {(void*)&qp, &Hq, &nq, &D, &a, &b2, &c2, (void*)&R, (void*)&qrot, &n_rows};
-        const size_t rsmem = (size_t)(D * D + kRotRows * D) * 4;
+        const size_t rsmem = (size_t)(D * (D + 1) + kRotRows * D) * 4;
         FADE_CUDA_TRY(rotate_queries_smem_attr(fn, d->dtype == FADE_F16 ? 0 : 1));
         FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)((n_rows + kRotRows - 1) / kRotRows)), dim3((unsigned)D),
                                  rsmem, s, args));
@@ -2491,13 +2422,6 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
         mp.ws_o = reinterpret_cast<float*>(ws + pl.off_o);
         mp.ws_err = reinterpret_cast<int*>(ws + pl.off_err);
         mp.scale_tma = scale_tma;
-        if (std::getenv("FADE_DEBUG_PLAN")) {
-            std::fprintf(stderr,
-                         "[fade] decode plan: B=%d Hq=%d Hkv=%d D=%d rows=%d kb=%d vb=%d grouped=%d "
-                         "units/z=%d ctas=%d occ=%d smem=%d scale_tma=%d n_rows=%lld\n",
-                         d->B, d->Hq, d->Hkv, d->D, pl.rows, pl.kb, pl.vb, (int)pl.vg, pl.units_per_z,
-                         pl.n_ctas, pl.mk.occ, pl.mk.smem, scale_tma, (long long)n_rows);
-        }
         mp.early = (a && a->prefetch_tiers) ? 1 : 0;
         // FP tiers for the FP warp
         mp.n_fp = 0;
@@ -2662,15 +2586,3 @@ extern "C" int fade_decode_attn_noalloc_check(void* stream) {
     if (st != FADE_OK) return st;
     return fade_workspace_check(ws, fade::kNoAllocScratchBytes, stream);
 }
-
-#ifdef FADE_TRACE
-extern "C" int fade_trace_read(unsigned long long* host, size_t n) {
-    const size_t bytes = n * sizeof(unsigned long long) < sizeof(fade::g_trace) ? n * sizeof(unsigned long long)
-                                                                               : sizeof(fade::g_trace);
-    return cudaMemcpyFromSymbol(host, fade::g_trace, bytes) == cudaSuccess ? 0 : 7;
-}
-extern "C" int fade_trace_clear(void) {
-    static unsigned long long zeros[1024 * fade::kTraceEv];
-    return cudaMemcpyToSymbol(fade::g_trace, zeros, sizeof(zeros)) == cudaSuccess ? 0 : 7;
-}
-#endif

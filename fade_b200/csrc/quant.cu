@@ -477,7 +477,9 @@ static int launch_quant_k(const void* x, const fade_view4& v, uint8_t* packed, v
     const int E = e8 ? 8 : 2;
     int dims_per_cta = (int)(v.D < 256 ? v.D : 256);
     // For few (b,h) pairs, split channels across CTAs to fill the machine.
-    while (Z * (v.D / dims_per_cta) < 148 * 8 && dims_per_cta > 2 * E && dims_per_cta % (2 * E) == 0 &&
+    // (blocks of at least 64 channels: 128-byte row segments; narrower ones
+    // double the DRAM sectors fetched per useful byte)
+    while (Z * (v.D / dims_per_cta) < 148 && dims_per_cta > 8 * E && dims_per_cta % (2 * E) == 0 &&
            (dims_per_cta / 2) % E == 0 && v.D % (dims_per_cta / 2) == 0)
         dims_per_cta /= 2;
     dim3 grid((unsigned)Z, (unsigned)((v.D + dims_per_cta - 1) / dims_per_cta));

@@ -21,7 +21,7 @@ constexpr int kRotThreads = 256;
 // DC == 0 is the generic form.  `y` may alias `in`: the results are written
 // after a block-wide barrier.
 template <int DC>
-__device__ __forceinline__ void rot_matmul(const float* in, const float* __restrict__ M, float* y, int D_rt) {
+__device__ __forceinline__ void rot_matmul(const float* in, const float* __restrict__ M, int ldm, float* y, int D_rt) {
     const int D = DC > 0 ? DC : D_rt;
     const int groups = blockDim.x / D;                          // >= 2 for D <= 128
     const int tpg = (kRotTokens + groups - 1) / groups;         // <= kRotAcc
@@ -34,8 +34,8 @@ __device__ __forceinline__ void rot_matmul(const float* in, const float* __restr
     for (int j = 0; j < NJ; ++j) acc[j] = 0.f;
     if (on) {
         for (int e = 0; e < D; e += 4) {
-            const float m0 = M[e * D + d], m1 = M[(e + 1) * D + d], m2 = M[(e + 2) * D + d],
-                        m3 = M[(e + 3) * D + d];
+            const float m0 = M[e * ldm + d], m1 = M[(e + 1) * ldm + d], m2 = M[(e + 2) * ldm + d],
+                        m3 = M[(e + 3) * ldm + d];
 #pragma unroll
             for (int j = 0; j < NJ; ++j) {
                 if (DC > 0 || j < nj) {
@@ -72,7 +72,7 @@ __device__ void rotate_tile(const typename Elem<DT>::T* __restrict__ x, const fa
         xin[i] = (t < nt) ? Elem<DT>::to_f(x[b * v.sb + h * v.sh + (t0 + t) * v.ss + (int64_t)e * v.sd]) : 0.f;
     }
     __syncthreads();
-    rot_matmul<DC>(xin, Rt, xs, D);
+    rot_matmul<DC>(xin, Rt, D + 1, xs, D);
     __syncthreads();
 }
 
@@ -85,8 +85,8 @@ rotated_quant_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, c
                      typename Elem<DT>::T* __restrict__ scale) {
     extern __shared__ float sm[];
     const int D = (int)v.D;
-    float* Rt = sm;                    // [D][D] transposed: Rt[e][d] = R[d][e]
-    float* xin = Rt + D * D;           // [kRotTokens][D]
+    float* Rt = sm;                    // [D][D+1] transposed: Rt[e][d] = R[d][e]
+    float* xin = Rt + D * (D + 1);     // [kRotTokens][D]
     float* xs = xin;                   // the rotation is written over its input
     float* tsc = xin + kRotTokens * D; // [kRotTokens] per-token inv
     const int64_t tiles = (v.S + kRotTokens - 1) / kRotTokens;
@@ -94,9 +94,15 @@ rotated_quant_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, c
     const int64_t b = bh / v.H, h = bh % v.H;
     const int64_t t0 = tile * kRotTokens;
     const int nt = (int)min((int64_t)kRotTokens, v.S - t0);
-    for (int i = threadIdx.x; i < D * D; i += blockDim.x) {
+    // R in 16-byte pieces, 8 loads in flight per thread (D % 4 == 0)
+#pragma unroll 8
+    for (int i = threadIdx.x * 4; i < D * D; i += blockDim.x * 4) {
+        const float4 r4 = __ldg(reinterpret_cast<const float4*>(R + i));
         const int d = i / D, e = i % D;
-        Rt[e * D + d] = R[i];
+        Rt[e * (D + 1) + d] = r4.x;          // rows padded to D + 1: conflict-free
+        Rt[(e + 1) * (D + 1) + d] = r4.y;
+        Rt[(e + 2) * (D + 1) + d] = r4.z;
+        Rt[(e + 3) * (D + 1) + d] = r4.w;
     }
     __syncthreads();
     rotate_tile<DT, DC>(x, v, b, h, t0, nt, Rt, xin, xs);
@@ -175,7 +181,9 @@ rotated_dequant_kernel(const uint8_t* __restrict__ packed, int bits, const typen
     const int64_t bh = blockIdx.x / tiles, tile = blockIdx.x % tiles;
     const int64_t t0 = tile * kRotTokens;
     const int nt = (int)min((int64_t)kRotTokens, S - t0);
-    for (int i = threadIdx.x; i < D * D; i += blockDim.x) Rs[i] = R[i];
+#pragma unroll 8
+    for (int i = threadIdx.x * 4; i < D * D; i += blockDim.x * 4)
+        *reinterpret_cast<float4*>(Rs + i) = __ldg(reinterpret_cast<const float4*>(R + i));
     for (int i = threadIdx.x; i < kRotTokens * D; i += blockDim.x) {
         const int t = i / D, e = i % D;
         float val = 0.f;
@@ -187,7 +195,7 @@ rotated_dequant_kernel(const uint8_t* __restrict__ packed, int bits, const typen
         xs[i] = val;
     }
     __syncthreads();
-    rot_matmul<DC>(xs, Rs, xs, D);
+    rot_matmul<DC>(xs, Rs, D, xs, D);
     __syncthreads();
     for (int i = threadIdx.x; i < nt * D; i += blockDim.x)
         out[(bh * S + t0) * D + i] = Elem<DT>::from_f(xs[i]);
@@ -259,12 +267,13 @@ extern "C" int fade_rotated_quant(const void* x, int dtype, fade_view4 xv, const
     const int64_t Z = xv.B * xv.H;
     if (Z == 0 || xv.S == 0) return FADE_OK;
     if (!x || !R || !packed || !scale) return FADE_ERR_INVALID_ARG;
+    if (reinterpret_cast<uintptr_t>(R) % 16) return FADE_ERR_ALIGN;   // staged with 16-byte loads
     const size_t need = (size_t)Z * xv.D * 4;
     if (kind == 0 && (!workspace || ws_bytes < need)) return FADE_ERR_WORKSPACE;
     cudaStream_t st = as_stream(stream);
     const int D = (int)xv.D;
     // R (transposed) + one token tile, rotated in place + per-token scales
-    const size_t smem = ((size_t)D * D + kRotTokens * D + kRotTokens) * 4;
+    const size_t smem = ((size_t)D * (D + 1) + kRotTokens * D + kRotTokens) * 4;
     const int64_t tiles = (xv.S + kRotTokens - 1) / kRotTokens;
     const unsigned grid = (unsigned)(Z * tiles);
     float* amax = reinterpret_cast<float*>(workspace);
@@ -286,6 +295,7 @@ extern "C" int fade_rotated_dequant(const uint8_t* packed, int bits, const void*
     const int64_t Z = B * H;
     if (Z == 0 || S == 0) return FADE_OK;
     if (!packed || !scale || !R || !out) return FADE_ERR_INVALID_ARG;
+    if (reinterpret_cast<uintptr_t>(R) % 16) return FADE_ERR_ALIGN;   // staged with 16-byte loads
     const size_t smem = ((size_t)D * D + kRotTokens * D) * 4;   // R + one tile, rotated in place
     const int64_t tiles = (S + kRotTokens - 1) / kRotTokens;
     const unsigned grid = (unsigned)(Z * tiles);

@@ -112,7 +112,8 @@ int fade_dequant(const void* codes, int bits, const void* scale, int scale_mode,
  * x_rot = x @ R^T in fp32 (sequential-d accumulation, no FMA contraction),
  * then symmetric quant at `bits` (2, 3 or 4) with fp32 math; scale is cast to
  * x's dtype.  packed: bits 4 -> [..,D/2], 2 -> [..,D/4], 3 -> int8 [..,D].
- * R: [D,D] fp32 row-major on the device.  workspace: >= B*H*D*4 bytes
+ * R: [D,D] fp32 row-major on the device, 16-byte aligned (else FADE_ERR_ALIGN);
+ * D a multiple of 4, at most 128.  workspace: >= B*H*D*4 bytes
  * (per-channel absmax, kind 0 only). */
 int fade_rotated_quant(const void* x, int dtype, fade_view4 xv, const float* R,
                        int bits, int kind, uint8_t* packed, void* scale,
@@ -216,7 +217,8 @@ typedef struct fade_decode_desc {
     float sm_scale;          /* softmax scale (1/sqrt(D) in the reference)     */
     const void* q;  int64_t q_sb, q_sh, q_ss;    /* [B,Hq,n_q,D], elements */
     void* out;      int64_t o_sb, o_sh, o_ss;
-    const float* rotation;   /* [D,D] fp32; required with a FADE_SEG_ROT tier  */
+    const float* rotation;   /* [D,D] fp32, 16-byte aligned; required with a
+                                FADE_SEG_ROT tier                               */
     int32_t n_segments;
     int32_t n_ctas;          /* 0 = auto (persistent grid: SMs x occupancy)    */
     const int32_t* cu_units; /* optional device int32 [B*Hkv+1]: prefix sum over
