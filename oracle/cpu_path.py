@@ -1,4 +1,4 @@
-"""The reference's per-step CPU decode path, restated -- TEST/BASELINE ONLY.
+"""The reference's per-step CPU decode path, restated -- TEST AND CPU-BASELINE USE ONLY.
 
 What the reference pays per layer per decode step on the CPU (fade/cache.py:
 update -> _materialize 683-808 -> torch.cat 699, with the INT4 middle's

@@ -65,7 +65,7 @@ CFG4 = dict(Hq=28, Hkv=4, D=128, n_seq=6, lo=512, hi=4096, n_sink=4, recent=64, 
 
 def cfg4_inputs():
     """Qwen2.5-7B-shaped ragged batch (bf16): n_seq sequences with lengths
-    uniform in [lo, hi] (BASELINE's 512..32768 scaled down for the fixture).
+    uniform in [lo, hi] (the benchmark's 512..32768 scaled down for the fixture).
     Returns (lengths, [(k, v) per sequence], q [n_seq, Hq, 1, D])."""
     c = CFG4
     gen = torch.Generator().manual_seed(41)

@@ -263,7 +263,7 @@ def main(ref: str) -> None:
 
 
 def decode_cfg3_g32(ref: str) -> None:
-    """Config 3 at BASELINE's settings (batch sliced to 1): H2O survivors of a
+    """Config 3 at the benchmark configuration's settings (batch sliced to 1): H2O survivors of a
     4096-token prompt (_assign_one_layer, budget 400) through the reference's
     evicting apply_tier_assignment (un-RoPE / re-RoPE), K INT4, V grouped INT2
     with group 32 (quant_v_int2(pad_to_group(v, 32), 32)), then the reference's

@@ -1,4 +1,4 @@
-"""BASELINE configs 3 and 4 on the GPU against fixtures made by running the
+"""Benchmark configurations 3 and 4 on the GPU against fixtures made by running the
 reference (tests/golden/make_golden.py).  The inputs are regenerated here from
 their seeds (tests/golden/inputs.py) and checked against the fixture's
 checksums first, so the GPU sees exactly the bits the reference saw."""

@@ -177,7 +177,7 @@ def test_rotated_dequant_matches_reference(dt, D, bits):
         assert (err != 0).mean() < 5e-3, (kind, (err != 0).mean())
 
 
-# ------------------------------------------- config 3 at BASELINE settings
+# ------------------------------- config 3 at the benchmark configuration settings
 def _gi():
     import sys
 
