@@ -86,6 +86,9 @@ def parse():
                          "stream overlapping the next layers")
     ap.add_argument("--reassign", action="store_true",
                     help="time the tier-reassignment kernels (quantisers, rotation, re-RoPE, dequant) instead")
+    ap.add_argument("--reserve-sms", type=int, default=None,
+                    help="multi-GPU heads partition with side-stream gathers: SMs left free of the persistent "
+                         "middle kernel so the collective overlaps it (default 8)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="layers per step (profiling captures use 1)")
@@ -339,7 +342,7 @@ def config_block(ws: int, parallelism: str) -> dict:
 # --------------------------------------------------------------------------
 # fade arm: configs 1, 2, 5 (TieredDecoder: age-out + fused attention per layer)
 # --------------------------------------------------------------------------
-def build_decoder(dev, extra_steps, plan, seed_base):
+def build_decoder(dev, extra_steps, plan, seed_base, n_ctas=0):
     import torch
 
     from fade_b200.decoder import TieredDecoder
@@ -349,7 +352,7 @@ def build_decoder(dev, extra_steps, plan, seed_base):
     n_mid = c["context"] - c["n_sink"] - c["recent"]
     dec = TieredDecoder(c["layers"], plan.batch, plan.n_q_heads, plan.n_kv_heads, c["head_dim"], dtype=dt,
                         n_sink=c["n_sink"], recent_window=c["recent"], mid_capacity=n_mid + extra_steps + 8,
-                        device=dev)
+                        device=dev, n_ctas=n_ctas)
     gen = torch.Generator(device=dev)
     B, H, S, D = plan.batch, plan.n_kv_heads, c["context"], c["head_dim"]
     for layer in range(c["layers"]):
@@ -394,7 +397,11 @@ def run_int4(args, ws, rank, local):
     roof_steps = min(K, 10) if ws == 1 else 0
     e2e_steps = 0 if args.no_e2e else min(K, 20)
     total = 4 + 2 * W + 3 * K + roof_steps + e2e_steps
-    dec, _ = build_decoder(dev, total, plan, 1000 + 100003 * rank)
+    n_ctas = 0
+    if plan.gathers and args.gather_stream == "side":
+        reserve = 8 if args.reserve_sms is None else max(0, args.reserve_sms)
+        n_ctas = max(1, torch.cuda.get_device_properties(dev).multi_processor_count - reserve)
+    dec, _ = build_decoder(dev, total, plan, 1000 + 100003 * rank, n_ctas=n_ctas)
     gen = torch.Generator(device=dev).manual_seed(7 + rank)
     dt = _torch_dt(c["dtype"])
     q = torch.randn(dec.q.shape, device=dev, generator=gen).to(dt)
@@ -526,6 +533,7 @@ def run_int4(args, ws, rank, local):
         per_layer = int(dec.out[0].numel() * dec.out.element_size())
         coll = {"op": "all_gather (NCCL) of each layer's attention output", "ranks": ws,
                 "stream": args.gather_stream,
+                "middle_kernel_ctas": n_ctas or "one per SM",
                 "bytes_in_per_rank_per_layer": per_layer, "bytes_out_per_layer": per_layer * ws,
                 "graph_captured": graph_ok,
                 "ms_per_step_without_collective": round(ms_ng, 4) if ms_ng else None,

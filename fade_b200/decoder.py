@@ -92,13 +92,16 @@ class TieredDecoder:
     def __init__(self, n_layers: int, batch: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
                  dtype: torch.dtype = torch.bfloat16, n_sink: int = 4, recent_window: int = 64,
                  mid_capacity: int = 8192, device: torch.device | str = "cuda", sm_scale: float | None = None,
-                 fused: bool = True):
+                 fused: bool = True, n_ctas: int = 0):
         self.L, self.B, self.Hq, self.Hkv, self.D = n_layers, batch, n_q_heads, n_kv_heads, head_dim
         self.dtype, self.n_sink, self.R = dtype, n_sink, recent_window
         self.cap = int(-(-mid_capacity // 128) * 128)
         self.device = torch.device(device)
         self.sm_scale = sm_scale
         self.fused = fused
+        # middle-kernel CTAs (0 = one per SM); fewer leaves SMs free for work
+        # that should overlap the layers, e.g. collectives on another stream
+        self.n_ctas = int(n_ctas)
         B, H, D = batch, n_kv_heads, head_dim
         dev = self.device
         self.q = torch.zeros(n_layers, B, n_q_heads, 1, D, dtype=dtype, device=dev)
@@ -183,7 +186,7 @@ class TieredDecoder:
                 FPTier(ly.ring_k, ly.ring_v),
             ]
             ly.plan = DecodePlan(self.q[layer], tiers, out=self.out[layer], sm_scale=self.sm_scale,
-                                 workspace=self._ws)
+                                 workspace=self._ws, n_ctas=self.n_ctas)
             self._ws = ly.plan.workspace
             # prebuilt argument tuple for fade_age_out_int4 (no per-step Python work)
             B, H, R, D = ly.ring_k.shape
