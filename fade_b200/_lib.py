@@ -66,7 +66,12 @@ class KVSegment(ctypes.Structure):
         ("ks_sb", _c_i64),
         ("ks_sh", _c_i64),
         ("n_rows", _c_i64),
+        ("page_table", _vp),
+        ("pages_per_row", _c_i64),
     ]
+
+
+PAGE_TOKENS = 128
 
 
 class DecodeDesc(ctypes.Structure):

@@ -35,7 +35,13 @@ class FPTier:
 
 @dataclass
 class Int4Tier:
-    """INT4 middle: K per-channel (k_scale [B,Hkv,1,D]), V per-token (v_scale [B,Hkv,S,1])."""
+    """INT4 middle: K per-channel (k_scale [B,Hkv,1,D]), V per-token (v_scale [B,Hkv,S,1]).
+
+    Paged form: with ``page_table`` (int32 [B*Hkv, pages_per_row] on the
+    device), k_packed / v_packed are a page pool [n_pages*128, D/2] and
+    v_scale [n_pages*128, 1]; token t of (b, h) lives at pool row
+    ``page_table[b*Hkv + h, t // 128] * 128 + t % 128``.  ``lens`` / ``max_len``
+    give the tokens per batch row (``max_len`` defaults to the table's capacity)."""
 
     k_packed: Tensor
     k_scale: Tensor
@@ -43,6 +49,7 @@ class Int4Tier:
     v_scale: Tensor
     lens: Tensor | None = None
     max_len: int | None = None
+    page_table: Tensor | None = None
 
 
 @dataclass
@@ -156,7 +163,40 @@ def align_tier(tier, D: int):
     return dataclasses.replace(tier, **changes)
 
 
+def _fill_paged(seg: _lib.KVSegment, tier: Int4Tier, D: int, dtype: torch.dtype) -> list:
+    """A paged INT4 middle: page pool + block table (see Int4Tier)."""
+    seg.kind = _lib.SEG_INT4
+    rb = D // 2
+    kp, vp, vs, pt = tier.k_packed, tier.v_packed, tier.v_scale, tier.page_table
+    if kp.dim() != 2 or kp.shape[1] != rb or not kp.is_contiguous() or vp.shape != kp.shape or not vp.is_contiguous():
+        raise ValueError("paged middle: k_packed / v_packed must be contiguous pools [n_pages*128, D/2]")
+    rows = int(kp.shape[0])
+    if rows % _lib.PAGE_TOKENS or kp.storage_offset() % 128 or vp.storage_offset() % 128:
+        raise ValueError("paged middle: pools must hold whole 128-token pages and start 128-byte aligned")
+    if vs.dtype != dtype or vs.numel() != rows or not vs.is_contiguous():
+        raise ValueError("paged middle: v_scale must be a contiguous [n_pages*128, 1] pool in the model dtype")
+    if pt.dtype != torch.int32 or pt.dim() != 2 or not pt.is_contiguous():
+        raise ValueError("page_table must be a contiguous int32 [B*Hkv, pages_per_row] tensor")
+    ks = tier.k_scale
+    if ks.dtype != dtype or ks.stride(-1) != 1:
+        raise ValueError("k_scale must be contiguous in D and in the model dtype")
+    seg.k, seg.v = kp.data_ptr(), vp.data_ptr()
+    seg.row_sb = seg.row_sh = 0
+    seg.k_scale, seg.ks_sb, seg.ks_sh = ks.data_ptr(), ks.stride(0), ks.stride(1)
+    seg.v_scale = vs.data_ptr()
+    seg.page_table, seg.pages_per_row = pt.data_ptr(), int(pt.shape[1])
+    cap = int(pt.shape[1]) * _lib.PAGE_TOKENS
+    seg.max_len = int(tier.max_len) if tier.max_len is not None else cap
+    seg.len = seg.max_len
+    if tier.lens is not None:
+        seg.lens = tier.lens.data_ptr()
+    seg.n_rows = rows
+    return [kp, vp, ks, vs, pt, tier.lens]
+
+
 def _fill_mid(seg: _lib.KVSegment, tier, D: int, dtype: torch.dtype) -> list:
+    if isinstance(tier, Int4Tier) and tier.page_table is not None:
+        return _fill_paged(seg, tier, D, dtype)
     if isinstance(tier, Int4Tier):
         seg.kind, kb, vb = _lib.SEG_INT4, 4, 4
     elif isinstance(tier, Int4K2VTier):
@@ -249,7 +289,7 @@ class DecodePlan:
                 h = t.k.shape[1]
                 keep += _fill_fp(d.seg[n], t, D)
             else:
-                h = t.k_packed.shape[1]
+                h = t.k_scale.shape[1] if getattr(t, "page_table", None) is not None else t.k_packed.shape[1]
                 keep += _fill_mid(d.seg[n], t, D, dtype)
                 if isinstance(t, RotTier):
                     R = t.rotation

@@ -55,6 +55,7 @@ namespace fade {
 
 constexpr int kConsumerWarps = 4;  // per consumer group; 32 tokens of a stage each
 constexpr int kStageTokens = 128;  // 32 tokens per consumer warp
+static_assert(kStageTokens == FADE_PAGE_TOKENS, "a page of a paged middle is one streaming unit");
 // One middle CTA per SM: G consumer groups (3 for up to 8 query rows per kv
 // head; 1 above, where the wider state needs the registers) share one
 // producer warp and one ring of stages; group g
@@ -375,6 +376,8 @@ struct MidParams {
     const int32_t* lens;
     int64_t len;
     const int32_t* cu_units;        // ragged: [Z+1]; null = uniform
+    const int32_t* page_table;      // paged middle: [Z][pages_per_row] page ids, or null
+    int64_t pages_per_row;
     int units_per_z;                // uniform case
     int n_ctas;
     float* ws_ml;                   // [U][rows][2] partial (max, sum), log2 domain
@@ -992,7 +995,10 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             }
             if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.ws_err)) continue;
             const int64_t tok0 = (int64_t)(u - zb) * kStageTokens;
-            const int64_t row0 = zrow0 + tok0;
+            // a unit is one page of a paged middle (kStageTokens == FADE_PAGE_TOKENS)
+            const int64_t row0 = p.page_table
+                ? (int64_t)__ldg(p.page_table + (int64_t)z * p.pages_per_row + (u - zb)) * kStageTokens
+                : zrow0 + tok0;
             const int64_t len = zlen;
             uint8_t* st = smem + s * L::STAGE_BYTES;
             // Units past this row's length (uniform grid over a capacity bound)
@@ -2251,6 +2257,7 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
         if (!s.k || !s.v || !s.k_scale || !s.v_scale) return FADE_ERR_INVALID_ARG;
         if (!aligned16(s.k) || !aligned16(s.v)) return FADE_ERR_ALIGN;
         if (s.lens && s.max_len <= 0 && !d->cu_units) return FADE_ERR_INVALID_ARG;
+        if (s.page_table && (s.pages_per_row <= 0 || s.n_rows <= 0)) return FADE_ERR_INVALID_ARG;
     }
     const int Z = d->B * d->Hkv;
     pl->units_per_z = 0;
@@ -2342,6 +2349,7 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
         if (rg.kind != FADE_SEG_FP || md.kind != FADE_SEG_INT4) return FADE_ERR_UNSUPPORTED;
         if (d->n_q != 1 || !a->k_new || !a->v_new || !md.lens || md.max_len <= 0) return FADE_ERR_INVALID_ARG;
         if (rg.lens || rg.len != a->ring_cap || a->ring_cap <= 0) return FADE_ERR_INVALID_ARG;
+        if (md.page_table) return FADE_ERR_UNSUPPORTED;   // the age-out writes dense rows
     }
     if (d->B == 0) return FADE_OK;
     if (!d->q || !d->out) return FADE_ERR_INVALID_ARG;
@@ -2377,7 +2385,7 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
         const int64_t maxlen = sg.lens ? sg.max_len : sg.len;
         int64_t n_rows = sg.n_rows;
         if (n_rows <= 0) {
-            if (sg.row_base) return FADE_ERR_INVALID_ARG;
+            if (sg.row_base || sg.page_table) return FADE_ERR_INVALID_ARG;
             n_rows = (int64_t)(d->B - 1) * sg.row_sb + (int64_t)(d->Hkv - 1) * sg.row_sh + maxlen;
         }
         if (n_rows <= 0) n_rows = 1;
@@ -2416,6 +2424,8 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
         mp.row_sb = sg.row_sb; mp.row_sh = sg.row_sh; mp.row_base = sg.row_base;
         mp.lens = sg.lens; mp.len = sg.len;
         mp.cu_units = d->cu_units;
+        mp.page_table = sg.page_table;
+        mp.pages_per_row = sg.pages_per_row;
         mp.units_per_z = pl.units_per_z;
         mp.n_ctas = pl.n_ctas;
         mp.ws_ml = reinterpret_cast<float*>(ws + pl.off_ml);

@@ -205,8 +205,22 @@ typedef struct fade_kv_segment {
     int64_t max_len;         /* bound on lens[] (sizes the grid)                */
     int64_t ks_sb, ks_sh;
     int64_t n_rows;          /* rows held by k/v (bounds the TMA reads); 0 = derive
-                                from the dense strides (required with row_base) */
+                                from the dense strides (required with row_base or
+                                page_table) */
+    /* Paged middle (quantised tiers; FADE_PAGE_TOKENS-token pages): when
+     * page_table is set, token t of (b,h) lives at row
+     *   page_table[(b*Hkv+h)*pages_per_row + t/FADE_PAGE_TOKENS]*FADE_PAGE_TOKENS
+     *   + t%FADE_PAGE_TOKENS
+     * of a shared page pool (codes, per-token V scales; grouped V scales at
+     * row/group) instead of row_base / row_sb / row_sh.  Device int32 table.
+     * Not combined with fade_decode_attn_age_out (FADE_ERR_UNSUPPORTED).
+     * (Block tables for continuous batching; the reference's roadmap item A1,
+     * it has no paged layout itself.) */
+    const int32_t* page_table;
+    int64_t pages_per_row;
 } fade_kv_segment;
+
+#define FADE_PAGE_TOKENS 128
 
 #define FADE_MAX_SEGMENTS 4
 

@@ -342,3 +342,59 @@ def test_fused_int4_sdpa_dropin(cuda_device, causal, Sq, Sk):
         n = min(m + 1, Sk) if causal else Sk
         ref = oa.sdpa(q[:, :, m:m + 1], kd[:, :, :n], vd[:, :, :n])
         assert_attn_close(out[:, :, m:m + 1], ref, dt, TOL[dt], ulps=2 if n <= 16 else 1)
+
+
+def test_paged_int4_middle(cuda_device):
+    """A paged middle (128-token pages scattered over a shared pool, a block
+    table per (b, h), ragged lengths) gives the oracle's attention, and the
+    same result as the contiguous layout of the same tokens."""
+    from fade_b200.attention import FPTier, Int4Tier, tiered_decode_attention
+
+    dt = "bf16"
+    B, Hq, Hkv, D, cap = 3, 8, 2, 128, 1024
+    lens = np.array([1000, 130, 640], dtype=np.int32)
+    x = seeded_outliers((B, Hkv, cap, D), 81, dt)
+    v = seeded_outliers((B, Hkv, cap, D), 82, dt)
+    kp = np.zeros((B, Hkv, cap, D // 2), np.uint8)
+    vp = np.zeros_like(kp)
+    ks = np.zeros((B, Hkv, 1, D), np.float32)
+    vs = np.zeros((B, Hkv, cap, 1), np.float32)
+    for b in range(B):
+        n = lens[b]
+        kp[b:b + 1, :, :n], ks[b:b + 1] = oq.quant_k_int4(x[b:b + 1, :, :n], dt)
+        vp[b:b + 1, :, :n], vs[b:b + 1, :, :n] = oq.quant_v_int4(v[b:b + 1, :, :n], dt)
+    ppr = cap // 128
+    rng = np.random.default_rng(5)
+    n_pages = B * Hkv * ppr + 3
+    perm = rng.permutation(n_pages)[:B * Hkv * ppr].astype(np.int32)     # scattered, some pool pages unused
+    table = perm.reshape(B * Hkv, ppr)
+    pool_k = np.zeros((n_pages * 128, D // 2), np.uint8)
+    pool_v = np.zeros_like(pool_k)
+    pool_s = np.full((n_pages * 128, 1), 0.0, np.float32)
+    for z in range(B * Hkv):
+        b, h = divmod(z, Hkv)
+        for pg in range(ppr):
+            r = table[z, pg] * 128
+            pool_k[r:r + 128] = kp[b, h, pg * 128:(pg + 1) * 128]
+            pool_v[r:r + 128] = vp[b, h, pg * 128:(pg + 1) * 128]
+            pool_s[r:r + 128] = vs[b, h, pg * 128:(pg + 1) * 128]
+    q = from_bits_dt(rng.standard_normal((B, Hq, 1, D)).astype(np.float32), dt)
+    sink = seeded_outliers((B, Hkv, 4, D), 83, dt)
+    qt = np_to_dt_tensor(q, dt)
+    lens_t = torch.from_numpy(lens).cuda()
+    fp = FPTier(np_to_dt_tensor(sink, dt), np_to_dt_tensor(sink, dt))
+    paged = Int4Tier(torch.from_numpy(pool_k).cuda(), np_to_dt_tensor(ks, dt), torch.from_numpy(pool_v).cuda(),
+                     np_to_dt_tensor(pool_s, dt), lens=lens_t, max_len=cap,
+                     page_table=torch.from_numpy(table).cuda())
+    dense = Int4Tier(torch.from_numpy(kp).cuda(), np_to_dt_tensor(ks, dt), torch.from_numpy(vp).cuda(),
+                     np_to_dt_tensor(vs, dt), lens=lens_t, max_len=cap)
+    units = np.repeat(-(-lens // 128), Hkv)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(units)]).astype(np.int32)).cuda()
+    out_p = t_vals(tiered_decode_attention(qt, [fp, paged], cu_units=cu))
+    out_d = t_vals(tiered_decode_attention(qt, [fp, dense], cu_units=cu))
+    np.testing.assert_array_equal(out_p, out_d)      # same tokens, same order of work
+    for b in range(B):
+        n = lens[b]
+        t = {"sink_k": sink[b:b + 1], "sink_v": sink[b:b + 1], "int4_kq": kp[b:b + 1, :, :n],
+             "int4_ks": ks[b:b + 1], "int4_vq": vp[b:b + 1, :, :n], "int4_vs": vs[b:b + 1, :, :n]}
+        assert_attn_close(out_p[b:b + 1], oa.tiered_attention(q[b:b + 1], t, dt), dt, TOL[dt])
