@@ -310,12 +310,31 @@ template <int DT> struct Conv {
         for (int i = 0; i < 8; ++i)
             h[i] = Pk<DT>::sub(lop3_and_xor(x >> (2 * i), 0x00030003u, Pk<DT>::K2), Pk<DT>::B2);
     }
-    // the same fields as the biased values kBias2 + code (no subtraction)
+    // bf16, biased and scaled by powers of 4: fields 3, 2, 1 of a byte are
+    // masked where they lie (bits 0-1, 2-3, 4-5 sit inside the 7 mantissa
+    // bits of bf16(128 + m)), field 0 (bits 6-7) is shifted down.  h[i] holds
+    // the same fields as int2() but as the exact value F * (code + 2) + 128,
+    // F = 1, 4, 16, 1 for fields 3, 2, 1, 0 (the channel's kF2 factor), so a
+    // word of 16 codes takes 3 shifts + 8 lop3 instead of 8 + 8.
     __device__ __forceinline__ static void int2_biased(uint32_t x, uint32_t (&h)[8]) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) h[i] = lop3_and_xor(x >> (2 * i), 0x00030003u, Pk<DT>::K2);
+        static_assert(DT == FADE_BF16, "scaled biased 2-bit conversion is bf16 only");
+        const uint32_t y = x >> 8;
+        h[0] = lop3_and_xor(x, 0x00030003u, 0x43024302u);
+        h[1] = lop3_and_xor(x, 0x000C000Cu, 0x43084308u);
+        h[2] = lop3_and_xor(x, 0x00300030u, 0x43204320u);
+        h[3] = lop3_and_xor(x >> 6, 0x00030003u, 0x43024302u);
+        h[4] = lop3_and_xor(y, 0x00030003u, 0x43024302u);
+        h[5] = lop3_and_xor(y, 0x000C000Cu, 0x43084308u);
+        h[6] = lop3_and_xor(y, 0x00300030u, 0x43204320u);
+        h[7] = lop3_and_xor(x >> 14, 0x00030003u, 0x43024302u);
     }
 };
+
+// Channel d of a 2-bit row is field d % 4 of its byte; int2_biased() returns
+// it as kF2(d) * code + kH2(d) (kH2 = 128 + 2 * kF2).
+__host__ __device__ constexpr float kF2(int d) { return (d & 3) == 1 ? 16.f : (d & 3) == 2 ? 4.f : 1.f; }
+__host__ __device__ constexpr float kInvF2(int d) { return (d & 3) == 1 ? 0.0625f : (d & 3) == 2 ? 0.25f : 1.f; }
+__host__ __device__ constexpr float kH2(int d) { return 128.f + 2.f * kF2(d); }
 
 // ---------------------------------------------------------------------------
 // Channel maps.  For the K operand, k-step ks and slot s in {0,1,2,3} (= the
@@ -910,15 +929,22 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // exactly: K's per-channel scale into the fp32 query (before its hi + lo
     // split), V's per-token scale into P.  The codes enter the MMA as is.
     constexpr bool FOLD2 = KB == 2 && VB == 2 && !VGROUP && QSPLIT;
-    // bf16 with folded scales: the codes enter the MMA as 130 + c (the magic-
-    // exponent value, no subtraction) and the bias is removed algebraically:
-    // K: scores start from -130 * sum_d q'_d; V: O loses 130 * sum_t p'_t
-    // (accumulated from the same rounded P' the MMA consumes) at each flush.
+    // bf16 with folded scales: the codes of channel d enter the MMA as
+    // F_d * c + H_d (int2_biased(): the magic-exponent value, no subtraction,
+    // F_d a power of 4) and both are removed exactly: K: the query channel is
+    // pre-multiplied by 1 / F_d and scores start from -sum_d q'_d H_d / F_d;
+    // V: at each flush O_d = (O_d - H_d sum_t p'_t) / F_d, the sum taken over
+    // the same rounded P' the MMA consumes.
     constexpr bool FOLD2B = FOLD2 && DT == FADE_BF16;
-    constexpr float kBias2 = 130.f;
+    // QK accumulators split in two (shorter dependent MMA chains) where the
+    // registers allow it without spilling
+    constexpr bool kSplitAcc = KB == 2 || (!QSPLIT && !VGROUP);
 
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base, derived from smem_raw by pointer arithmetic (not
+    // an integer round trip) so every pointer taken from it stays in the
+    // shared address space and its loads compile to shared, not generic, loads
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int G = L::G, NS = L::NS;
     constexpr int PRODUCER = G * kConsumerWarps;   // first producer warp (one per group)
     constexpr int FPWARP = PRODUCER + G;            // the FP-tier warp
@@ -1139,8 +1165,13 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                         const int ks = cb * (CHW / 16) + u;
 #pragma unroll
                         for (int hs = 0; hs < 2; ++hs) {
-                            const float v0 = e[KMap::kdim(ks, 2 * hs, t) - cb * CHW - CH * t];
-                            const float v1 = e[KMap::kdim(ks, 2 * hs + 1, t) - cb * CHW - CH * t];
+                            const int d0 = KMap::kdim(ks, 2 * hs, t), d1 = KMap::kdim(ks, 2 * hs + 1, t);
+                            float v0 = e[d0 - cb * CHW - CH * t];
+                            float v1 = e[d1 - cb * CHW - CH * t];
+                            if constexpr (FOLD2B) {   // powers of 2: exact
+                                v0 *= kInvF2(d0);
+                                v1 *= kInvF2(d1);
+                            }
                             const uint32_t hp = P::pack(v0, v1);
                             const float h0 = P::unpack_lo(hp), h1 = P::unpack_lo(hp >> 16);
                             qf[0][nt][ks][hs] = hp;
@@ -1185,12 +1216,13 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     for (int ks = 0; ks < KSTEPS; ++ks)
 #pragma unroll
                         for (int hs = 0; hs < 2; ++hs)
-                            sum += P::unpack_lo(qf[qs][nt][ks][hs]) + P::unpack_lo(qf[qs][nt][ks][hs] >> 16);
+                            sum += kH2(KMap::kdim(ks, 2 * hs, t)) * P::unpack_lo(qf[qs][nt][ks][hs]) +
+                                   kH2(KMap::kdim(ks, 2 * hs + 1, t)) * P::unpack_lo(qf[qs][nt][ks][hs] >> 16);
                 sum += __shfl_xor_sync(0xffffffffu, sum, 1);
                 sum += __shfl_xor_sync(0xffffffffu, sum, 2);
                 // C-fragment columns 2t, 2t+1 are query rows held by lanes 8t, 8t+4
-                kb[nt][0] = kBias2 * __shfl_sync(0xffffffffu, sum, (2 * t) * 4);
-                kb[nt][1] = kBias2 * __shfl_sync(0xffffffffu, sum, (2 * t + 1) * 4);
+                kb[nt][0] = __shfl_sync(0xffffffffu, sum, (2 * t) * 4);
+                kb[nt][1] = __shfl_sync(0xffffffffu, sum, (2 * t + 1) * 4);
             }
         }
         cur_len = seg_len(p, b);
@@ -1231,7 +1263,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 }
         }
         named_bar_sync(bar_id, kConsumerWarps * 32);
-        if constexpr (FOLD2B) {   // remove the code bias: O -= 130 * sum_t P'
+        if constexpr (FOLD2B) {   // remove the code bias and factor: O_d = (O_d - H_d sum_t P') / F_d
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1240,11 +1272,12 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     q += __shfl_xor_sync(0xffffffffu, q, 4);
                     q += __shfl_xor_sync(0xffffffffu, q, 8);
                     q += __shfl_xor_sync(0xffffffffu, q, 16);
-                    const float bias = kBias2 * q;
 #pragma unroll
                     for (int mi = 0; mi < MT; ++mi) {
-                        o[nt][mi][e] -= bias;
-                        o[nt][mi][e + 2] -= bias;
+                        // C-fragment rows gid, gid + 8 are channels vdim(mi, 0 / 1, gid); d % 4 = 2 (mi % 2) + hr
+                        const int d0 = 2 * (mi & 1), d1 = 2 * (mi & 1) + 1;
+                        o[nt][mi][e] = (o[nt][mi][e] - kH2(d0) * q) * kInvF2(d0);
+                        o[nt][mi][e + 2] = (o[nt][mi][e + 2] - kH2(d1) * q) * kInvF2(d1);
                     }
                 }
         }
@@ -1350,6 +1383,16 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) sacc[mt][nt][e] = FOLD2B ? -kb[nt][e & 1] : 0.f;
+                // Two accumulators per tile halve the dependent MMA chain: the
+                // low query part (or the odd k-steps) goes to sacc2.
+                float sacc2[NT][4];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) sacc2[nt][e] = 0.f;
+                auto acc = [&](int ks, int qs, int nt) -> float (&)[4] {
+                    return kSplitAcc && (NQ == 2 ? qs == 1 : (ks & 1) == 1) ? sacc2[nt] : sacc[mt][nt];
+                };
                 uint32_t kr[2][L::NCHK];
                 load_tiles_at<L::NCHK, false>(kbase, koffs, mt, kr);
 #pragma unroll
@@ -1369,7 +1412,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
                                 for (int nt = 0; nt < NT; ++nt)
-                                    P::mma(sacc[mt][nt], a0, a1, a2, a3,
+                                    P::mma(acc(ks, qs, nt), a0, a1, a2, a3,
                                            qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     } else {
@@ -1392,11 +1435,15 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
                                 for (int nt = 0; nt < NT; ++nt)
-                                    P::mma(sacc[mt][nt], a0, a1, a2, a3,
+                                    P::mma(acc(ks, qs, nt), a0, a1, a2, a3,
                                            qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     }
                 }
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) sacc[mt][nt][e] += sacc2[nt][e];
             }
             // ---- online softmax over the 32 tokens (log2 domain) ----
             // Scores stay unscaled; the running maxima are in scaled units
@@ -1614,57 +1661,91 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
 }
 
 // ---------------------------------------------------------------------------
-// k0: q_rot = q @ R^T (fp32), one CTA per query row
+// k0: q_rot = q @ R^T (fp32), kRotRows query rows per CTA
 // ---------------------------------------------------------------------------
 constexpr int kRotRows = 16;   // query rows per rotate_queries CTA
+constexpr int kRotQS = 20;     // padded row of the transposed query tile (16-byte multiple)
 
-// q_rot[row][d] = sum_e q[row][e] * R[d][e] in fp32, summed in e order with
-// no FMA contraction (deterministic).  One CTA per kRotRows query rows, one
-// thread per output channel; R is staged once per CTA, transposed, so the
-// threads of a warp read consecutive words.
-template <int DT>
-__global__ void rotate_queries_kernel(const void* q, int Hq, int n_q, int D, int64_t q_sb,
-                                      int64_t q_sh, int64_t q_ss, const float* __restrict__ R,
-                                      float* __restrict__ q_rot, int n_rows) {
-    extern __shared__ float rsm[];
-    const int RS = D + 1;          // padded row: the transposed store is conflict-free
-    float* rt = rsm;               // [D][RS]: rt[e*RS + d] = R[d][e]
-    float* qs = rsm + D * RS;      // [kRotRows][D]
-    griddep_wait();              // q and R may come from the preceding kernel
+// q_rot[row][d] = sum_e q[row][e] * R[d][e] in fp32 (FMA, e ascending:
+// deterministic).  2 * D threads per CTA, each owning a 2-row x 4-channel
+// tile of the CTA's kRotRows x D block, so one e step is an 8-byte and a
+// 16-byte shared load (2 query values, 4 consecutive R^T values) and 8 FMAs.
+// R^T and the transposed query tile are staged in shared memory once per CTA
+// with every global load of a thread issued before its stores (trip counts
+// are compile-time), so staging costs about one L2 round trip, not one per
+// load; R^T stores go lane -> channel, conflict-free.
+template <int DT, int D>
+__global__ void __launch_bounds__(2 * D) rotate_queries_kernel(const void* q, int Hq, int n_q, int64_t q_sb,
+                                                             int64_t q_sh, int64_t q_ss,
+                                                             const float* __restrict__ R,
+                                                             float* __restrict__ q_rot, int n_rows) {
+    constexpr int NT = 2 * D, D4 = D / 4;
+    constexpr int RP = D * D4 / NT;          // float4 pieces of R per thread
+    constexpr int QP = kRotRows * D / NT;    // query elements per thread
+    extern __shared__ __align__(16) float rsm[];
+    float* rt = rsm;               // [D][D]: rt[e*D + d] = R[d][e]
+    float* qt = rsm + D * D;       // [D][kRotQS]: qt[e*kRotQS + r] = q[row0 + r][e]
+    griddep_wait();                // q and R may come from the preceding kernel
     griddep_launch_dependents();
-    // R in 16-byte pieces, 8 loads in flight per thread
-#pragma unroll 8
-    for (int i = threadIdx.x * 4; i < D * D; i += blockDim.x * 4) {
-        const float4 r4 = __ldg(reinterpret_cast<const float4*>(R + i));
-        const int d = i / D, e = i % D;
-        rt[e * RS + d] = r4.x;
-        rt[(e + 1) * RS + d] = r4.y;
-        rt[(e + 2) * RS + d] = r4.z;
-        rt[(e + 3) * RS + d] = r4.w;
-    }
+    const int tid = threadIdx.x;
     const int row0 = blockIdx.x * kRotRows;
     const int nr = (n_rows - row0) < kRotRows ? (n_rows - row0) : kRotRows;
-    for (int i = threadIdx.x; i < nr * D; i += blockDim.x) {
-        const int r = i / D, d = i % D;
-        const int row = row0 + r;   // (b*Hq + hq)*n_q + s
-        const int s = row % n_q, bh = row / n_q;
-        const int hq = bh % Hq, b = bh / Hq;
-        qs[r * D + d] = load_f<DT>(q, (int64_t)b * q_sb + (int64_t)hq * q_sh + (int64_t)s * q_ss + d);
+    float4 r4[RP];
+    float qv[QP];
+#pragma unroll
+    for (int k = 0; k < RP; ++k) {
+        const int i = tid + k * NT, d = i % D, e = (i / D) * 4;
+        r4[k] = __ldg(reinterpret_cast<const float4*>(R + d * D + e));
+    }
+#pragma unroll
+    for (int k = 0; k < QP; ++k) {
+        const int i = tid + k * NT, r = i / D, e = i % D;
+        qv[k] = 0.f;
+        if (r < nr) {
+            const int row = row0 + r;   // (b*Hq + hq)*n_q + s
+            const int s = row % n_q, bh = row / n_q;
+            const int hq = bh % Hq, b = bh / Hq;
+            qv[k] = load_f<DT>(q, (int64_t)b * q_sb + (int64_t)hq * q_sh + (int64_t)s * q_ss + e);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < RP; ++k) {
+        const int i = tid + k * NT, d = i % D, e = (i / D) * 4;
+        rt[e * D + d] = r4[k].x;
+        rt[(e + 1) * D + d] = r4[k].y;
+        rt[(e + 2) * D + d] = r4[k].z;
+        rt[(e + 3) * D + d] = r4[k].w;
+    }
+#pragma unroll
+    for (int k = 0; k < QP; ++k) {
+        const int i = tid + k * NT;
+        qt[(i % D) * kRotQS + i / D] = qv[k];
     }
     __syncthreads();
-    const int d = threadIdx.x;
-    if (d >= D) return;
-    float acc[kRotRows];
+    const int tc = tid % D4, tr = tid / D4;   // channels 4tc.., rows 2tr, 2tr+1
+    float acc[2][4];
 #pragma unroll
-    for (int r = 0; r < kRotRows; ++r) acc[r] = 0.f;
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+#pragma unroll 8
     for (int e = 0; e < D; ++e) {
-        const float re = rt[e * RS + d];
+        const float2 qa = *reinterpret_cast<const float2*>(qt + e * kRotQS + 2 * tr);
+        const float4 rv = *reinterpret_cast<const float4*>(rt + e * D + 4 * tc);
+        const float ra[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-        for (int r = 0; r < kRotRows; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(qs[r * D + e], re));
+        for (int j = 0; j < 4; ++j) {
+            acc[0][j] = fmaf(qa.x, ra[j], acc[0][j]);
+            acc[1][j] = fmaf(qa.y, ra[j], acc[1][j]);
+        }
     }
 #pragma unroll
-    for (int r = 0; r < kRotRows; ++r)
-        if (r < nr) q_rot[(int64_t)(row0 + r) * D + d] = acc[r];
+    for (int i = 0; i < 2; ++i) {
+        const int r = 2 * tr + i;
+        if (r < nr)
+            *reinterpret_cast<float4*>(q_rot + (int64_t)(row0 + r) * D + 4 * tc) =
+                make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -2296,7 +2377,7 @@ static int make_plan(const fade_decode_desc* d, Plan* pl) {
 // The query rotation stages R (up to 64 KB) in shared memory: opt in once per
 // device and kernel instantiation.
 static cudaError_t rotate_queries_smem_attr(const void* fn, int which) {
-    static bool done[kMaxDevices][2] = {};
+    static bool done[kMaxDevices][4] = {};
     static std::mutex mu;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -2304,7 +2385,7 @@ static cudaError_t rotate_queries_smem_attr(const void* fn, int which) {
     if (dev < 0 || dev >= kMaxDevices) dev = 0;
     std::lock_guard<std::mutex> lock(mu);
     if (!done[dev][which]) {
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (128 * 129 + kRotRows * 128) * 4);
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (128 * 128 + 128 * kRotQS) * 4);
         if (e != cudaSuccess) return e;
         done[dev][which] = true;
     }
@@ -2363,17 +2444,18 @@ static int decode_attn_impl(const fade_decode_desc* d, const fade_age_out_desc* 
     const float qk_scale = d->sm_scale * kLog2e;
 
     if (rot) {
-        void* fn = d->dtype == FADE_F16 ? (void*)&rotate_queries_kernel<FADE_F16>
-                                        : (void*)&rotate_queries_kernel<FADE_BF16>;
+        const bool f16 = d->dtype == FADE_F16, d64 = d->D == 64;
+        void* fn = f16 ? (d64 ? (void*)&rotate_queries_kernel<FADE_F16, 64> : (void*)&rotate_queries_kernel<FADE_F16, 128>)
+                       : (d64 ? (void*)&rotate_queries_kernel<FADE_BF16, 64> : (void*)&rotate_queries_kernel<FADE_BF16, 128>);
         const void* qp = d->q;
         int Hq = d->Hq, nq = d->n_q, D = d->D;
         int64_t a = d->q_sb, b2 = d->q_sh, c2 = d->q_ss;
         const float* R = d->rotation;
         int n_rows = d->B * d->Hq * d->n_q;
-        void* args[] = {(void*)&qp, &Hq, &nq, &D, &a, &b2, &c2, (void*)&R, (void*)&qrot, &n_rows};
-        const size_t rsmem = (size_t)(D * (D + 1) + kRotRows * D) * 4;
-        FADE_CUDA_TRY(rotate_queries_smem_attr(fn, d->dtype == FADE_F16 ? 0 : 1));
-        FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)((n_rows + kRotRows - 1) / kRotRows)), dim3((unsigned)D),
+        void* args[] = {(void*)&qp, &Hq, &nq, &a, &b2, &c2, (void*)&R, (void*)&qrot, &n_rows};
+        const size_t rsmem = (size_t)(D * D + D * kRotQS) * 4;
+        FADE_CUDA_TRY(rotate_queries_smem_attr(fn, (f16 ? 0 : 2) + (d64 ? 0 : 1)));
+        FADE_CUDA_TRY(launch_pdl(fn, dim3((unsigned)((n_rows + kRotRows - 1) / kRotRows)), dim3((unsigned)(2 * D)),
                                  rsmem, s, args));
     }
     if (has_mid) {
