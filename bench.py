@@ -89,6 +89,8 @@ def parse():
     ap.add_argument("--reserve-sms", type=int, default=None,
                     help="multi-GPU heads partition with side-stream gathers: SMs left free of the persistent "
                          "middle kernel so the collective overlaps it (default 8)")
+    ap.add_argument("--middle", choices=("mma_sync", "tcgen05"), default="mma_sync",
+                    help="middle kernel for INT4 K and V at head_dim 128 (configs 2 and 5)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="layers per step (profiling captures use 1)")
@@ -100,6 +102,7 @@ def parse():
         CFG["layers"] = args.layers
     if args.batch:
         CFG["batch"] = args.batch
+    CFG["middle"] = args.middle
     return args
 
 
@@ -335,7 +338,7 @@ def config_block(ws: int, parallelism: str) -> dict:
            "n_kv_heads": c["n_kv_heads"], "head_dim": c["head_dim"], "parallelism": parallelism}
     if c["kind"] == "int4":
         blk.update(batch_per_gpu=c["batch"], global_batch=c["batch"] * ws, context=c["context"],
-                   n_sink=c["n_sink"], recent=c["recent"])
+                   n_sink=c["n_sink"], recent=c["recent"], middle_kernel=c.get("middle", "mma_sync"))
     return blk
 
 
@@ -380,11 +383,13 @@ def run_int4(args, ws, rank, local):
     import torch
     import torch.distributed as dist
 
+    from fade_b200.attention import set_middle_kernel
     from fade_b200.shard import gather_objects, max_over_ranks, shard_plan
 
     c = CFG
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    set_middle_kernel(c["middle"])
     K, W = args.steps, max(3, args.warmup)
     L = c["layers"]
     mode = args.shard or "heads"

@@ -167,6 +167,8 @@ _SIGNATURES = {
     "fade_decode_attn_noalloc_max_bytes": (ctypes.c_size_t, []),
     "fade_decode_attn_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeDesc), _vp]),
     "fade_decode_attn_noalloc_check": (ctypes.c_int, [_vp]),
+    "fade_set_middle_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "fade_get_middle_kernel": (ctypes.c_int, []),
 }
 
 _lib = None

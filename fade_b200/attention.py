@@ -435,7 +435,26 @@ def fused_int4_sdpa(q: Tensor, k_packed: Tensor, k_scale: Tensor, v_packed: Tens
     return out
 
 
+_MIDDLE_KERNELS = {"mma_sync": 0, "tcgen05": 1}
+
+
+def set_middle_kernel(kind: str) -> None:
+    """Choose the middle kernel for INT4 K and V at head_dim 128: ``"mma_sync"``
+    (default) or ``"tcgen05"`` (tensor-memory accumulators).  Process-wide;
+    takes effect for calls made (or graphs captured) afterwards."""
+    if kind not in _MIDDLE_KERNELS:
+        raise ValueError(f"middle kernel must be one of {sorted(_MIDDLE_KERNELS)}, got {kind!r}")
+    _lib.check(_lib.load().fade_set_middle_kernel(_MIDDLE_KERNELS[kind]), "fade_set_middle_kernel")
+
+
+def get_middle_kernel() -> str:
+    code = _lib.load().fade_get_middle_kernel()
+    return {v: k for k, v in _MIDDLE_KERNELS.items()}[code]
+
+
 __all__ = [
+    "get_middle_kernel",
+    "set_middle_kernel",
     "DecodePlan",
     "FPTier",
     "Int4K2VTier",

@@ -47,6 +47,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -619,7 +620,7 @@ __device__ __forceinline__ void load_tiles(uint32_t base, int trow0, int lane, u
 // and the new token is written into the freed ring slot.
 // ---------------------------------------------------------------------------
 template <int DT, int D, int NT>
-__device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, uint8_t* fsm, bool waited) {
+__device__ __forceinline__ void fp_rows_warp_body(const MidParams& p, int c, int n_cta, uint8_t* fsm, bool waited) {
     using T = typename Elem<DT>::T;
     using P = Pk<DT>;
     constexpr int KSTEPS = D / 16, MT = D / 16;
@@ -907,6 +908,15 @@ __device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, 
         __syncwarp();
     }
 }
+
+// The FP-tier warp as a call of its own in the mma.sync middle kernel (keeps
+// that kernel's register allocation unchanged); the tcgen05 kernel inlines
+// the body, where a call would keep its arrays in local memory.
+template <int DT, int D, int NT>
+__device__ __noinline__ void fp_rows_warp(const MidParams& p, int c, int n_cta, uint8_t* fsm, bool waited) {
+    fp_rows_warp_body<DT, D, NT>(p, c, n_cta, fsm, waited);
+}
+
 
 // ---------------------------------------------------------------------------
 // k1: middle tier, persistent stream-K
@@ -1660,6 +1670,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     }
 }
 
+#include "middle_tc.cuh"
+
 // ---------------------------------------------------------------------------
 // k0: q_rot = q @ R^T (fp32), kRotRows query rows per CTA
 // ---------------------------------------------------------------------------
@@ -2254,8 +2266,37 @@ static MidKernelInfo select_mid(int kb, int vb, bool vg, bool rot) {
     return MidKernelInfo{nullptr, 0, 0, 0, 0};
 }
 
+template <int DT, int NT>
+static MidKernelInfo mid_tc_info() {
+    static MidKernelInfo info[kMaxDevices] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) dev = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    MidKernelInfo& i = info[dev];
+    if (!i.fn) {
+        i.smem = TcLayout::SMEM_BYTES;
+        cudaFuncSetAttribute(&middle_tc_kernel<DT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, i.smem);
+        int occ = 0;
+        i.threads = kTcThreads;
+        i.groups = 1;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, &middle_tc_kernel<DT, NT>, i.threads, i.smem);
+        i.occ = occ > 0 ? occ : 1;
+        i.fn = reinterpret_cast<void*>(&middle_tc_kernel<DT, NT>);
+    }
+    return i;
+}
+
+// Middle-kernel family for INT4 K and V at D = 128: 0 = mma.sync (default,
+// the faster one on B200), 1 = tcgen05 (fade_set_middle_kernel).  Read when a
+// call builds its plan; process-wide.
+static std::atomic<int> g_middle_kernel{0};
+
 template <int DT>
 static MidKernelInfo select_mid_d(int D, int NT, int kb, int vb, bool vg, bool rot) {
+    if (g_middle_kernel.load(std::memory_order_relaxed) == 1 && D == 128 && !rot && kb == 4 && vb == 4 && !vg)
+        return NT == 1 ? mid_tc_info<DT, 1>() : mid_tc_info<DT, 2>();
     if (D == 128) return NT == 1 ? select_mid<DT, 128, 1>(kb, vb, vg, rot) : select_mid<DT, 128, 2>(kb, vb, vg, rot);
     if (D == 64) return NT == 1 ? select_mid<DT, 64, 1>(kb, vb, vg, rot) : select_mid<DT, 64, 2>(kb, vb, vg, rot);
     return MidKernelInfo{nullptr, 0, 0, 0, 0};
@@ -2671,6 +2712,14 @@ extern "C" int fade_decode_attn_noalloc(const fade_decode_desc* d, void* stream)
     // stays visible until the caller asks for it, as with a workspace).
     return fade_decode_attn(d, ws, fade::kNoAllocScratchBytes, stream);
 }
+
+extern "C" int fade_set_middle_kernel(int kind) {
+    if (kind != 0 && kind != 1) return FADE_ERR_INVALID_ARG;
+    fade::g_middle_kernel.store(kind, std::memory_order_relaxed);
+    return FADE_OK;
+}
+
+extern "C" int fade_get_middle_kernel(void) { return fade::g_middle_kernel.load(std::memory_order_relaxed); }
 
 extern "C" int fade_decode_attn_noalloc_check(void* stream) {
     void* ws = nullptr;

@@ -314,6 +314,15 @@ int fade_decode_attn_noalloc(const fade_decode_desc* d, void* stream);
  * this call clears it. */
 int fade_decode_attn_noalloc_check(void* stream);
 
+/* Middle-kernel family for INT4 K and V at D = 128 (no counterpart in the
+ * reference): 0 = mma.sync (default), 1 = tcgen05 (dequantised K in tensor
+ * memory, V in shared memory, accumulators in tensor memory).  Both give
+ * results within the same tolerance of the reference; process-wide, read
+ * when a call builds its plan (plans already captured in a CUDA graph keep
+ * their kernel).  Returns FADE_ERR_INVALID_ARG for other values. */
+int fade_set_middle_kernel(int kind);
+int fade_get_middle_kernel(void);
+
 /* Reads and clears the device error word of a workspace (synchronises the
  * stream).  Returns FADE_OK or FADE_ERR_TIMEOUT. */
 int fade_workspace_check(void* workspace, size_t ws_bytes, void* stream);

@@ -5,6 +5,10 @@ from __future__ import annotations
 import ctypes
 import re
 
+import pytest
+
+from fade_b200 import _lib
+
 from conftest import ROOT
 
 
@@ -47,3 +51,19 @@ def test_status_strings_and_host_validation():
     d.dtype, d.B, d.Hq, d.Hkv, d.D, d.n_q = 0, 1, 4, 1, 96, 1
     assert lib.fade_decode_attn_workspace_size(ctypes.byref(d)) == 0  # D=96 not compiled
     assert lib.fade_version() >= 100
+
+
+def test_middle_kernel_switch():
+    """The middle-kernel choice is a host-side switch (no GPU needed)."""
+    from fade_b200.attention import get_middle_kernel, set_middle_kernel
+
+    assert get_middle_kernel() == "mma_sync"
+    with pytest.raises(ValueError):
+        set_middle_kernel("wgmma")
+    assert _lib.load().fade_set_middle_kernel(7) == _lib.FADE_ERR_INVALID_ARG
+    try:
+        set_middle_kernel("tcgen05")
+        assert get_middle_kernel() == "tcgen05"
+    finally:
+        set_middle_kernel("mma_sync")
+    assert get_middle_kernel() == "mma_sync"
