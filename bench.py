@@ -91,6 +91,9 @@ def parse():
                          "middle kernel so the collective overlaps it (default 8)")
     ap.add_argument("--middle", choices=("mma_sync", "tcgen05"), default="mma_sync",
                     help="middle kernel for INT4 K and V at head_dim 128 (configs 2 and 5)")
+    ap.add_argument("--hf", action="store_true",
+                    help="time a Hugging Face decode step (random-init Llama-3.1-8B-shaped model, config 2's "
+                         "batch and context) through create_tiered_cache: fused attention vs materialise + SDPA")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="layers per step (profiling captures use 1)")
@@ -914,6 +917,89 @@ def run_fade(args, ws, rank, local):
     return (run_h2o if kind == "h2o" else run_rot)(args)
 
 
+# --------------------------------------------------------------------------
+# Hugging Face decode step through the reference's public API
+# --------------------------------------------------------------------------
+def run_hf(args):
+    """One decode step of a random-init Llama-3.1-8B-shaped model (32 layers,
+    hidden 4096, 32 q / 8 kv heads, head_dim 128, bf16; random weights: no
+    checkpoints here) over config 2's batch and context, through
+    create_tiered_cache + model.forward as a generate() loop runs it: the
+    prompt is prefilled into the cache, each layer's middle is moved to INT4
+    (4 sink + 64 recent tokens kept in bf16), then K decode steps (one token
+    per sequence, greedy next token) are timed with CUDA events, once with the
+    fused tiered attention and once with the cache materialised and passed to
+    SDPA (fused_attention=False, the reference's decode path).  Host-side work
+    of each step (HF's Python, the cache's bookkeeping) is inside the timing."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from fade_b200.cache import TIER_FP16, TIER_INT4
+    from fade_b200.patch import create_tiered_cache
+
+    c = CFG
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, S = c["batch"], c["context"]
+    L = c["layers"]
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=L,
+                      num_attention_heads=c["n_q_heads"], num_key_value_heads=c["n_kv_heads"],
+                      rope_theta=500000.0, max_position_embeddings=131072)
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).eval()
+    torch.set_default_dtype(prev)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    ids = torch.randint(0, cfg.vocab_size, (B, S - 1), device=dev, generator=gen)
+    K, W = args.steps, max(3, args.warmup)
+    res = {}
+    from transformers import DynamicCache
+
+    for mode in ("fused", "materialise", "dynamic"):
+        if mode == "dynamic":   # transformers' own bf16 cache, no compression
+            cache = DynamicCache()
+        else:
+            cache = create_tiered_cache(model, dtype=torch.bfloat16, n_sink=c["n_sink"],
+                                        recent_window=c["recent"], fused_attention=(mode == "fused"))
+        with torch.no_grad():
+            nxt = model(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1).logits[:, -1]
+            if mode != "dynamic":
+                n = cache.get_seq_length(0)
+                t = torch.full((n,), TIER_INT4, dtype=torch.long)
+                t[:c["n_sink"]] = TIER_FP16
+                t[n - c["recent"]:] = TIER_FP16
+                for layer in range(L):
+                    cache.apply_tier_assignment(layer, t)
+            tok = nxt.argmax(-1, keepdim=True)
+            for _ in range(W):
+                tok = model(input_ids=tok, past_key_values=cache, use_cache=True,
+                            logits_to_keep=1).logits[:, -1].argmax(-1, keepdim=True)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(K):
+                tok = model(input_ids=tok, past_key_values=cache, use_cache=True,
+                            logits_to_keep=1).logits[:, -1].argmax(-1, keepdim=True)
+            e1.record()
+            torch.cuda.synchronize(dev)
+        res[mode] = e0.elapsed_time(e1) / K
+        del cache
+        torch.cuda.empty_cache()
+    print(json.dumps({
+        "metric": "HF decode step through create_tiered_cache (Llama-3.1-8B shape, random init)",
+        "unit": "ms/step", "higher_is_better": False, "steps": K, "warmup": W, "dtype": "bf16",
+        "data": "synthetic (random weights and prompt)",
+        "config": {"workload": "config 2 shape as a whole model: 32 layers, batch 16, context 8192, "
+                               "4 sink + 64 recent bf16, INT4 middle", "batch": B, "context": S, "layers": L},
+        "fused_ms_per_step": round(res["fused"], 3), "materialise_sdpa_ms_per_step": round(res["materialise"], 3),
+        "fused_tokens_per_s": round(B / (res["fused"] / 1e3), 1),
+        "speedup": round(res["materialise"] / res["fused"], 2),
+        "uncompressed_dynamic_cache_ms_per_step": round(res["dynamic"], 3),
+    }), flush=True)
+
+
 def main():
     args = parse()
     ws, rank, local = dist_env()
@@ -930,6 +1016,8 @@ def main():
     try:
         if args.reassign:
             run_reassign(args)
+        elif args.hf:
+            run_hf(args)
         elif args.impl == "reference":
             run_reference(args, ws, rank)
         else:
