@@ -10,6 +10,7 @@
 //     (fade/rotated_quant.py:35-48).
 //   * A thread owns 8 consecutive channels of one token row when D % 8 == 0
 //     (one 16-byte load for 16-bit types), else 2 channels.
+
 #include "common.cuh"
 
 namespace fade {
@@ -163,6 +164,9 @@ quant_int4_v_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, in
     const int lane_in_row = threadIdx.x % tpr;
     const bool has_elems = lane_in_row * E < D;
     const int64_t step = (int64_t)gridDim.x * rows_per_cta;
+    // rows equally spaced in memory (a contiguous [B, H, S] row space): the
+    // row offset is row * ss, no per-row index decomposition
+    const bool flat = v.sh == v.S * v.ss && v.sb == v.H * v.sh;
     for (int64_t base = (int64_t)blockIdx.x * rows_per_cta + threadIdx.x / tpr; base < rows; base += U * step) {
         float e[U][E];
 #pragma unroll
@@ -171,10 +175,15 @@ quant_int4_v_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, in
 #pragma unroll
             for (int i = 0; i < E; ++i) e[u][i] = 0.f;
             if (row < rows && has_elems) {
-                const int64_t s = row % v.S, bh = row / v.S;
-                const int64_t b = bh / v.H, h = bh % v.H;
-                load_elems<DT, E>(x + b * v.sb + h * v.sh + s * v.ss + (int64_t)lane_in_row * E * v.sd,
-                                  v.sd, vec, e[u]);
+                int64_t off;
+                if (flat) {
+                    off = row * v.ss;
+                } else {
+                    const int64_t s = row % v.S, bh = row / v.S;
+                    const int64_t b = bh / v.H, h = bh % v.H;
+                    off = b * v.sb + h * v.sh + s * v.ss;
+                }
+                load_elems<DT, E>(x + off + (int64_t)lane_in_row * E * v.sd, v.sd, vec, e[u]);
             }
         }
 #pragma unroll
@@ -464,6 +473,109 @@ static bool can_vec(const void* x, const fade_view4& v, int elem_bytes) {
            ((v.sh * elem_bytes) % 16 == 0) && ((v.ss * elem_bytes) % 16 == 0);
 }
 
+// quant_k_int4 for long rows: a cluster of kKClus CTAs per (b, h), each over
+// a contiguous slice of S and all D channels.  Each CTA reduces the absmax
+// of its slice (kKRows rows in flight per thread), the cluster combines the
+// kKClus partial maxima through distributed shared memory, and each CTA then
+// quantises its own slice, which it read moments before (most of a wave's
+// slices are still in the 126 MB L2).
+constexpr int kKClus = 8;
+constexpr int kKRows = 4;
+
+template <int DT>
+__global__ void __cluster_dims__(kKClus, 1, 1) __launch_bounds__(kQuantThreads)
+quant_int4_k_cluster_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, uint8_t* __restrict__ packed,
+                            typename Elem<DT>::T* __restrict__ scale, bool vec) {
+    using T = typename Elem<DT>::T;
+    constexpr int E = 8, U = kKRows;
+    const int z = blockIdx.x / kKClus, rank = blockIdx.x % kKClus;
+    const int b = z / (int)v.H, h = z % (int)v.H;
+    const int D = (int)v.D;
+    const int tpr = D / E;                       // threads per row (D <= 256: tpr <= 32)
+    const int rows_per_iter = kQuantThreads / tpr;
+    const int slot = threadIdx.x / tpr;
+    const int dg = (threadIdx.x % tpr) * E;
+    const int64_t s0 = v.S * rank / kKClus, s1 = v.S * (rank + 1) / kKClus;
+    const T* xb = x + b * v.sb + h * v.sh + (int64_t)dg * v.sd;
+
+    float amax[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) amax[i] = 0.f;
+    int64_t s = s0 + slot;
+    for (; s + (U - 1) * rows_per_iter < s1; s += U * rows_per_iter) {
+        float e[U][E];
+#pragma unroll
+        for (int u = 0; u < U; ++u) load_elems<DT, E>(xb + (s + u * rows_per_iter) * v.ss, v.sd, vec, e[u]);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int i = 0; i < E; ++i) amax[i] = fmaxf(amax[i], fabsf(e[u][i]));
+    }
+    for (; s < s1; s += rows_per_iter) {
+        float e[E];
+        load_elems<DT, E>(xb + s * v.ss, v.sd, vec, e);
+#pragma unroll
+        for (int i = 0; i < E; ++i) amax[i] = fmaxf(amax[i], fabsf(e[i]));
+    }
+    __shared__ float red[kQuantThreads * E];
+    __shared__ float camax[256];                 // this CTA's per-channel maxima
+    __shared__ float s_inv[256];
+#pragma unroll
+    for (int i = 0; i < E; ++i) red[threadIdx.x * E + i] = amax[i];
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += kQuantThreads) {
+        const int t = c / E, i = c % E;
+        float m = 0.f;
+        for (int r = 0; r < rows_per_iter; ++r) m = fmaxf(m, red[(r * tpr + t) * E + i]);
+        camax[c] = m;
+    }
+    // cluster-wide maxima: read every member's camax (distributed shared memory)
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    const uint32_t local = (uint32_t)__cvta_generic_to_shared(camax);
+    for (int c = threadIdx.x; c < D; c += kQuantThreads) {
+        float m = 0.f;
+#pragma unroll
+        for (int r = 0; r < kKClus; ++r) {
+            uint32_t remote;
+            float val;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local + 4u * c), "r"(r));
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(val) : "r"(remote) : "memory");
+            m = fmaxf(m, val);
+        }
+        // absmax.clamp(min=EPS) in the dtype; inv = 7/absmax; scale = absmax/7.
+        m = fmaxf(m, Elem<DT>::eps());
+        s_inv[c] = inv_scale<DT>(m, 7.f);
+        if (rank == 0) scale[(int64_t)z * D + c] = Elem<DT>::from_f(Elem<DT>::rnd(__fdiv_rn(m, 7.f)));
+    }
+    // no member leaves (or reuses camax) while another may still read it
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    float inv[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) inv[i] = s_inv[dg + i];
+    uint8_t* pb = packed + (int64_t)z * v.S * (D / 2) + dg / 2;
+    s = s0 + slot;
+    for (; s + (U - 1) * rows_per_iter < s1; s += U * rows_per_iter) {
+        float e[U][E];
+#pragma unroll
+        for (int u = 0; u < U; ++u) load_elems<DT, E>(xb + (s + u * rows_per_iter) * v.ss, v.sd, vec, e[u]);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            int q[E];
+#pragma unroll
+            for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[u][i], inv[i])), -8.f, 7.f);
+            store_int4<E>(pb + (s + u * rows_per_iter) * (D / 2), q);
+        }
+    }
+    for (; s < s1; s += rows_per_iter) {
+        float e[E];
+        load_elems<DT, E>(xb + s * v.ss, v.sd, vec, e);
+        int q[E];
+#pragma unroll
+        for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[i], inv[i])), -8.f, 7.f);
+        store_int4<E>(pb + s * (D / 2), q);
+    }
+}
+
 template <int DT>
 static int launch_quant_k(const void* x, const fade_view4& v, uint8_t* packed, void* scale,
                           cudaStream_t st) {
@@ -474,6 +586,13 @@ static int launch_quant_k(const void* x, const fade_view4& v, uint8_t* packed, v
         if (Z == 0) return FADE_OK;
     }
     const bool e8 = (v.D % 8 == 0);
+    if (e8 && v.D <= 256 && v.S >= 64 * kKClus) {
+        const bool vec = can_vec(x, v, sizeof(T));
+        quant_int4_k_cluster_kernel<DT><<<(unsigned)(Z * kKClus), kQuantThreads, 0, st>>>(
+            (const T*)x, v, packed, (T*)scale, vec);
+        FADE_LAUNCH_CHECK();
+        return FADE_OK;
+    }
     const int E = e8 ? 8 : 2;
     int dims_per_cta = (int)(v.D < 256 ? v.D : 256);
     // For few (b,h) pairs, split channels across CTAs to fill the machine.

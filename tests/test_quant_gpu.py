@@ -50,7 +50,8 @@ def test_int2_golden(cuda_device, dt, G):
 
 
 @pytest.mark.parametrize("dt", DTS)
-@pytest.mark.parametrize("shape", [(2, 4, 1000, 128), (1, 2, 2048, 64), (3, 1, 7, 96), (1, 1, 1, 6)])
+@pytest.mark.parametrize("shape", [(2, 4, 1000, 128), (1, 2, 2048, 64), (3, 1, 7, 96), (1, 1, 1, 6),
+                                   (1, 3, 1337, 256), (2, 2, 513, 128)])
 def test_int4_vs_oracle_random(cuda_device, dt, shape):
     from fade_b200.quant import quant_k_int4, quant_v_int4
 
@@ -70,19 +71,21 @@ def test_int4_strided_input(cuda_device):
     """Non-contiguous views (e.g. an index_select-free slice of a bigger cache)."""
     from fade_b200.quant import quant_k_int4, quant_v_int4
 
-    x = seeded_outliers((2, 3, 300, 128), seed=5, dt="f16")
+    x = seeded_outliers((2, 3, 2100, 128), seed=5, dt="f16")
     big = np_to_dt_tensor(x, "f16")
-    view = big[:, :, 17:250]          # strided along S (still contiguous rows)
-    tview = big.transpose(1, 2).contiguous().transpose(1, 2)[:, :, 17:250]  # exotic strides
-    for t in (view, tview):
-        kp, ks = quant_k_int4(t)
-        vp, vs = quant_v_int4(t)
-        okp, oks = oq.quant_k_int4(x[:, :, 17:250], "f16")
-        ovp, ovs = oq.quant_v_int4(x[:, :, 17:250], "f16")
-        np.testing.assert_array_equal(kp.cpu().numpy(), okp)
-        np.testing.assert_array_equal(t_bits(ks), to_bits(oks, "f16"))
-        np.testing.assert_array_equal(vp.cpu().numpy(), ovp)
-        np.testing.assert_array_equal(t_bits(vs), to_bits(ovs, "f16"))
+    # short rows (one CTA per (b, h) channel block), longer rows (clusters per (b, h))
+    for lo, hi in ((17, 250), (17, 800), (17, 2090)):
+        view = big[:, :, lo:hi]          # strided along S (still contiguous rows)
+        tview = big.transpose(1, 2).contiguous().transpose(1, 2)[:, :, lo:hi]  # exotic strides
+        okp, oks = oq.quant_k_int4(x[:, :, lo:hi], "f16")
+        ovp, ovs = oq.quant_v_int4(x[:, :, lo:hi], "f16")
+        for t in (view, tview):
+            kp, ks = quant_k_int4(t)
+            vp, vs = quant_v_int4(t)
+            np.testing.assert_array_equal(kp.cpu().numpy(), okp)
+            np.testing.assert_array_equal(t_bits(ks), to_bits(oks, "f16"))
+            np.testing.assert_array_equal(vp.cpu().numpy(), ovp)
+            np.testing.assert_array_equal(t_bits(vs), to_bits(ovs, "f16"))
 
 
 def test_errors_match_reference_messages(cuda_device):
