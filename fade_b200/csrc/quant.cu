@@ -637,12 +637,97 @@ static int launch_quant_v(const void* x, const fade_view4& v, uint8_t* packed, v
     return FADE_OK;
 }
 
+// Grouped INT2 at head_dim 128 for groups of up to 32 rows: one warp per
+// (b, h, group).  Lanes 0-15 hold the even rows, 16-31 the odd rows, 8
+// channels each; the group's rows stay in registers (raw 16-byte loads, all
+// issued before any math), the per-channel absmax is one shuffle across the
+// two halves, and the codes are made from the registers: one HBM read, no
+// shared memory and no block barrier.
+constexpr int kInt2MaxRows = 32;
+
+template <int DT>
+__global__ void __launch_bounds__(256, 2)
+quant_int2_grouped_warp_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, int group,
+                               int64_t n_groups, int8_t* __restrict__ codes_i8, uint8_t* __restrict__ codes_u8,
+                               typename Elem<DT>::T* __restrict__ scale) {
+    using T = typename Elem<DT>::T;
+    constexpr int E = 8, D = 128, RMAX = kInt2MaxRows / 2;
+    const int64_t zg = (int64_t)blockIdx.x * 8 + threadIdx.x / 32;   // (b*H + h) * G + g
+    if (zg >= n_groups) return;
+    const int lane = threadIdx.x % 32, half = lane >> 4, t = lane & 15;
+    const int64_t G = v.S / group;
+    const int64_t g = zg % G, bh = zg / G;
+    const int64_t b = bh / v.H, h = bh % v.H;
+    const T* xb = x + b * v.sb + h * v.sh + (g * group + half) * v.ss + (int64_t)t * E;
+    const int R = group / 2;
+    uint4 raw[RMAX];
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r)
+        if (r < R) raw[r] = __ldg(reinterpret_cast<const uint4*>(xb + (int64_t)(2 * r) * v.ss));
+    float amax[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) amax[i] = 0.f;
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+        if (r < R) {
+            const T* e = reinterpret_cast<const T*>(&raw[r]);
+#pragma unroll
+            for (int i = 0; i < E; ++i) amax[i] = fmaxf(amax[i], fabsf(Elem<DT>::to_f(e[i])));
+        }
+    }
+    float inv[E];
+    uint4 sw;
+    T* so = reinterpret_cast<T*>(&sw);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        float m = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], 16));
+        m = fmaxf(m, Elem<DT>::eps());
+        inv[i] = inv_scale<DT>(m, 1.f);                   // 1 / absmax
+        so[i] = Elem<DT>::from_f(Elem<DT>::rnd(__fdiv_rn(m, 1.f)));
+    }
+    if (half == 0) *reinterpret_cast<uint4*>(scale + zg * D + t * E) = sw;
+    const int64_t row0 = bh * v.S + g * group + half;
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+        if (r < R) {
+            const T* e = reinterpret_cast<const T*>(&raw[r]);
+            int q[E];
+#pragma unroll
+            for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(Elem<DT>::to_f(e[i]), inv[i])), -2.f, 1.f);
+            const int64_t row = row0 + 2 * r;
+            if (codes_i8) {
+                uint2 w;
+                w.x = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) |
+                      ((uint32_t)(q[3] & 0xFF) << 24);
+                w.y = (uint32_t)(q[4] & 0xFF) | ((uint32_t)(q[5] & 0xFF) << 8) | ((uint32_t)(q[6] & 0xFF) << 16) |
+                      ((uint32_t)(q[7] & 0xFF) << 24);
+                *reinterpret_cast<uint2*>(codes_i8 + row * D + t * E) = w;
+            }
+            if (codes_u8) {
+                const uint32_t w = pack_crumbs(q[0], q[1], q[2], q[3]) | (pack_crumbs(q[4], q[5], q[6], q[7]) << 8);
+                *reinterpret_cast<uint16_t*>(codes_u8 + row * (D / 4) + t * 2) = (uint16_t)w;
+            }
+        }
+    }
+}
+
 template <int DT>
 static int launch_int2(const void* x, const fade_view4& v, int group, int8_t* ci8, uint8_t* cu8,
                        void* scale, cudaStream_t st) {
     using T = typename Elem<DT>::T;
     const int64_t n = v.B * v.H * (v.S / group);
     if (n == 0) return FADE_OK;
+    if constexpr (DT != FADE_F32) {
+        // warp per group: D = 128, even group <= 32, 16-byte rows, 8-byte code rows
+        if (v.D == 128 && group % 2 == 0 && group <= kInt2MaxRows && can_vec(x, v, sizeof(T)) &&
+            (v.ss * (int64_t)sizeof(T)) % 16 == 0 && ((uintptr_t)ci8 % 8) == 0 && ((uintptr_t)cu8 % 2) == 0 &&
+            ((uintptr_t)scale % 16) == 0) {
+            quant_int2_grouped_warp_kernel<DT><<<(unsigned)((n + 7) / 8), 256, 0, st>>>(
+                (const T*)x, v, group, n, ci8, cu8, (T*)scale);
+            FADE_LAUNCH_CHECK();
+            return FADE_OK;
+        }
+    }
     if (v.D % 8 != 0 || v.D / 8 > kQuantThreads || v.D > 512) {
         if (cu8) return FADE_ERR_UNSUPPORTED;
         if (v.D / 2 > kQuantThreads) return FADE_ERR_UNSUPPORTED;
