@@ -9,7 +9,8 @@
 //
 // Launch sequence (one stream, chained with programmatic dependent launch):
 //   k0  rotate_queries   (only with a rotated tier): q_rot = q @ R^T in fp32,
-//                        16 query rows per CTA, R staged in shared memory.
+//                        16 query rows per CTA, R^T staged in shared memory,
+//                        a 2 x 4 register tile per thread.
 //   k1  middle_kernel    one persistent CTA per SM, 16 warps:
 //       * 3 consumer groups x 4 warps.  The CTA owns a contiguous range of
 //         128-token units of the quantised middle (stream-K over all (b, kv-
@@ -37,6 +38,9 @@
 //         token into the ring.
 //       * every mbarrier wait is bounded; a stalled pipeline sets the
 //         workspace error word (fade_workspace_check) instead of hanging.
+//   k1' middle_tc_kernel (middle_tc.cuh; opt-in with fade_set_middle_kernel,
+//                        INT4 K/V at D = 128): the same schedule and partials
+//                        with tcgen05 MMAs and tensor-memory accumulators.
 //   k2  finish_kernel    one CTA per (b, kv-head), after the middle grid: merge
 //                        of the FP partial with the row's middle partials (the
 //                        rotation R applied back for rotated tiers), normalise,
