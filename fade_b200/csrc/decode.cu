@@ -321,8 +321,23 @@ template <int DT> struct Conv {
     // the same fields as int2() but as the exact value F * (code + 2) + 128,
     // F = 1, 4, 16, 1 for fields 3, 2, 1, 0 (the channel's kF2 factor), so a
     // word of 16 codes takes 3 shifts + 8 lop3 instead of 8 + 8.
+    // fp16 (ten mantissa bits): all four fields of a byte lie inside the
+    // mantissa of fp16(1024 + m), so only the odd bytes are shifted: 16 codes
+    // take 1 shift + 8 lop3; h[i] = F * (code + 2) + 1024 with F = 1, 4, 16,
+    // 64 for fields 3, 2, 1, 0 (kF2h).
     __device__ __forceinline__ static void int2_biased(uint32_t x, uint32_t (&h)[8]) {
-        static_assert(DT == FADE_BF16, "scaled biased 2-bit conversion is bf16 only");
+        if constexpr (DT == FADE_F16) {
+            const uint32_t y = x >> 8;
+            h[0] = lop3_and_xor(x, 0x00030003u, 0x64026402u);
+            h[1] = lop3_and_xor(x, 0x000C000Cu, 0x64086408u);
+            h[2] = lop3_and_xor(x, 0x00300030u, 0x64206420u);
+            h[3] = lop3_and_xor(x, 0x00C000C0u, 0x64806480u);
+            h[4] = lop3_and_xor(y, 0x00030003u, 0x64026402u);
+            h[5] = lop3_and_xor(y, 0x000C000Cu, 0x64086408u);
+            h[6] = lop3_and_xor(y, 0x00300030u, 0x64206420u);
+            h[7] = lop3_and_xor(y, 0x00C000C0u, 0x64806480u);
+            return;
+        }
         const uint32_t y = x >> 8;
         h[0] = lop3_and_xor(x, 0x00030003u, 0x43024302u);
         h[1] = lop3_and_xor(x, 0x000C000Cu, 0x43084308u);
@@ -340,6 +355,11 @@ template <int DT> struct Conv {
 __host__ __device__ constexpr float kF2(int d) { return (d & 3) == 1 ? 16.f : (d & 3) == 2 ? 4.f : 1.f; }
 __host__ __device__ constexpr float kInvF2(int d) { return (d & 3) == 1 ? 0.0625f : (d & 3) == 2 ? 0.25f : 1.f; }
 __host__ __device__ constexpr float kH2(int d) { return 128.f + 2.f * kF2(d); }
+// The fp16 form (Conv<FADE_F16>::int2_biased): field 0 (d % 4 == 0) is read in
+// place as F = 64; kH2h = 1024 + 2 * kF2h.
+__host__ __device__ constexpr float kF2h(int d) { return (d & 3) == 0 ? 64.f : kF2(d); }
+__host__ __device__ constexpr float kInvF2h(int d) { return (d & 3) == 0 ? 0.015625f : kInvF2(d); }
+__host__ __device__ constexpr float kH2h(int d) { return 1024.f + 2.f * kF2h(d); }
 
 // ---------------------------------------------------------------------------
 // Channel maps.  For the K operand, k-step ks and slot s in {0,1,2,3} (= the
@@ -937,7 +957,6 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     using P = Pk<DT>;
     constexpr int KSTEPS = D / 16;   // k-steps of the QK product
     constexpr int MT = D / 16;       // m-tiles of the PV product (rows = channels)
-    constexpr int NQ = QSPLIT ? 2 : 1;
     // 2-bit codes c in {-2,-1,0,1}: c * scale is exactly representable, so the
     // reference's rnd(c * scale) equals c * scale and the scales can be folded
     // exactly: K's per-channel scale into the fp32 query (before its hi + lo
@@ -950,6 +969,18 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     // V: at each flush O_d = (O_d - H_d sum_t p'_t) / F_d, the sum taken over
     // the same rounded P' the MMA consumes.
     constexpr bool FOLD2B = FOLD2 && DT == FADE_BF16;
+    // bf16 with folded 2-bit scales: the QK product runs in fp16 with one
+    // query part.  The fp32 query q'_d = q_rot,d * s_d / F_d is rounded once
+    // to fp16 (11 significant bits, more than the hi + lo split in bf16 would
+    // need MMAs for), after scaling each query row by a power of two 2^-e_r
+    // that brings its largest |q'| into [2^13, 2^14) (no fp16 overflow,
+    // normal values); the softmax applies 2^e_r with the score scale.  The
+    // K codes enter as fp16(1024 + F_d * (code + 2)) (1 shift per 16 codes).
+    // The PV product stays in bf16.
+    constexpr bool QK16 = FOLD2B;
+    constexpr int QDT = QK16 ? FADE_F16 : DT;
+    using PQ = Pk<QDT>;
+    constexpr int NQ = (QSPLIT && !QK16) ? 2 : 1;
     // QK accumulators split in two (shorter dependent MMA chains) where the
     // registers allow it without spilling
     constexpr bool kSplitAcc = KB == 2 || (!QSPLIT && !VGROUP);
@@ -1107,6 +1138,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
     uint32_t ksc[KSTEPS][2];         // K scale pairs matching the A pairs
     float m_run[NT][2], l_run[NT][2];
     float kb[NT][2];                 // FOLD2B: 130 * sum of the row's query channels
+    float qsr[NT][2];                // QK16: score scale of the C-fragment columns (qk_scale * 2^e_r)
     float lp[NT][2];                 // FOLD2B: running sum of the rounded P' of the row
     float o[NT][MT][4];
     int cur_z = -1, z_first = 0;
@@ -1157,23 +1189,55 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
             const bool rv = r < p.rows;
             const int j = rv ? r / p.n_q : 0, sq = rv ? r % p.n_q : 0;
             const int64_t qoff = (int64_t)b * p.q_sb + (int64_t)(h * p.g + j) * p.q_sh + (int64_t)sq * p.q_ss;
+            // fp32 query chunk cb of this lane's row (rotated tiers), with the
+            // K scales folded in (FOLD2)
+            auto load_qrow = [&](int cb, float (&e)[CH]) {
+                const float* ptr = reinterpret_cast<const float*>(p.q) + qoff + cb * CHW + CH * t;
+#pragma unroll
+                for (int c4 = 0; c4 < CH / 4; ++c4) {
+                    const float4 v4 = rv ? __ldg(reinterpret_cast<const float4*>(ptr) + c4)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                    e[4 * c4] = v4.x; e[4 * c4 + 1] = v4.y; e[4 * c4 + 2] = v4.z; e[4 * c4 + 3] = v4.w;
+                }
+                if constexpr (FOLD2) {
+                    uint16_t kse[CH];
+                    load_block_bits(p.k_scale, ks_off + cb * CHW + CH * t, kse);
+#pragma unroll
+                    for (int jj = 0; jj < CH; ++jj) e[jj] *= P::unpack_lo((uint32_t)kse[jj]);
+                }
+            };
+            // QK16: the row's power-of-two normalisation 2^-sh (lanes 4 gid ..
+            // 4 gid + 3 hold the row's channels)
+            float rsc = 1.f;
+            if constexpr (QK16) {
+                float amax = 0.f;
+#pragma unroll
+                for (int cb = 0; cb < KSTEPS * 16 / CHW; ++cb) {
+                    float e[CH];
+                    load_qrow(cb, e);
+#pragma unroll
+                    for (int jj = 0; jj < CH; ++jj) {
+                        const int d = cb * CHW + CH * t + jj;
+                        amax = fmaxf(amax, fabsf(e[jj] * kInvF2h(d)));
+                    }
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                int ex = 0;
+                if (amax > 0.f && amax < INFINITY) frexpf(amax, &ex);
+                const int sh = (amax > 0.f && amax < INFINITY) ? ex - 14 : 0;
+                rsc = ldexpf(1.f, -sh);
+                const float rq = ldexpf(p.qk_scale, sh);
+                qsr[nt][0] = __shfl_sync(0xffffffffu, rq, (2 * t) * 4);
+                qsr[nt][1] = __shfl_sync(0xffffffffu, rq, (2 * t + 1) * 4);
+            } else {
+                qsr[nt][0] = qsr[nt][1] = p.qk_scale;
+            }
 #pragma unroll
             for (int cb = 0; cb < KSTEPS * 16 / CHW; ++cb) {
                 if constexpr (QSPLIT) {
                     float e[CH];
-                    const float* ptr = reinterpret_cast<const float*>(p.q) + qoff + cb * CHW + CH * t;
-#pragma unroll
-                    for (int c4 = 0; c4 < CH / 4; ++c4) {
-                        const float4 v4 = rv ? __ldg(reinterpret_cast<const float4*>(ptr) + c4)
-                                             : make_float4(0.f, 0.f, 0.f, 0.f);
-                        e[4 * c4] = v4.x; e[4 * c4 + 1] = v4.y; e[4 * c4 + 2] = v4.z; e[4 * c4 + 3] = v4.w;
-                    }
-                    if constexpr (FOLD2) {
-                        uint16_t kse[CH];
-                        load_block_bits(p.k_scale, ks_off + cb * CHW + CH * t, kse);
-#pragma unroll
-                        for (int jj = 0; jj < CH; ++jj) e[jj] *= P::unpack_lo((uint32_t)kse[jj]);
-                    }
+                    load_qrow(cb, e);
 #pragma unroll
                     for (int u = 0; u < CHW / 16; ++u) {
                         const int ks = cb * (CHW / 16) + u;
@@ -1182,14 +1246,19 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             const int d0 = KMap::kdim(ks, 2 * hs, t), d1 = KMap::kdim(ks, 2 * hs + 1, t);
                             float v0 = e[d0 - cb * CHW - CH * t];
                             float v1 = e[d1 - cb * CHW - CH * t];
-                            if constexpr (FOLD2B) {   // powers of 2: exact
+                            if constexpr (QK16) {   // powers of 2: exact
+                                v0 *= kInvF2h(d0) * rsc;
+                                v1 *= kInvF2h(d1) * rsc;
+                            } else if constexpr (FOLD2B) {
                                 v0 *= kInvF2(d0);
                                 v1 *= kInvF2(d1);
                             }
-                            const uint32_t hp = P::pack(v0, v1);
-                            const float h0 = P::unpack_lo(hp), h1 = P::unpack_lo(hp >> 16);
+                            const uint32_t hp = PQ::pack(v0, v1);
                             qf[0][nt][ks][hs] = hp;
-                            qf[NQ - 1][nt][ks][hs] = P::pack(v0 - h0, v1 - h1);
+                            if constexpr (NQ == 2) {
+                                const float h0 = PQ::unpack_lo(hp), h1 = PQ::unpack_lo(hp >> 16);
+                                qf[1][nt][ks][hs] = PQ::pack(v0 - h0, v1 - h1);
+                            }
                         }
                     }
                 } else {
@@ -1230,8 +1299,12 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     for (int ks = 0; ks < KSTEPS; ++ks)
 #pragma unroll
                         for (int hs = 0; hs < 2; ++hs)
-                            sum += kH2(KMap::kdim(ks, 2 * hs, t)) * P::unpack_lo(qf[qs][nt][ks][hs]) +
-                                   kH2(KMap::kdim(ks, 2 * hs + 1, t)) * P::unpack_lo(qf[qs][nt][ks][hs] >> 16);
+                            if constexpr (QK16)
+                                sum += kH2h(KMap::kdim(ks, 2 * hs, t)) * PQ::unpack_lo(qf[qs][nt][ks][hs]) +
+                                       kH2h(KMap::kdim(ks, 2 * hs + 1, t)) * PQ::unpack_lo(qf[qs][nt][ks][hs] >> 16);
+                            else
+                                sum += kH2(KMap::kdim(ks, 2 * hs, t)) * P::unpack_lo(qf[qs][nt][ks][hs]) +
+                                       kH2(KMap::kdim(ks, 2 * hs + 1, t)) * P::unpack_lo(qf[qs][nt][ks][hs] >> 16);
                 sum += __shfl_xor_sync(0xffffffffu, sum, 1);
                 sum += __shfl_xor_sync(0xffffffffu, sum, 2);
                 // C-fragment columns 2t, 2t+1 are query rows held by lanes 8t, 8t+4
@@ -1426,14 +1499,14 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
                                 for (int nt = 0; nt < NT; ++nt)
-                                    P::mma(acc(ks, qs, nt), a0, a1, a2, a3,
-                                           qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
+                                    PQ::mma(acc(ks, qs, nt), a0, a1, a2, a3,
+                                            qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     } else {
                         uint32_t h0[8], h1[8];
                         if constexpr (FOLD2B) {
-                            Conv<DT>::int2_biased(kr[0][cb], h0);
-                            Conv<DT>::int2_biased(kr[1][cb], h1);
+                            Conv<QDT>::int2_biased(kr[0][cb], h0);
+                            Conv<QDT>::int2_biased(kr[1][cb], h1);
                         } else {
                             Conv<DT>::int2(kr[0][cb], h0);
                             Conv<DT>::int2(kr[1][cb], h1);
@@ -1449,8 +1522,8 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                             for (int qs = 0; qs < NQ; ++qs)
 #pragma unroll
                                 for (int nt = 0; nt < NT; ++nt)
-                                    P::mma(acc(ks, qs, nt), a0, a1, a2, a3,
-                                           qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
+                                    PQ::mma(acc(ks, qs, nt), a0, a1, a2, a3,
+                                            qf[qs][nt][ks][0], qf[qs][nt][ks][1]);
                         }
                     }
                 }
@@ -1491,7 +1564,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     for (int e = 0; e < 2; ++e) {
                         const float lm = fmaxf(fmaxf(sacc[0][nt][e], sacc[0][nt][e + 2]),
                                                fmaxf(sacc[1][nt][e], sacc[1][nt][e + 2]));
-                        need |= lm * qks > m_run[nt][e] + 8.f;
+                        need |= lm * (QK16 ? qsr[nt][e] : qks) > m_run[nt][e] + 8.f;
                     }
                 full = __any_sync(0xffffffffu, need);
             }
@@ -1507,7 +1580,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    const float mnew = fmaxf(m_run[nt][e], mx * qks);
+                    const float mnew = fmaxf(m_run[nt][e], mx * (QK16 ? qsr[nt][e] : qks));
                     grow |= mnew > m_run[nt][e];
                     corr[nt][e] = ex2(m_run[nt][e] - mnew);
                     m_run[nt][e] = mnew;
@@ -1550,7 +1623,7 @@ middle_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant_
                     float pv[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float pe = ex2(fmaf(sacc[mt][nt][e], qks, -m_run[nt][e & 1]));
+                        const float pe = ex2(fmaf(sacc[mt][nt][e], QK16 ? qsr[nt][e & 1] : qks, -m_run[nt][e & 1]));
                         l_run[nt][e & 1] += pe;
                         pv[e] = FOLD2 ? pe * tsc[mt][e >> 1] : pe;
                     }
