@@ -69,13 +69,17 @@ CONFIGS = {
 }
 L2_BYTES = 126 * 1024 * 1024
 CFG: dict = {}
+# default timed steps per configuration (about 1 s of device time on one B200;
+# configurations 1 and 3 flush L2 between steps, outside the timed events)
+DEFAULT_STEPS = {1: 2000, 2: 700, 3: 1000, 4: 250, 5: 90}
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: about 1 s of timed work for the configuration)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("fade", "reference"), default="fade")
     ap.add_argument("--shard", choices=("heads", "batch"), default=None,
@@ -100,6 +104,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="layers per step (profiling captures use 1)")
     ap.add_argument("--batch", type=int, default=None, help="batch per GPU-equivalent (default: the config's)")
     args = ap.parse_args()
+    if args.steps is None:   # roughly one second of timed steps, so clock samples cover the load
+        args.steps = 10 if args.impl == "reference" else (
+            DEFAULT_STEPS[args.config] if not (args.reassign or args.hf) else 50)
     CFG.update(CONFIGS[args.config])
     CFG["id"] = args.config
     if args.layers:
