@@ -296,13 +296,31 @@ class TieredDecoder:
 
     def capture_host(self, q_host: Tensor, k_host: Tensor, v_host: Tensor, out_host: Tensor) -> torch.cuda.CUDAGraph:
         """Record step_host for these (pinned) host buffers as one CUDA graph in
-        which the copies overlap the layers: a side stream copies every layer's
-        inputs in layer order and layer l waits only for its own; layer l's
-        output is copied back while the later layers run.  Later step_host
-        calls with the same buffers replay it.  Call after a warm-up step."""
+        which the copies overlap the layers.  A side stream copies the inputs
+        in layer chunks of growing size (1, 3, 12, 48, ... layers: the first
+        layer starts after one layer's copies, and each later chunk lands long
+        before its first layer runs, since a layer's copies take a fraction of
+        its attention time); the layers wait only at chunk boundaries, so the
+        kernels of consecutive layers keep their programmatic dependent
+        launches everywhere else.  Outputs go back in the mirrored chunks (the
+        last layer's alone).  Later step_host calls with the same buffers
+        replay it.  Call after a warm-up step."""
         for i in range(self.L):
             self._plan(i)
         dev = self.device
+        L = self.L
+        sizes, n = [], 1
+        while sum(sizes) < L:
+            sizes.append(min(n, L - sum(sizes)))
+            n = 3 if n == 1 else 4 * n
+        in_chunks, a = [], 0
+        for z in sizes:
+            in_chunks.append((a, a + z))
+            a += z
+        out_chunks, a = [], 0
+        for z in reversed(sizes):
+            out_chunks.append((a, a + z))
+            a += z
         torch.cuda.synchronize(dev)
         g = torch.cuda.CUDAGraph()
         s, cin, cout = (torch.cuda.Stream(dev) for _ in range(3))
@@ -313,25 +331,30 @@ class TieredDecoder:
                 start.record(s)
                 cin.wait_event(start)
                 cout.wait_event(start)
-                ev_in = []
+                ev_in = {}
                 with torch.cuda.stream(cin):
-                    for i in range(self.L):
-                        self.q[i].copy_(q_host[i], non_blocking=True)
-                        self.k_new[i].copy_(k_host[i], non_blocking=True)
-                        self.v_new[i].copy_(v_host[i], non_blocking=True)
+                    for i0, i1 in in_chunks:
+                        self.q[i0:i1].copy_(q_host[i0:i1], non_blocking=True)
+                        self.k_new[i0:i1].copy_(k_host[i0:i1], non_blocking=True)
+                        self.v_new[i0:i1].copy_(v_host[i0:i1], non_blocking=True)
                         e = torch.cuda.Event()
                         e.record(cin)
-                        ev_in.append(e)
+                        ev_in[i0] = e
+                out_last = {i1 - 1: i0 for i0, i1 in out_chunks}
 
                 def before(i):
-                    s.wait_event(ev_in[i])
+                    if i in ev_in:
+                        s.wait_event(ev_in[i])
 
                 def after(i):
+                    if i not in out_last:
+                        return
+                    i0 = out_last[i]
                     e = torch.cuda.Event()
                     e.record(s)
                     cout.wait_event(e)
                     with torch.cuda.stream(cout):
-                        out_host[i].copy_(self.out[i], non_blocking=True)
+                        out_host[i0:i + 1].copy_(self.out[i0:i + 1], non_blocking=True)
 
                 self._launch_all(before=before, after=after)
                 s.wait_stream(cin)
