@@ -139,6 +139,7 @@ _SIGNATURES = {
         [_vp, ctypes.c_int, View4, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp,
          ctypes.c_size_t, _vp],
     ),
+    "fade_rotated_quant_check": (ctypes.c_int, [_vp]),
     "fade_rotated_dequant": (
         ctypes.c_int,
         [_vp, ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int, _c_i64, _c_i64, _c_i64,

@@ -6,6 +6,7 @@
 // own order, so codes match it except where a rotated value sits within an
 // fp32 ulp of a rounding boundary.
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace fade {
 
@@ -154,6 +155,255 @@ rotated_quant_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, c
     }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core rotation (bf16 inputs, D = 128, 2- and 4-bit codes).
+//
+// R (fp32) is split into three bf16 parts, R = R0 + R1 + R2 exactly (each part
+// the bf16 rounding of what the previous parts leave), so every product
+// x_e * Rj[d][e] of a bf16 input is exact in fp32 and x_rot = sum_j x Rj^T is
+// the exact dot product up to the fp32 accumulation inside the tensor core
+// (as close to the exact value as the fixed sequential order of the CUDA-core
+// kernel above, but in another order: the two can differ in the last fp32
+// bit, and a code only where a rotated value sits that close to a rounding
+// boundary, as against the reference's own matmul).
+//
+// One CTA per SM, persistent over 128-token tiles of the [B, H, S] row space.
+// Shared memory holds the three R parts and two token tiles (cp.async double
+// buffering: tile i + 1 loads while tile i is multiplied and quantised), all
+// in the canonical K-major layout without swizzle (8-row x 16-byte core
+// matrices, 128 bytes apart along K, 2048 bytes apart along the rows).  One
+// elected thread issues 3 x 8 tcgen05.mma (M = N = 128, K = 16) into a
+// 128-column fp32 accumulator in tensor memory; thread r of the warpgroup then
+// reads token r's 128 rotated values (tcgen05.ld, 16 columns at a time) and
+// quantises them in fp32 exactly like the CUDA-core kernel.
+// ---------------------------------------------------------------------------
+constexpr int kRqThreads = 128;
+constexpr int kRqParts = 3;
+constexpr uint32_t kRqOp = 128 * 128 * 2;   // one [128 x 128] bf16 operand
+constexpr uint32_t kRqR = 0;                                   // R parts
+constexpr uint32_t kRqX = kRqR + kRqParts * kRqOp;             // two token tiles
+constexpr uint32_t kRqBar = kRqX + 2 * kRqOp;                  // MMA-done mbarrier
+constexpr uint32_t kRqSlot = kRqBar + 16;                      // tensor-memory address
+constexpr uint32_t kRqInv = kRqSlot + 16;                      // [128] per-channel 1/scale
+constexpr uint32_t kRqRed = kRqInv + 128 * 4;                  // [4][128] per-warp column maxima
+constexpr uint32_t kRqSmem = kRqRed + 4 * 128 * 4 + 1024;      // + alignment
+constexpr uint32_t kRqPolls = 1u << 24;
+
+// Set by a rotation kernel whose wait for its MMAs gave up (never expected;
+// the outputs of that call are then undefined).  Read with
+// fade_rotated_quant_check().
+__device__ int g_rotq_error;
+
+__device__ __forceinline__ uint32_t rq_off(int row, int k) {
+    return (uint32_t)((row >> 3) * 2048 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
+}
+
+// kind::f16 instruction descriptor: f32 accumulator, bf16 A and B, both
+// K-major, N = 128, M = 128
+constexpr uint32_t kRqIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void rq_cp16(uint32_t dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+__global__ void __launch_bounds__(kRqThreads, 1)
+rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const float* __restrict__ R, int bits,
+                        int kind, int pass, float* __restrict__ amax, uint8_t* __restrict__ packed,
+                        __nv_bfloat16* __restrict__ scale) {
+    extern __shared__ uint8_t rq_raw[];
+    uint8_t* sm = rq_raw + ((1024u - (smem_u32(rq_raw) & 1023u)) & 1023u);
+    const uint32_t sb = smem_u32(sm);
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    constexpr int D = 128;
+    const int64_t S = v.S, Z = v.B * v.H;
+    const int64_t tiles_z = (S + 127) / 128, total = Z * tiles_z;
+    float* inv_s = reinterpret_cast<float*>(sm + kRqInv);
+    float* red = reinterpret_cast<float*>(sm + kRqRed);
+
+    // R parts: Rj[d][e] at part j, K-major over e
+    for (int i = tid * 4; i < D * D; i += kRqThreads * 4) {
+        const float4 r4 = __ldg(reinterpret_cast<const float4*>(R + i));
+        const int d = i / D, e = i % D;
+        const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            float rem = rr[c];
+#pragma unroll
+            for (int j = 0; j < kRqParts; ++j) {
+                const __nv_bfloat16 pj = __float2bfloat16_rn(rem);
+                rem -= __bfloat162float(pj);   // exact: pj holds rem's leading bits
+                *reinterpret_cast<__nv_bfloat16*>(sm + kRqR + j * kRqOp + rq_off(d, e + c)) = pj;
+            }
+        }
+    }
+    if (tid == 0) {
+        mbar_init(sb + kRqBar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        tc_alloc(sb + kRqSlot, 128);
+        tc_relinquish();
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + kRqSlot);
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+
+    float lo, hi;
+    qrange(bits, lo, hi);
+    // stage tile t into buffer `buf` (rows past S are zero-filled)
+    auto load_tile = [&](int64_t t, int buf) {
+        const int64_t z = t / tiles_z, t0 = (t % tiles_z) * 128;
+        const int64_t b = z / v.H, h = z % v.H;
+        const __nv_bfloat16* xz = x + b * v.sb + h * v.sh;
+        const uint32_t dst0 = sb + kRqX + (uint32_t)buf * kRqOp;
+        for (int c = tid; c < 128 * 16; c += kRqThreads) {
+            const int row = c / 16, kc = c % 16;
+            const bool ok = t0 + row < S;
+            const __nv_bfloat16* src = xz + (ok ? t0 + row : 0) * v.ss + kc * 8;
+            rq_cp16(dst0 + rq_off(row, kc * 8), src, ok ? 16u : 0u);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    bool failed = false;
+    int it = 0;
+    if ((int64_t)blockIdx.x < total) load_tile(blockIdx.x, 0);
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (t + gridDim.x < total) load_tile(t + gridDim.x, buf ^ 1);
+        const int64_t z = t / tiles_z, t0 = (t % tiles_z) * 128;
+        if (warp == 0) {
+            tc_fence_after();
+            if (elect_one()) {
+                const uint32_t xb = sb + kRqX + (uint32_t)buf * kRqOp;
+#pragma unroll
+                for (int j = 0; j < kRqParts; ++j)
+#pragma unroll
+                    for (int ks = 0; ks < D / 16; ++ks)
+                        tc_mma_ss(tmem, tc_desc(xb + ks * 256, 128, 2048, 0),
+                                  tc_desc(sb + kRqR + j * kRqOp + ks * 256, 128, 2048, 0), kRqIdesc,
+                                  (j | ks) ? 1u : 0u);
+                tc_commit(sb + kRqBar);
+            }
+            __syncwarp();
+        }
+        // per-channel inverse scales of this row (K, quantisation pass)
+        if (kind == 0 && pass == 1) {
+            const float m = fmaxf(amax[z * D + tid], 1e-8f);
+            inv_s[tid] = inv_scale<FADE_F32>(m, hi);
+            if (t0 == 0) scale[z * D + tid] = __float2bfloat16_rn(__fdiv_rn(m, hi));
+        }
+        uint32_t polls = 0;
+        bool timed_out = false;
+        while (!mbar_try_wait(sb + kRqBar, (uint32_t)it & 1u)) {
+            if (++polls == kRqPolls) { timed_out = true; break; }
+        }
+        // one decision for the whole CTA (also: inv_s written)
+        if (__syncthreads_or(timed_out)) {
+            if (tid == 0) atomicExch(&g_rotq_error, 1);
+            failed = true;
+            break;
+        }
+        tc_fence_after();
+        const int r = tid;   // token row of this thread
+        const bool valid = t0 + r < S;
+        if (kind == 0 && pass == 0) {
+            // per-channel maxima over the tile's tokens
+#pragma unroll 1
+            for (int c = 0; c < D / 16; ++c) {
+                uint32_t vv[16];
+                tc_ld16(tmem + lane_base + 16 * c, vv);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    float m = valid ? fabsf(__uint_as_float(vv[j])) : 0.f;
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+                    if (lane == j) red[warp * D + 16 * c + j] = m;
+                }
+            }
+            __syncthreads();
+            const float m = fmaxf(fmaxf(red[tid], red[D + tid]), fmaxf(red[2 * D + tid], red[3 * D + tid]));
+            atomicMax(reinterpret_cast<int*>(amax) + z * D + tid, __float_as_int(m));
+        } else {
+            float inv_t = 0.f;
+            if (kind == 1) {
+                float m = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < D / 16; ++c) {
+                    uint32_t vv[16];
+                    tc_ld16(tmem + lane_base + 16 * c, vv);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) m = fmaxf(m, fabsf(__uint_as_float(vv[j])));
+                }
+                m = fmaxf(m, 1e-8f);
+                inv_t = inv_scale<FADE_F32>(m, hi);
+                if (valid) scale[z * S + t0 + r] = __float2bfloat16_rn(__fdiv_rn(m, hi));
+            }
+            uint32_t words[16];   // the row's packed codes: 64 bytes (4-bit) or 32 (2-bit)
+#pragma unroll
+            for (int c = 0; c < D / 16; ++c) {
+                uint32_t vv[16];
+                tc_ld16(tmem + lane_base + 16 * c, vv);
+                int q[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float inv = kind == 1 ? inv_t : inv_s[16 * c + j];
+                    q[j] = quant_code(__fmul_rn(__uint_as_float(vv[j]), inv), lo, hi);
+                }
+                if (bits == 4) {
+#pragma unroll
+                    for (int w = 0; w < 2; ++w) {
+                        uint32_t word = 0;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)   // byte k: channels 2k (high nibble), 2k + 1
+                            word |= (((uint32_t)(q[8 * w + 2 * k] & 15) << 4) | (uint32_t)(q[8 * w + 2 * k + 1] & 15))
+                                    << (8 * k);
+                        words[2 * c + w] = word;
+                    }
+                } else {
+                    uint32_t word = 0;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {      // byte k: channels 4k .. 4k + 3 at bits 6, 4, 2, 0
+                        uint32_t byte = 0;
+#pragma unroll
+                        for (int f = 0; f < 4; ++f) byte |= (uint32_t)(q[4 * k + f] & 3) << (6 - 2 * f);
+                        word |= byte << (8 * k);
+                    }
+                    words[c] = word;
+                }
+            }
+            if (valid) {
+                const int nw = bits == 4 ? 16 : 8;
+                uint4* dst = reinterpret_cast<uint4*>(packed + (z * S + t0 + r) * (int64_t)(nw * 4));
+#pragma unroll
+                for (int w4 = 0; w4 < 4; ++w4)
+                    if (4 * w4 < nw) dst[w4] = make_uint4(words[4 * w4], words[4 * w4 + 1], words[4 * w4 + 2],
+                                                          words[4 * w4 + 3]);
+            }
+        }
+        tc_fence_before();
+        __syncthreads();   // tensor memory read (and red / inv_s) before the next tile's MMAs
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (failed && warp == 0) {
+        // MMAs may still be in flight: wait (bounded) for the last commit
+        // before the tensor memory is released
+        for (uint32_t i = 0; i < kRqPolls && !mbar_try_wait(sb + kRqBar, (uint32_t)it & 1u); ++i) {
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tc_dealloc(tmem, 128);
+    }
+}
+
 __device__ __forceinline__ int unpack_code(const uint8_t* __restrict__ p, int bits, int64_t row, int D, int d) {
     if (bits == 4) {
         const uint32_t byte = p[row * (D / 2) + d / 2];
@@ -271,6 +521,28 @@ extern "C" int fade_rotated_quant(const void* x, int dtype, fade_view4 xv, const
     const size_t need = (size_t)Z * xv.D * 4;
     if (kind == 0 && (!workspace || ws_bytes < need)) return FADE_ERR_WORKSPACE;
     cudaStream_t st = as_stream(stream);
+    // bf16 at D = 128 with 2- or 4-bit codes and 16-byte rows: tensor cores
+    if (dtype == FADE_BF16 && xv.D == 128 && bits != 3 && xv.sd == 1 && aligned16(x) && aligned16(packed) &&
+        (xv.sb * 2) % 16 == 0 && (xv.sh * 2) % 16 == 0 && (xv.ss * 2) % 16 == 0) {
+        int dev = 0, n_sm = 0;
+        FADE_CUDA_TRY(cudaGetDevice(&dev));
+        FADE_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+        FADE_CUDA_TRY(cudaFuncSetAttribute(rotated_quant_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kRqSmem));
+        const int64_t tiles = Z * ((xv.S + 127) / 128);
+        const unsigned g = (unsigned)(tiles < n_sm ? tiles : n_sm);
+        float* am = reinterpret_cast<float*>(workspace);
+        const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+        auto* sc = reinterpret_cast<__nv_bfloat16*>(scale);
+        if (kind == 0) {
+            FADE_CUDA_TRY(cudaMemsetAsync(am, 0, need, st));
+            rotated_quant_tc_kernel<<<g, kRqThreads, kRqSmem, st>>>(xb, xv, R, bits, 0, 0, am, packed, sc);
+            FADE_LAUNCH_CHECK();
+        }
+        rotated_quant_tc_kernel<<<g, kRqThreads, kRqSmem, st>>>(xb, xv, R, bits, kind, 1, am, packed, sc);
+        FADE_LAUNCH_CHECK();
+        return FADE_OK;
+    }
     const int D = (int)xv.D;
     // R (transposed) + one token tile, rotated in place + per-token scales
     const size_t smem = ((size_t)D * (D + 1) + kRotTokens * D + kRotTokens) * 4;
@@ -306,4 +578,18 @@ extern "C" int fade_rotated_dequant(const uint8_t* packed, int bits, const void*
         case FADE_F32: return rotated_dequant_d<FADE_F32>(packed, bits, scale, scale_mode, R, H, S, (int)D, out, smem, grid, st);
         default: return FADE_ERR_INVALID_ARG;
     }
+}
+
+extern "C" int fade_rotated_quant_check(void* stream) {
+    cudaStream_t st = as_stream(stream);
+    int h = 0;
+    FADE_CUDA_TRY(cudaMemcpyFromSymbolAsync(&h, g_rotq_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
+    FADE_CUDA_TRY(cudaStreamSynchronize(st));
+    if (h) {
+        const int zero = 0;
+        FADE_CUDA_TRY(cudaMemcpyToSymbolAsync(g_rotq_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st));
+        FADE_CUDA_TRY(cudaStreamSynchronize(st));
+        return FADE_ERR_TIMEOUT;
+    }
+    return FADE_OK;
 }

@@ -109,15 +109,24 @@ int fade_dequant(const void* codes, int bits, const void* scale, int scale_mode,
 
 /* Replaces fade/rotated_quant.py:106-131 rotated_quant_k (kind 0, per-channel
  * scale over S) and 148-173 rotated_quant_v (kind 1, per-token scale).
- * x_rot = x @ R^T in fp32 (sequential-d accumulation, no FMA contraction),
- * then symmetric quant at `bits` (2, 3 or 4) with fp32 math; scale is cast to
- * x's dtype.  packed: bits 4 -> [..,D/2], 2 -> [..,D/4], 3 -> int8 [..,D].
+ * x_rot = x @ R^T in fp32, then symmetric quant at `bits` (2, 3 or 4) with
+ * fp32 math; scale is cast to x's dtype.  bf16 x at D = 128 with 2- or 4-bit
+ * codes, unit channel stride and 16-byte aligned rows and packed output:
+ * tensor cores (R split exactly into three bf16 parts, fp32 accumulation in
+ * the tensor core's order); otherwise CUDA cores with sequential-d
+ * accumulation and no FMA contraction.  packed: bits 4 -> [..,D/2], 2 -> [..,D/4], 3 -> int8 [..,D].
  * R: [D,D] fp32 row-major on the device, 16-byte aligned (else FADE_ERR_ALIGN);
  * D a multiple of 4, at most 128.  workspace: >= B*H*D*4 bytes
  * (per-channel absmax, kind 0 only). */
 int fade_rotated_quant(const void* x, int dtype, fade_view4 xv, const float* R,
                        int bits, int kind, uint8_t* packed, void* scale,
                        void* workspace, size_t ws_bytes, void* stream);
+
+/* No counterpart in the reference (its rotation is a library matmul): reads
+ * and clears the flag a tensor-core fade_rotated_quant kernel sets when its
+ * bounded wait for its own MMAs gave up (the outputs of that call are then
+ * undefined).  Synchronises `stream`.  FADE_OK or FADE_ERR_TIMEOUT. */
+int fade_rotated_quant_check(void* stream);
 
 /* Replaces fade/rotated_quant.py:134-145 / 176-187: out = rnd(rnd(q*scale) @ R)
  * (dequant in `dtype`, rotation in fp32).  scale_mode 0 (K) or 1 (V). */
