@@ -85,10 +85,14 @@ __device__ __forceinline__ int code_from_float(float v) {
 
 // q = clamp(rint(x), lo, hi) with NaN -> 0; rintf rounds half to even like
 // torch.round.
+// round half to even, clamp to [lo, hi]; NaN -> 0 (torch.clamp keeps NaN and
+// NaN -> int8 gives 0).  cvt.rni.s32.f32 rounds to nearest even, saturates
+// out-of-range values and turns NaN into 0, so the integer clamp after it
+// equals rint + clamp in fp32 + conversion.
 __device__ __forceinline__ int quant_code(float x, float lo, float hi) {
-    const float r = rintf(x);
-    if (r != r) return 0;  // torch.clamp keeps NaN; NaN -> int8 gives 0
-    return (int)fminf(fmaxf(r, lo), hi);
+    int i;
+    asm("cvt.rni.s32.f32 %0, %1;" : "=r"(i) : "f"(x));
+    return min(max(i, (int)lo), (int)hi);
 }
 
 // The reference's `qmax / absmax` is torch's __rtruediv__, i.e.

@@ -173,11 +173,14 @@ rotated_quant_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, c
 // in the canonical K-major layout without swizzle (8-row x 16-byte core
 // matrices, 128 bytes apart along K, 2048 bytes apart along the rows).  One
 // elected thread issues 3 x 8 tcgen05.mma (M = N = 128, K = 16) into a
-// 128-column fp32 accumulator in tensor memory; thread r of the warpgroup then
-// reads token r's 128 rotated values (tcgen05.ld, 16 columns at a time) and
-// quantises them in fp32 exactly like the CUDA-core kernel.
+// 128-column fp32 accumulator in tensor memory; then warpgroup g reads
+// columns [32 g, 32 g + 32) of every token (thread r of the group: token r,
+// tcgen05.ld, 16 columns at a time) and quantises them in fp32 exactly like
+// the CUDA-core kernel (per-token maxima combined across the four groups in
+// shared memory), each thread storing its 32 codes with one vector store.
 // ---------------------------------------------------------------------------
-constexpr int kRqThreads = 128;
+constexpr int kRqGroups = 4;                  // epilogue warpgroups, 32 columns each
+constexpr int kRqThreads = 128 * kRqGroups;
 constexpr int kRqParts = 3;
 constexpr uint32_t kRqOp = 128 * 128 * 2;   // one [128 x 128] bf16 operand
 constexpr uint32_t kRqR = 0;                                   // R parts
@@ -249,7 +252,7 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + kRqSlot);
-    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    const uint32_t lane_base = (uint32_t)(32 * (warp % 4)) << 16;   // a warp reaches its quarter of the lanes
 
     float lo, hi;
     qrange(bits, lo, hi);
@@ -294,7 +297,7 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
             __syncwarp();
         }
         // per-channel inverse scales of this row (K, quantisation pass)
-        if (kind == 0 && pass == 1) {
+        if (kind == 0 && pass == 1 && tid < D) {
             const float m = fmaxf(amax[z * D + tid], 1e-8f);
             inv_s[tid] = inv_scale<FADE_F32>(m, hi);
             if (t0 == 0) scale[z * D + tid] = __float2bfloat16_rn(__fdiv_rn(m, hi));
@@ -311,50 +314,66 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
             break;
         }
         tc_fence_after();
-        const int r = tid;   // token row of this thread
+        const int grp = tid / 128;            // columns [32 grp, 32 grp + 32)
+        const int r = tid % 128;              // token row of this thread (its TMEM lane)
+        const int q4 = warp % 4;              // the warp's quarter of the lanes
+        const uint32_t col0 = 32u * grp;
         const bool valid = t0 + r < S;
         if (kind == 0 && pass == 0) {
-            // per-channel maxima over the tile's tokens
-#pragma unroll 1
-            for (int c = 0; c < D / 16; ++c) {
-                uint32_t vv[16];
-                tc_ld16(tmem + lane_base + 16 * c, vv);
+            // per-channel maxima over the tile's tokens: each warp reduces its
+            // 32 tokens for its group's 32 channels by a transposing butterfly
+            // (after the step over lane bit b, a lane keeps the half of its
+            // channels whose bit b matches its own and the pairwise maxima:
+            // 16 + 8 + 4 + 2 + 1 shuffles leave lane l with channel l), then
+            // the 4 quarters combine in shared memory
+            uint32_t vv[2][16];
+            tc_ld16(tmem + lane_base + col0, vv[0]);
+            tc_ld16(tmem + lane_base + col0 + 16, vv[1]);
+            float a[32];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    float m = valid ? fabsf(__uint_as_float(vv[j])) : 0.f;
+            for (int j = 0; j < 32; ++j) a[j] = valid ? fabsf(__uint_as_float(vv[j / 16][j % 16])) : 0.f;
 #pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-                    if (lane == j) red[warp * D + 16 * c + j] = m;
+            for (int h = 16; h >= 1; h >>= 1) {
+                const bool up = (lane & h) != 0;
+#pragma unroll
+                for (int k = 0; k < h; ++k) {
+                    const float send = up ? a[k] : a[k + h];
+                    const float keep = up ? a[k + h] : a[k];
+                    a[k] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, h));
                 }
             }
+            red[q4 * D + col0 + lane] = a[0];
             __syncthreads();
-            const float m = fmaxf(fmaxf(red[tid], red[D + tid]), fmaxf(red[2 * D + tid], red[3 * D + tid]));
-            atomicMax(reinterpret_cast<int*>(amax) + z * D + tid, __float_as_int(m));
+            if (tid < D) {
+                const float m = fmaxf(fmaxf(red[tid], red[D + tid]), fmaxf(red[2 * D + tid], red[3 * D + tid]));
+                atomicMax(reinterpret_cast<int*>(amax) + z * D + tid, __float_as_int(m));
+            }
         } else {
+            uint32_t vv[2][16];
+            tc_ld16(tmem + lane_base + col0, vv[0]);
+            tc_ld16(tmem + lane_base + col0 + 16, vv[1]);
             float inv_t = 0.f;
             if (kind == 1) {
                 float m = 0.f;
-#pragma unroll 1
-                for (int c = 0; c < D / 16; ++c) {
-                    uint32_t vv[16];
-                    tc_ld16(tmem + lane_base + 16 * c, vv);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) m = fmaxf(m, fabsf(__uint_as_float(vv[j])));
-                }
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) m = fmaxf(m, fabsf(__uint_as_float(vv[c][j])));
+                red[grp * D + r] = m;
+                __syncthreads();
+                m = fmaxf(fmaxf(red[r], red[D + r]), fmaxf(red[2 * D + r], red[3 * D + r]));
                 m = fmaxf(m, 1e-8f);
                 inv_t = inv_scale<FADE_F32>(m, hi);
-                if (valid) scale[z * S + t0 + r] = __float2bfloat16_rn(__fdiv_rn(m, hi));
+                if (valid && grp == 0) scale[z * S + t0 + r] = __float2bfloat16_rn(__fdiv_rn(m, hi));
             }
-            uint32_t words[16];   // the row's packed codes: 64 bytes (4-bit) or 32 (2-bit)
+            uint32_t words[4];   // this thread's 32 codes: 16 bytes (4-bit) or 8 (2-bit)
 #pragma unroll
-            for (int c = 0; c < D / 16; ++c) {
-                uint32_t vv[16];
-                tc_ld16(tmem + lane_base + 16 * c, vv);
+            for (int c = 0; c < 2; ++c) {
                 int q[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const float inv = kind == 1 ? inv_t : inv_s[16 * c + j];
-                    q[j] = quant_code(__fmul_rn(__uint_as_float(vv[j]), inv), lo, hi);
+                    const float inv = kind == 1 ? inv_t : inv_s[col0 + 16 * c + j];
+                    q[j] = quant_code(__fmul_rn(__uint_as_float(vv[c][j]), inv), lo, hi);
                 }
                 if (bits == 4) {
 #pragma unroll
@@ -379,12 +398,12 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
                 }
             }
             if (valid) {
-                const int nw = bits == 4 ? 16 : 8;
-                uint4* dst = reinterpret_cast<uint4*>(packed + (z * S + t0 + r) * (int64_t)(nw * 4));
-#pragma unroll
-                for (int w4 = 0; w4 < 4; ++w4)
-                    if (4 * w4 < nw) dst[w4] = make_uint4(words[4 * w4], words[4 * w4 + 1], words[4 * w4 + 2],
-                                                          words[4 * w4 + 3]);
+                if (bits == 4)
+                    *reinterpret_cast<uint4*>(packed + (z * S + t0 + r) * (int64_t)64 + 16 * grp) =
+                        make_uint4(words[0], words[1], words[2], words[3]);
+                else
+                    *reinterpret_cast<uint2*>(packed + (z * S + t0 + r) * (int64_t)32 + 8 * grp) =
+                        make_uint2(words[0], words[1]);
             }
         }
         tc_fence_before();
