@@ -168,12 +168,14 @@ rotated_quant_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, c
 // boundary, as against the reference's own matmul).
 //
 // One CTA per SM, persistent over 128-token tiles of the [B, H, S] row space.
-// Shared memory holds the three R parts and two token tiles (cp.async double
-// buffering: tile i + 1 loads while tile i is multiplied and quantised), all
+// Shared memory holds the three R parts and three token tiles (cp.async,
+// two tiles ahead: tiles i + 1 and i + 2 load while tile i is multiplied and
+// quantised, enough bytes in flight per SM to keep HBM busy), all
 // in the canonical K-major layout without swizzle (8-row x 16-byte core
 // matrices, 128 bytes apart along K, 2048 bytes apart along the rows).  One
-// elected thread issues 3 x 8 tcgen05.mma (M = N = 128, K = 16) into a
-// 128-column fp32 accumulator in tensor memory; then warpgroup g reads
+// elected thread issues 3 x 8 tcgen05.mma (M = N = 128, K = 16) into one of
+// two 128-column fp32 accumulators in tensor memory (tile i + 1's MMAs run
+// while tile i is quantised from the other); then warpgroup g reads
 // columns [32 g, 32 g + 32) of every token (thread r of the group: token r,
 // tcgen05.ld, 16 columns at a time) and quantises them in fp32 exactly like
 // the CUDA-core kernel (per-token maxima combined across the four groups in
@@ -184,8 +186,9 @@ constexpr int kRqThreads = 128 * kRqGroups;
 constexpr int kRqParts = 3;
 constexpr uint32_t kRqOp = 128 * 128 * 2;   // one [128 x 128] bf16 operand
 constexpr uint32_t kRqR = 0;                                   // R parts
-constexpr uint32_t kRqX = kRqR + kRqParts * kRqOp;             // two token tiles
-constexpr uint32_t kRqBar = kRqX + 2 * kRqOp;                  // MMA-done mbarrier
+constexpr int kRqBufs = 3;                                     // token tiles in shared memory
+constexpr uint32_t kRqX = kRqR + kRqParts * kRqOp;             // token tiles
+constexpr uint32_t kRqBar = kRqX + kRqBufs * kRqOp;            // MMA-done mbarriers, one per accumulator
 constexpr uint32_t kRqSlot = kRqBar + 16;                      // tensor-memory address
 constexpr uint32_t kRqInv = kRqSlot + 16;                      // [128] per-channel 1/scale
 constexpr uint32_t kRqRed = kRqInv + 128 * 4;                  // [4][128] per-warp column maxima
@@ -241,10 +244,11 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
     }
     if (tid == 0) {
         mbar_init(sb + kRqBar, 1);
+        mbar_init(sb + kRqBar + 8, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
-        tc_alloc(sb + kRqSlot, 128);
+        tc_alloc(sb + kRqSlot, 256);
         tc_relinquish();
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -257,45 +261,71 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
     float lo, hi;
     qrange(bits, lo, hi);
     // stage tile t into buffer `buf` (rows past S are zero-filled)
+    // this thread's 16-byte pieces of a tile: rows tid / 16 + 32 k, piece tid % 16
+    constexpr int kPieces = 128 * 16 / kRqThreads;
+    const int row0 = tid / 16, kc = tid % 16;
+    const uint32_t doff0 = rq_off(row0, kc * 8);   // + k * 4 * 2048 for row0 + 32 k
     auto load_tile = [&](int64_t t, int buf) {
         const int64_t z = t / tiles_z, t0 = (t % tiles_z) * 128;
         const int64_t b = z / v.H, h = z % v.H;
-        const __nv_bfloat16* xz = x + b * v.sb + h * v.sh;
-        const uint32_t dst0 = sb + kRqX + (uint32_t)buf * kRqOp;
-        for (int c = tid; c < 128 * 16; c += kRqThreads) {
-            const int row = c / 16, kc = c % 16;
+        const __nv_bfloat16* xr = x + b * v.sb + h * v.sh + (t0 + row0) * v.ss + kc * 8;
+        const uint32_t dst0 = sb + kRqX + (uint32_t)buf * kRqOp + doff0;
+#pragma unroll
+        for (int k = 0; k < kPieces; ++k) {
+            const int row = row0 + 32 * k;
             const bool ok = t0 + row < S;
-            const __nv_bfloat16* src = xz + (ok ? t0 + row : 0) * v.ss + kc * 8;
-            rq_cp16(dst0 + rq_off(row, kc * 8), src, ok ? 16u : 0u);
+            rq_cp16(dst0 + (uint32_t)k * 4u * 2048u, ok ? xr + (int64_t)(32 * k) * v.ss : xr - row0 * v.ss,
+                    ok ? 16u : 0u);
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
-    bool failed = false;
-    int it = 0;
-    if ((int64_t)blockIdx.x < total) load_tile(blockIdx.x, 0);
-    for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-        const int buf = it & 1;
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (t + gridDim.x < total) load_tile(t + gridDim.x, buf ^ 1);
-        const int64_t z = t / tiles_z, t0 = (t % tiles_z) * 128;
+    // MMAs of iteration `i` (tile t) into accumulator i % 2, committed to
+    // mbarrier i % 2 (its (i / 2)-th phase)
+    auto issue_mma = [&](int i) {
         if (warp == 0) {
             tc_fence_after();
             if (elect_one()) {
-                const uint32_t xb = sb + kRqX + (uint32_t)buf * kRqOp;
+                const uint32_t xb = sb + kRqX + (uint32_t)(i % kRqBufs) * kRqOp;
 #pragma unroll
                 for (int j = 0; j < kRqParts; ++j)
 #pragma unroll
                     for (int ks = 0; ks < D / 16; ++ks)
-                        tc_mma_ss(tmem, tc_desc(xb + ks * 256, 128, 2048, 0),
+                        tc_mma_ss(tmem + 128u * (uint32_t)(i & 1), tc_desc(xb + ks * 256, 128, 2048, 0),
                                   tc_desc(sb + kRqR + j * kRqOp + ks * 256, 128, 2048, 0), kRqIdesc,
                                   (j | ks) ? 1u : 0u);
-                tc_commit(sb + kRqBar);
+                tc_commit(sb + kRqBar + 8u * (uint32_t)(i & 1));
             }
             __syncwarp();
         }
+    };
+    bool failed = false;
+    int it = 0, issued = -1;   // last iteration whose MMAs were issued
+    const int64_t G = gridDim.x;
+    if ((int64_t)blockIdx.x < total) {
+        load_tile(blockIdx.x, 0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        if ((int64_t)blockIdx.x + G < total) load_tile(blockIdx.x + G, 1);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        issue_mma(0);
+        issued = 0;
+    }
+    for (int64_t t = blockIdx.x; t < total; t += G, ++it) {
+        // tile it + 1 landed (all groups complete); its buffer and tile it's
+        // stay untouched, tile it + 2 goes to the one that held tile it - 1
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (t + 2 * G < total) load_tile(t + 2 * G, (it + 2) % kRqBufs);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        // accumulator (it + 1) % 2 was last read by tile it - 1's epilogue
+        if (t + G < total) {
+            issue_mma(it + 1);
+            issued = it + 1;
+        }
+        const int64_t z = t / tiles_z, t0 = (t % tiles_z) * 128;
         // per-channel inverse scales of this row (K, quantisation pass)
         if (kind == 0 && pass == 1 && tid < D) {
             const float m = fmaxf(amax[z * D + tid], 1e-8f);
@@ -304,7 +334,7 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
         }
         uint32_t polls = 0;
         bool timed_out = false;
-        while (!mbar_try_wait(sb + kRqBar, (uint32_t)it & 1u)) {
+        while (!mbar_try_wait(sb + kRqBar + 8u * (uint32_t)(it & 1), (uint32_t)(it >> 1) & 1u)) {
             if (++polls == kRqPolls) { timed_out = true; break; }
         }
         // one decision for the whole CTA (also: inv_s written)
@@ -314,6 +344,7 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
             break;
         }
         tc_fence_after();
+        const uint32_t acc = tmem + 128u * (uint32_t)(it & 1);
         const int grp = tid / 128;            // columns [32 grp, 32 grp + 32)
         const int r = tid % 128;              // token row of this thread (its TMEM lane)
         const int q4 = warp % 4;              // the warp's quarter of the lanes
@@ -321,28 +352,22 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
         const bool valid = t0 + r < S;
         if (kind == 0 && pass == 0) {
             // per-channel maxima over the tile's tokens: each warp reduces its
-            // 32 tokens for its group's 32 channels by a transposing butterfly
-            // (after the step over lane bit b, a lane keeps the half of its
-            // channels whose bit b matches its own and the pairwise maxima:
-            // 16 + 8 + 4 + 2 + 1 shuffles leave lane l with channel l), then
-            // the 4 quarters combine in shared memory
+            // 32 tokens for its group's 32 channels with one redux.sync per
+            // channel (non-negative floats order like their bit patterns as
+            // unsigned integers), lane j keeping channel j; then the 4
+            // quarters combine in shared memory
             uint32_t vv[2][16];
-            tc_ld16(tmem + lane_base + col0, vv[0]);
-            tc_ld16(tmem + lane_base + col0 + 16, vv[1]);
-            float a[32];
+            tc_ld16(acc + lane_base + col0, vv[0]);
+            tc_ld16(acc + lane_base + col0 + 16, vv[1]);
+            uint32_t mine = 0;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) a[j] = valid ? fabsf(__uint_as_float(vv[j / 16][j % 16])) : 0.f;
-#pragma unroll
-            for (int h = 16; h >= 1; h >>= 1) {
-                const bool up = (lane & h) != 0;
-#pragma unroll
-                for (int k = 0; k < h; ++k) {
-                    const float send = up ? a[k] : a[k + h];
-                    const float keep = up ? a[k + h] : a[k];
-                    a[k] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, h));
-                }
+            for (int j = 0; j < 32; ++j) {
+                const uint32_t a = valid ? (vv[j / 16][j % 16] & 0x7FFFFFFFu) : 0u;
+                uint32_t m;
+                asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(m) : "r"(a));
+                mine = lane == j ? m : mine;
             }
-            red[q4 * D + col0 + lane] = a[0];
+            red[q4 * D + col0 + lane] = __uint_as_float(mine);
             __syncthreads();
             if (tid < D) {
                 const float m = fmaxf(fmaxf(red[tid], red[D + tid]), fmaxf(red[2 * D + tid], red[3 * D + tid]));
@@ -350,8 +375,8 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
             }
         } else {
             uint32_t vv[2][16];
-            tc_ld16(tmem + lane_base + col0, vv[0]);
-            tc_ld16(tmem + lane_base + col0 + 16, vv[1]);
+            tc_ld16(acc + lane_base + col0, vv[0]);
+            tc_ld16(acc + lane_base + col0 + 16, vv[1]);
             float inv_t = 0.f;
             if (kind == 1) {
                 float m = 0.f;
@@ -410,16 +435,17 @@ rotated_quant_tc_kernel(const __nv_bfloat16* __restrict__ x, fade_view4 v, const
         __syncthreads();   // tensor memory read (and red / inv_s) before the next tile's MMAs
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (failed && warp == 0) {
+    if (failed && warp == 0 && issued >= 0) {
         // MMAs may still be in flight: wait (bounded) for the last commit
         // before the tensor memory is released
-        for (uint32_t i = 0; i < kRqPolls && !mbar_try_wait(sb + kRqBar, (uint32_t)it & 1u); ++i) {
+        const uint32_t bar = sb + kRqBar + 8u * (uint32_t)(issued & 1), par = (uint32_t)(issued >> 1) & 1u;
+        for (uint32_t i = 0; i < kRqPolls && !mbar_try_wait(bar, par); ++i) {
         }
     }
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tc_dealloc(tmem, 128);
+        tc_dealloc(tmem, 256);
     }
 }
 
