@@ -473,30 +473,35 @@ static bool can_vec(const void* x, const fade_view4& v, int elem_bytes) {
            ((v.sh * elem_bytes) % 16 == 0) && ((v.ss * elem_bytes) % 16 == 0);
 }
 
-// quant_k_int4 for long rows: a cluster of kKClus CTAs per (b, h), each over
-// a contiguous slice of S and all D channels.  Each CTA reduces the absmax
-// of its slice (kKRows rows in flight per thread), the cluster combines the
-// kKClus partial maxima through distributed shared memory, and each CTA then
-// quantises its own slice, which it read moments before (most of a wave's
-// slices are still in the 126 MB L2).
+// quant_k_int4 for long rows: a cluster of kKClus CTAs per (b, h) and
+// channel part (D / nsplit channels), each CTA over a contiguous slice of S.
+// Each CTA reduces the absmax of its slice (kKRows rows in flight per
+// thread), the cluster combines the kKClus partial maxima through
+// distributed shared memory, and each CTA then quantises its own slice,
+// which it read moments before.  With D = 128 split in two halves (128-byte
+// row segments) the resident CTAs' slices total less than the 126 MB L2, so
+// that second read is an L2 hit rather than a second trip to HBM.
 constexpr int kKClus = 8;
 constexpr int kKRows = 4;
 
 template <int DT>
 __global__ void __cluster_dims__(kKClus, 1, 1) __launch_bounds__(kQuantThreads)
 quant_int4_k_cluster_kernel(const typename Elem<DT>::T* __restrict__ x, fade_view4 v, uint8_t* __restrict__ packed,
-                            typename Elem<DT>::T* __restrict__ scale, bool vec) {
+                            typename Elem<DT>::T* __restrict__ scale, bool vec, int nsplit) {
     using T = typename Elem<DT>::T;
     constexpr int E = 8, U = kKRows;
-    const int z = blockIdx.x / kKClus, rank = blockIdx.x % kKClus;
+    const int cid = blockIdx.x / kKClus, rank = blockIdx.x % kKClus;
+    const int z = cid / nsplit;
     const int b = z / (int)v.H, h = z % (int)v.H;
-    const int D = (int)v.D;
+    const int Dfull = (int)v.D;
+    const int D = Dfull / nsplit;                // this cluster's channels: [c0, c0 + D)
+    const int c0 = (cid % nsplit) * D;
     const int tpr = D / E;                       // threads per row (D <= 256: tpr <= 32)
     const int rows_per_iter = kQuantThreads / tpr;
     const int slot = threadIdx.x / tpr;
     const int dg = (threadIdx.x % tpr) * E;
     const int64_t s0 = v.S * rank / kKClus, s1 = v.S * (rank + 1) / kKClus;
-    const T* xb = x + b * v.sb + h * v.sh + (int64_t)dg * v.sd;
+    const T* xb = x + b * v.sb + h * v.sh + (int64_t)(c0 + dg) * v.sd;
 
     float amax[E];
 #pragma unroll
@@ -545,14 +550,14 @@ quant_int4_k_cluster_kernel(const typename Elem<DT>::T* __restrict__ x, fade_vie
         // absmax.clamp(min=EPS) in the dtype; inv = 7/absmax; scale = absmax/7.
         m = fmaxf(m, Elem<DT>::eps());
         s_inv[c] = inv_scale<DT>(m, 7.f);
-        if (rank == 0) scale[(int64_t)z * D + c] = Elem<DT>::from_f(Elem<DT>::rnd(__fdiv_rn(m, 7.f)));
+        if (rank == 0) scale[(int64_t)z * Dfull + c0 + c] = Elem<DT>::from_f(Elem<DT>::rnd(__fdiv_rn(m, 7.f)));
     }
     // no member leaves (or reuses camax) while another may still read it
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
     float inv[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) inv[i] = s_inv[dg + i];
-    uint8_t* pb = packed + (int64_t)z * v.S * (D / 2) + dg / 2;
+    uint8_t* pb = packed + (int64_t)z * v.S * (Dfull / 2) + (c0 + dg) / 2;
     s = s0 + slot;
     for (; s + (U - 1) * rows_per_iter < s1; s += U * rows_per_iter) {
         float e[U][E];
@@ -563,7 +568,7 @@ quant_int4_k_cluster_kernel(const typename Elem<DT>::T* __restrict__ x, fade_vie
             int q[E];
 #pragma unroll
             for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[u][i], inv[i])), -8.f, 7.f);
-            store_int4<E>(pb + (s + u * rows_per_iter) * (D / 2), q);
+            store_int4<E>(pb + (s + u * rows_per_iter) * (Dfull / 2), q);
         }
     }
     for (; s < s1; s += rows_per_iter) {
@@ -572,7 +577,7 @@ quant_int4_k_cluster_kernel(const typename Elem<DT>::T* __restrict__ x, fade_vie
         int q[E];
 #pragma unroll
         for (int i = 0; i < E; ++i) q[i] = quant_code(Elem<DT>::rnd(__fmul_rn(e[i], inv[i])), -8.f, 7.f);
-        store_int4<E>(pb + s * (D / 2), q);
+        store_int4<E>(pb + s * (Dfull / 2), q);
     }
 }
 
@@ -588,8 +593,10 @@ static int launch_quant_k(const void* x, const fade_view4& v, uint8_t* packed, v
     const bool e8 = (v.D % 8 == 0);
     if (e8 && v.D <= 256 && v.S >= 64 * kKClus) {
         const bool vec = can_vec(x, v, sizeof(T));
-        quant_int4_k_cluster_kernel<DT><<<(unsigned)(Z * kKClus), kQuantThreads, 0, st>>>(
-            (const T*)x, v, packed, (T*)scale, vec);
+        // two channel halves when each stays a whole 128-byte row segment
+        const int nsplit = (v.D % 16 == 0 && v.D / 2 * (int64_t)sizeof(T) >= 128) ? 2 : 1;
+        quant_int4_k_cluster_kernel<DT><<<(unsigned)(Z * nsplit * kKClus), kQuantThreads, 0, st>>>(
+            (const T*)x, v, packed, (T*)scale, vec, nsplit);
         FADE_LAUNCH_CHECK();
         return FADE_OK;
     }
