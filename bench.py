@@ -735,7 +735,7 @@ def run_h2o(args):
 
     from fade_b200.attention import DecodePlan
     from fade_b200.cache import TieredKVCache
-    from fade_b200.policy import _assign_one_layer
+    from fade_b200.policy import _assign_one_layer, assign_counts
     from fade_b200.rope import Vanilla
 
     c = CFG
@@ -761,7 +761,9 @@ def run_h2o(args):
         scores = torch.distributions.Dirichlet(torch.full((S,), 0.1, device=dev)).sample((H,)).sum(0)
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        cache.apply_tier_assignment(layer, _assign_one_layer(S, scores, c["n_sink"], c["recent"], c["budget"], 0))
+        args_l = (S, c["n_sink"], c["recent"], c["budget"], 0)
+        cache.apply_tier_assignment(layer, _assign_one_layer(args_l[0], scores, *args_l[1:]),
+                                    counts=assign_counts(*args_l))
         torch.cuda.synchronize(dev)
         reassign_ms.append((time.perf_counter() - t0) * 1e3)
         del k, v
@@ -782,8 +784,9 @@ def run_h2o(args):
         + (n_pad // G) * D * eb + 2 * g_ * D * eb
     extra = {"reassignment": {"ms_per_layer_median": round(statistics.median(reassign_ms[1:] or reassign_ms), 3),
                               "what": "TieredKVCache.apply_tier_assignment of a 4096-token layer on the GPU "
-                                      "(un-RoPE/re-RoPE gather, INT4 K + INT2 V quantisers), host wall clock "
-                                      "incl. its host syncs; not in the timed decode step"},
+                                      "(un-RoPE/re-RoPE gather, INT4 K + INT2 V quantisers) with the tier "
+                                      "counts from the budgets (no host sync), host wall clock; not in the "
+                                      "timed decode step"},
              "config": {"batch": B, "prompt": S, "int4_budget": n, "v_int2_group": G}}
     print(json.dumps(_fixed_tier_line(args, ms, clocks, hot, B * H * per_z, extra, 2 * L)), flush=True)
 

@@ -651,12 +651,22 @@ class TieredKVCache(DynamicCache):
             st._fp16_len_dev = torch.empty(B, dtype=torch.int32, device=st._fp16_buf_k.device)
         st._fp16_len_dev.fill_(st._fp16_len)
 
-    def apply_tier_assignment(self, layer_idx: int, tiers: Tensor, scores: Tensor | None = None) -> None:
+    def apply_tier_assignment(self, layer_idx: int, tiers: Tensor, scores: Tensor | None = None, *,
+                              counts: tuple[int, int, int] | None = None) -> None:
         """Move tokens between tiers (``fade/cache.py:881-1057``): ``tiers``
         [S] in ascending position order with values TIER_FP16 / INT4 / INT2 /
         EVICT.  Evicting re-RoPEs the survivors to contiguous positions and
         resets ``next_position``; FP16 survivors split into the first
-        ``n_sink`` sinks and the recent tier."""
+        ``n_sink`` sinks and the recent tier.
+
+        ``counts`` (an extension; the reference has no such argument): the
+        number of FP16, INT4 and INT2 entries of ``tiers`` when the caller
+        knows them, as after ``_assign_one_layer`` (``assign_counts`` gives
+        them from the budgets).  The tiers' positions are then grouped with
+        one device sort instead of boolean masks and ``nonzero``, and the call
+        makes no host synchronisation (the reference synchronises on every
+        reassignment, ``fade/cache.py:912``).  Wrong counts give wrong tiers;
+        TIER_PQ entries are not detected on this path."""
         del scores
         st = self._layers[layer_idx]
         k_full, v_full, pos_full = self._all_in_position_order(layer_idx)
@@ -664,20 +674,47 @@ class TieredKVCache(DynamicCache):
         if int(tiers.shape[0]) != S:
             raise ValueError(f"tiers length {int(tiers.shape[0])} != cache length {S} for layer {layer_idx}")
         tiers = tiers.to(pos_full.device)
-        if bool((tiers == TIER_PQ).any()):
-            raise NotImplementedError("TIER_PQ (product-quantisation codebooks) is not supported by fade_b200")
-        keep = tiers != TIER_EVICT
-        n_kept = int(keep.sum().item())
-        if n_kept < S:
-            keep_idx = keep.nonzero(as_tuple=False).squeeze(-1)
-            k_full, v_full, pos_full = self._rerope(k_full, v_full, pos_full, keep_idx)
-            tiers = tiers[keep]
-            st.next_position = n_kept
+        if counts is None:
+            if bool((tiers == TIER_PQ).any()):
+                raise NotImplementedError("TIER_PQ (product-quantisation codebooks) is not supported by fade_b200")
+            keep = tiers != TIER_EVICT
+            n_kept = int(keep.sum().item())
+            if n_kept < S:
+                keep_idx = keep.nonzero(as_tuple=False).squeeze(-1)
+                k_full, v_full, pos_full = self._rerope(k_full, v_full, pos_full, keep_idx)
+                tiers = tiers[keep]
+                st.next_position = n_kept
+            groups = None
+        else:
+            n_fp, n_i4, n_i2 = (int(c) for c in counts)
+            if min(n_fp, n_i4, n_i2) < 0 or n_fp + n_i4 + n_i2 > S:
+                raise ValueError(f"counts {counts} do not fit a cache of length {S}")
+            n_kept = n_fp + n_i4 + n_i2
+            if n_kept < S:
+                # kept positions in ascending order: evicted ones sort last
+                ar = torch.arange(S, device=tiers.device)
+                keep_idx = torch.argsort((tiers == TIER_EVICT).to(torch.int64) * S + ar)[:n_kept]
+                keep_idx = keep_idx.sort().values
+                k_full, v_full, pos_full = self._rerope(k_full, v_full, pos_full, keep_idx)
+                tiers = tiers.index_select(0, keep_idx)
+                st.next_position = n_kept
+            # every tier's positions, ascending, as consecutive runs of one sort
+            rank = torch.full_like(tiers, 3)
+            rank = torch.where(tiers == TIER_FP16, torch.zeros_like(rank), rank)
+            rank = torch.where(tiers == TIER_INT4, torch.ones_like(rank), rank)
+            rank = torch.where(tiers == TIER_INT2, torch.full_like(rank, 2), rank)
+            order = torch.argsort(rank * n_kept + torch.arange(n_kept, device=tiers.device))
+            groups = (order[:n_fp], order[n_fp:n_fp + n_i4], order[n_fp + n_i4:n_kept])
 
         def sel(t, idx, dim):
             return t.index_select(dim, idx).contiguous()
 
-        fp_idx = (tiers == TIER_FP16).nonzero(as_tuple=False).squeeze(-1)
+        def tier_idx(which: int, tier: int) -> Tensor:
+            if groups is not None:
+                return groups[which]
+            return (tiers == tier).nonzero(as_tuple=False).squeeze(-1)
+
+        fp_idx = tier_idx(0, TIER_FP16)
         if fp_idx.numel() > 0:
             fk, fv, fpos = sel(k_full, fp_idx, -2), sel(v_full, fp_idx, -2), sel(pos_full, fp_idx, 0)
             ns = min(self.n_sink, int(fp_idx.numel()))
@@ -694,14 +731,14 @@ class TieredKVCache(DynamicCache):
             st.sink_k = st.sink_v = st.sink_pos = None
         self._reseed_fp16_buffer(st)
 
-        i4 = (tiers == TIER_INT4).nonzero(as_tuple=False).squeeze(-1)
+        i4 = tier_idx(1, TIER_INT4)
         if i4.numel() > 0:
             self._quant_int4_tier(st, sel(k_full, i4, -2), sel(v_full, i4, -2), sel(pos_full, i4, 0))
         else:
             st.int4_kq = st.int4_vq = st.int4_ks = st.int4_vs = st.int4_pos = None
             st.backend_k = st.backend_v = st.backend_pos = None
 
-        i2 = (tiers == TIER_INT2).nonzero(as_tuple=False).squeeze(-1)
+        i2 = tier_idx(2, TIER_INT2)
         if i2.numel() > 0:
             gs = DEFAULT_INT2_GROUP_SIZE
             k2, _ = pad_to_group(sel(k_full, i2, -2), gs)

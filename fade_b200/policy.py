@@ -24,26 +24,41 @@ def _assign_one_layer(S: int, scores: Tensor, n_sink: int, recent_window: int, i
     middle token in INT4 and evicts nothing.  Ranking is by descending score;
     the reference takes the same single descending sort, so equal scores are
     the only source of a possible difference (torch's sort order among ties).
+    The middle is the contiguous range [n_sink, S - recent_window) and the
+    tiers are set with slices and index_fill_, so on a CUDA tensor the
+    selection makes no host synchronisation.
     """
     dev = scores.device
-    pos = torch.arange(S, device=dev)
     head = min(n_sink, S)
     tail = max(head, S - recent_window)
-    fp = (pos < head) | (pos >= tail)
-    tiers = torch.where(fp, torch.full_like(pos, TIER_FP16), torch.full_like(pos, TIER_EVICT))
-    mid = pos[~fp]
-    n_mid = int(mid.numel())
+    tiers = torch.full((S,), TIER_FP16, dtype=torch.long, device=dev)
+    n_mid = tail - head
     if n_mid == 0:
         return tiers
     if int4_budget is None or int4_budget >= n_mid:
-        tiers[mid] = TIER_INT4
+        tiers[head:tail] = TIER_INT4
         return tiers
-    order = mid[scores[mid].argsort(descending=True)]
-    tiers[order[:int4_budget]] = TIER_INT4
+    tiers[head:tail] = TIER_EVICT
+    order = scores[head:tail].argsort(descending=True) + head
+    tiers.index_fill_(0, order[:int4_budget], TIER_INT4)
     n2 = min(max(int2_budget, 0), n_mid - int4_budget)
     if n2 > 0:
-        tiers[order[int4_budget:int4_budget + n2]] = TIER_INT2
+        tiers.index_fill_(0, order[int4_budget:int4_budget + n2], TIER_INT2)
     return tiers
 
 
-__all__ = ["_assign_one_layer"]
+def assign_counts(S: int, n_sink: int, recent_window: int, int4_budget: int | None,
+                  int2_budget: int) -> tuple[int, int, int]:
+    """(FP16, INT4, INT2) entries of ``_assign_one_layer``'s result with the
+    same arguments, from the budgets alone (for
+    ``TieredKVCache.apply_tier_assignment(..., counts=...)``)."""
+    head = min(n_sink, S)
+    tail = max(head, S - recent_window)
+    n_mid = tail - head
+    if int4_budget is None or int4_budget >= n_mid:
+        return S - n_mid, n_mid, 0
+    b4 = max(int4_budget, 0)
+    return S - n_mid, b4, min(max(int2_budget, 0), n_mid - b4)
+
+
+__all__ = ["_assign_one_layer", "assign_counts"]

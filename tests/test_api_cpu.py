@@ -214,3 +214,22 @@ def test_fade_import_alias():
     finally:
         compat.uninstall_fade_alias()
         sys.modules.update(saved)
+
+
+def test_assign_counts_match_assign_one_layer():
+    """assign_counts gives, from the budgets alone, the FP16 / INT4 / INT2
+    counts of _assign_one_layer's tiers (fade/policy.py:232-274)."""
+    import torch
+
+    from fade_b200.cache import TIER_FP16, TIER_INT2, TIER_INT4
+    from fade_b200.policy import _assign_one_layer, assign_counts
+
+    g = torch.Generator().manual_seed(0)
+    for S in (0, 1, 4, 68, 69, 500, 4096):
+        for n_sink, recent in ((0, 0), (4, 64)):
+            for b4 in (None, 0, 1, 400, 10000):
+                for b2 in (0, 10, 300):
+                    t = _assign_one_layer(S, torch.rand(S, generator=g), n_sink, recent, b4, b2)
+                    got = assign_counts(S, n_sink, recent, b4, b2)
+                    assert got == (int((t == TIER_FP16).sum()), int((t == TIER_INT4).sum()),
+                                   int((t == TIER_INT2).sum())), (S, n_sink, recent, b4, b2)

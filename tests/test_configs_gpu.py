@@ -65,6 +65,48 @@ def test_cfg3_g32_h2o_eviction_and_decode(cuda_device):
     assert_attn_close(out, t_vals(t_from_bits(g["out_ref32"], "f32")), "f16", 2e-3)
 
 
+def test_cfg3_reassignment_without_host_sync(cuda_device):
+    """The config-3 reassignment with the tier counts known on the host
+    (``assign_counts`` from the budgets): ``_assign_one_layer`` on the GPU
+    scores and ``apply_tier_assignment(..., counts=...)`` make no host
+    synchronisation (torch's sync debug mode raises on one), and every tier
+    of the cache equals the mask path's bit for bit."""
+    from fade_b200.cache import TieredKVCache
+    from fade_b200.policy import _assign_one_layer, assign_counts
+    from fade_b200.rope import Vanilla
+
+    c = gi.CFG3
+    scheme = Vanilla(theta=c["theta"], head_dim=c["D"])
+    k, v, q, scores = gi.cfg3_inputs(lambda p: scheme.compute_cos_sin(p, "cpu", model_dtype=torch.float16))
+    dev = cuda_device
+    k, v, q, scores = k.to(dev), v.to(dev), q.to(dev), scores.to(dev)
+    caches = []
+    for _ in range(2):
+        cache = TieredKVCache(n_sink=c["n_sink"], recent_window=c["recent"], int4_budget=c["budget"],
+                              dtype=torch.float16, rope_theta=c["theta"], head_dim=c["D"], middle_v_bits=2,
+                              rope_scheme=scheme, v_int2_group_size=c["group"])
+        cache.update(k, v, 0)
+        caches.append(cache)
+    args = (c["S"], c["n_sink"], c["recent"], c["budget"], 0)
+    caches[0].apply_tier_assignment(0, _assign_one_layer(args[0], scores, *args[1:]))
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        tiers = _assign_one_layer(args[0], scores, *args[1:])
+        caches[1].apply_tier_assignment(0, tiers, counts=assign_counts(*args))
+    finally:
+        torch.cuda.set_sync_debug_mode(0)
+    a, b = caches[0]._layers[0], caches[1]._layers[0]
+    assert a.next_position == b.next_position
+    for name in ("sink_k", "sink_v", "sink_pos", "fp16_k", "fp16_v", "fp16_pos", "int4_kq", "int4_ks",
+                 "int4_vq", "int4_vs", "int4_pos"):
+        ta, tb = getattr(a, name), getattr(b, name)
+        assert (ta is None) == (tb is None), name
+        if ta is not None:
+            assert ta.shape == tb.shape and torch.equal(ta, tb), name
+    assert torch.equal(caches[0].decode_attention(0, q), caches[1].decode_attention(0, q))
+
+
 def test_cfg4_ragged_rotated_decode(cuda_device):
     """Qwen2.5-7B shape, ragged batch (per-sequence middle lengths, ragged
     unit grid) with the rotated 2-bit middle: GPU quantiser codes against the
